@@ -1,0 +1,128 @@
+/*
+ * vkq.h -- C ABI of the B200 (sm_100a) k-quant dequantize-and-matmul path.
+ *
+ * Drop-in boundary for xupit3r/vibrant's GPU matmul path.  Every entry point
+ * is extern "C", takes plain pointers and sizes, returns an int status
+ * (0 = VKQ_OK) and never throws.  On failure vkq_last_error() gives a
+ * thread-local message.  Device pointers are owned by the caller (vibrant's
+ * gpu.Buffer, internal/gpu/buffer.go:6-29; the raw pointer comes from
+ * Buffer.Ptr(), internal/gpu/cuda.go:250-254).
+ *
+ * Conventions shared by all entry points
+ *  - device: CUDA ordinal made current on the calling thread before any CUDA
+ *    call (Go may run a cgo call on any OS thread); pass -1 to keep the
+ *    thread's current device.
+ *  - stream: a cudaStream_t passed as void*; NULL is the legacy default
+ *    stream, which is what vibrant's kernels use today
+ *    (internal/tensor/ops_cuda.go:62,71).  Calls are asynchronous: nothing
+ *    synchronizes the host, so the caller keeps its Device.Sync()
+ *    (ops_cuda.go:81) where it needs one.
+ *  - qtype: GGML type code of the weight, as in internal/gguf/metadata.go:21-23.
+ *  - Weight orientation follows the reference: a quantized weight is
+ *    logically row-major [K, N] = [in, out] (internal/gguf/loader.go:24-27);
+ *    W[k][n] is dequantized value k*N + n of the byte stream, and the stream
+ *    holds ceil(K*N/256) super-blocks (calculateTensorSize,
+ *    internal/gguf/metadata.go:170-204).  x is float32 [M, K] row-major and
+ *    y is float32 [M, N] row-major.
+ *  - There is no CPU fallback: when the GPU path cannot run, the call fails.
+ */
+#ifndef VKQ_H
+#define VKQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VKQ_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VKQ_API __attribute__((visibility("default")))
+#else
+#define VKQ_API
+#endif
+
+/* GGML type codes, internal/gguf/metadata.go:21-23. */
+enum vkq_qtype { VKQ_Q4_K = 12, VKQ_Q5_K = 13, VKQ_Q6_K = 14 };
+
+enum vkq_status {
+    VKQ_OK = 0,
+    VKQ_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size, short buffer */
+    VKQ_ERR_UNSUPPORTED = 2,      /* unknown qtype, or a shape/device no kernel serves */
+    VKQ_ERR_MISALIGNED = 3,       /* a pointer lacks the alignment the kernel needs */
+    VKQ_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
+    VKQ_ERR_CUDA = 5,             /* CUDA runtime error (message in vkq_last_error) */
+    VKQ_ERR_DEVICE_TIMEOUT = 6,   /* a bounded device-side wait gave up */
+    VKQ_ERR_NCCL = 7              /* collective failure in the sharded path */
+};
+
+/* Version of this ABI (VKQ_ABI_VERSION of the built library). */
+VKQ_API int vkq_abi_version(void);
+/* Static text for a status code. */
+VKQ_API const char *vkq_status_string(int status);
+/* Message of the last failing call made on this thread ("" if none). */
+VKQ_API const char *vkq_last_error(void);
+
+/* Bytes of one super-block: 144 / 176 / 210 (Q4_K_BLOCK_SIZE,
+ * quant_q4k.go:9-11; Q5_K_BLOCK_SIZE, quant_q5k.go:9-13; Q6_K_BLOCK_SIZE,
+ * quant_q6k.go:9-11).  0 for an unknown type. */
+VKQ_API int64_t vkq_block_bytes(int qtype);
+
+/* Byte size of a [K, N] weight: ceil(K*N/256) blocks.  Replaces
+ * calculateTensorSize for the k-quant types (internal/gguf/metadata.go:170-204). */
+VKQ_API int vkq_weight_bytes(int qtype, int64_t K, int64_t N, int64_t *bytes);
+
+/* Dequantize nblocks super-blocks to float32 (nblocks*256 values), bit-exact
+ * with the reference Go decoders: every non-NaN result has the same bits as
+ * DequantizeQ4_K / Q5_K / Q6_K (quant_q4k.go:37-79, quant_q5k.go:39-88,
+ * quant_q6k.go:39-80) including float16ToFloat32's choices (tensor.go:629-676);
+ * NaN results are NaN.  Replaces the CPU expansion done before upload by
+ * dequantizeForGPU (internal/tensor/tensor_cuda_api.go:39-53).
+ * w: device, any alignment; out: device, 4-byte aligned. */
+VKQ_API int vkq_dequantize_f32(int device, int qtype, const void *w, int64_t nblocks, float *out,
+                       void *stream);
+
+/* Fused dequantize + transpose: quantized [K, N] -> float32 [N, K], bit-exact
+ * with DequantTransposeQ4K / Q5K / Q6K (internal/tensor/dequant_transpose.go:15-157)
+ * as used by GetOrDequantTranspose (internal/tensor/tensor.go:535-588),
+ * including its handling of a trailing partial block (left zero). */
+VKQ_API int vkq_dequant_transpose_f32(int device, int qtype, const void *w, int64_t K, int64_t N,
+                              float *out, void *stream);
+
+/* Workspace needed by vkq_matmul / vkq_gemv / vkq_gemm for this problem on
+ * this device.  The workspace is caller-owned device memory, at least
+ * 256-byte aligned, zero-filled before its first use; every call leaves it
+ * ready for the next one.  Calls that may run concurrently need separate
+ * workspaces. */
+VKQ_API int vkq_matmul_workspace_bytes(int device, int qtype, int64_t M, int64_t K, int64_t N,
+                               size_t *bytes);
+
+/* y[M,N] = x[M,K] . W[K,N] with W quantized (qtype), float32 in and out.
+ * Dispatch: M <= 8 runs vkq_gemv (fp32 accumulate, max relative error 1e-5
+ * against the reference's float32 CPU MatMul); larger M runs vkq_gemm (bf16
+ * tensor cores, 2e-2).  w_bytes is the size of the weight buffer (at least
+ * vkq_weight_bytes).  w must be 16-byte aligned.
+ * Replaces matmul_f32_single_row_launch (internal/gpu/cuda/launch.cu:37-48,
+ * M == 1) and matmul_f32_launch (launch.cu:25-35, M > 1) as called by
+ * matmulGPU (internal/tensor/ops_cuda.go:16-101), with the weight kept
+ * quantized on the device instead of expanded to float32. */
+VKQ_API int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+               const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
+               void *stream);
+
+/* The fp32 CUDA-core path of vkq_matmul, for 1 <= M <= 8 (decode). */
+VKQ_API int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+             const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
+             void *stream);
+
+/* Reads and clears the device-side status word of this library on a device
+ * (set when a bounded wait inside a kernel gave up).  Synchronizes with the
+ * device.  *code receives VKQ_OK or VKQ_ERR_DEVICE_TIMEOUT. */
+VKQ_API int vkq_device_status(int device, int *code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VKQ_H */

@@ -1,0 +1,399 @@
+/*
+ * kq_oracle.c -- CPU oracle (test infrastructure only) for the k-quant
+ * dequantize-and-matmul path.  A plain-C restatement of the reference Go
+ * arithmetic; see kq_oracle.h for the scope and for what pins it.  Every
+ * function cites the reference file:line it follows (paths relative to the
+ * root of xupit3r/vibrant).
+ *
+ * Build: oracle/Makefile (-O2 -ffp-contract=off -fno-tree-vectorize; the Go
+ * compiler emits scalar code, and lane-wise vector code would give the same
+ * bits anyway, so the flag only keeps the timing honest).
+ */
+#include "kq_oracle.h"
+
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+static inline float bits_to_f32(uint32_t b) {
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+static inline uint32_t f32_to_bits(float f) {
+    uint32_t b;
+    memcpy(&b, &f, 4);
+    return b;
+}
+
+int ko_block_bytes(int qtype) {
+    switch (qtype) {
+    case KO_Q4_K: return KO_Q4K_BYTES;
+    case KO_Q5_K: return KO_Q5K_BYTES;
+    case KO_Q6_K: return KO_Q6K_BYTES;
+    default: return 0;
+    }
+}
+
+/* internal/tensor/tensor.go:629-676.  Two deliberate departures from IEEE
+ * half->single conversion are reproduced: 0x8000 yields +0 (the Go constant
+ * -0.0 is +0, tensor.go:637-639) and every NaN yields float32(math.NaN()),
+ * whose bits are 0x7FC00000 (tensor.go:669-670). */
+float ko_f16_to_f32(uint16_t h) {
+    uint32_t sign = (h >> 15) & 1u;
+    uint32_t exp = (h >> 10) & 0x1Fu;
+    uint32_t mant = h & 0x3FFu;
+    if (exp == 0) {
+        if (mant == 0) return bits_to_f32(0u); /* both zeros -> +0 */
+        uint32_t shift = 0, m = mant;
+        while ((m & 0x400u) == 0) {           /* tensor.go:647-652 */
+            m <<= 1;
+            shift++;
+        }
+        m &= 0x3FFu;
+        uint32_t exp32 = 127u - 14u - shift;  /* tensor.go:656 */
+        return bits_to_f32((sign << 31) | (exp32 << 23) | (m << 13));
+    }
+    if (exp == 31) {
+        if (mant == 0) return bits_to_f32((sign << 31) | 0x7F800000u);
+        return bits_to_f32(0x7FC00000u);
+    }
+    return bits_to_f32((sign << 31) | ((exp - 15u + 127u) << 23) | (mant << 13));
+}
+
+/* internal/tensor/tensor.go:606-627: truncating conversion used only by the
+ * reference's test quantizers. */
+uint16_t ko_f32_to_f16(float f) {
+    if (f == 0.0f) return 0;
+    uint32_t bits = f32_to_bits(f);
+    uint32_t sign = (bits >> 31) & 1u;
+    int32_t exp = (int32_t)((bits >> 23) & 0xFFu) - 127 + 15;
+    uint32_t mant = (bits >> 13) & 0x3FFu;
+    if (exp <= 0) return (uint16_t)(sign << 15);
+    if (exp >= 31) return (uint16_t)((sign << 15) | 0x7C00u);
+    return (uint16_t)((sign << 15) | ((uint32_t)exp << 10) | mant);
+}
+
+/* internal/tensor/quant_q5k.go:97-120 */
+void ko_extract_scales_mins(const uint8_t s[12], uint8_t sc[8], uint8_t m[8]) {
+    sc[0] = s[0] & 0x3F;
+    sc[1] = (uint8_t)((s[0] >> 6) | (s[1] << 2)) & 0x3F;
+    sc[2] = (uint8_t)((s[1] >> 4) | (s[2] << 4)) & 0x3F;
+    sc[3] = (s[2] >> 2) & 0x3F;
+    sc[4] = s[3] & 0x3F;
+    sc[5] = (uint8_t)((s[3] >> 6) | (s[4] << 2)) & 0x3F;
+    sc[6] = (uint8_t)((s[4] >> 4) | (s[5] << 4)) & 0x3F;
+    sc[7] = (s[5] >> 2) & 0x3F;
+    m[0] = s[6] & 0x3F;
+    m[1] = (uint8_t)((s[6] >> 6) | (s[7] << 2)) & 0x3F;
+    m[2] = (uint8_t)((s[7] >> 4) | (s[8] << 4)) & 0x3F;
+    m[3] = (s[8] >> 2) & 0x3F;
+    m[4] = s[9] & 0x3F;
+    m[5] = (uint8_t)((s[9] >> 6) | (s[10] << 2)) & 0x3F;
+    m[6] = (uint8_t)((s[10] >> 4) | (s[11] << 4)) & 0x3F;
+    m[7] = (s[11] >> 2) & 0x3F;
+}
+
+static inline uint16_t le16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* dequantizeQ4KBlockBatch, internal/tensor/block_cache.go:222-248 (same math
+ * as DequantizeQ4_K, quant_q4k.go:37-79).  Layout quant_q4k.go:137-157:
+ * d[0:2] dmin[2:4] scales[4:16] qs[16:144]. */
+void ko_dequant_block_q4k(const uint8_t *blk, float out[256]) {
+    float d = ko_f16_to_f32(le16(blk + 0));
+    float dmin = ko_f16_to_f32(le16(blk + 2));
+    uint8_t sc[8], m[8];
+    ko_extract_scales_mins(blk + 4, sc, m);
+    const uint8_t *qs = blk + 16;
+    for (int sb = 0; sb < 8; sb++) {
+        float scale = d * (float)sc[sb];
+        float mn = dmin * (float)m[sb];
+        for (int i = 0; i < 32; i++) {
+            int v = sb * 32 + i;
+            uint8_t bits = qs[v / 2];
+            uint8_t q = (v % 2 == 0) ? (bits & 0x0F) : (bits >> 4);
+            out[v] = scale * (float)q - mn;
+        }
+    }
+}
+
+/* dequantizeQ5KBlockBatch, internal/tensor/block_cache.go:82-122 (same math
+ * as DequantizeQ5_K, quant_q5k.go:39-88).  Layout quant_q5k.go:229-252:
+ * d[0:2] dmin[2:4] scales[4:16] qh[16:48] qs[48:176]. */
+void ko_dequant_block_q5k(const uint8_t *blk, float out[256]) {
+    float d = ko_f16_to_f32(le16(blk + 0));
+    float dmin = ko_f16_to_f32(le16(blk + 2));
+    uint8_t sc[8], m[8];
+    ko_extract_scales_mins(blk + 4, sc, m);
+    const uint8_t *qh = blk + 16;
+    const uint8_t *qs = blk + 48;
+    for (int sb = 0; sb < 8; sb++) {
+        float scale = d * (float)sc[sb];
+        float mn = dmin * (float)m[sb];
+        for (int i = 0; i < 32; i++) {
+            int v = sb * 32 + i;
+            uint8_t lo = qs[v / 2];
+            lo = (v % 2 == 0) ? (lo & 0x0F) : (lo >> 4);
+            uint8_t hi = (qh[v / 8] >> (v % 8)) & 0x01;
+            uint8_t q = lo | (uint8_t)(hi << 4);
+            out[v] = scale * (float)q - mn;
+        }
+    }
+}
+
+/* dequantizeQ6KBlockBatch, internal/tensor/block_cache.go:158-186 (same math
+ * as DequantizeQ6_K, quant_q6k.go:39-80).  Layout quant_q6k.go:134-156:
+ * ql[0:128] qh[128:192] scales[192:208] (int8) d[208:210]. */
+void ko_dequant_block_q6k(const uint8_t *blk, float out[256]) {
+    const uint8_t *ql = blk;
+    const uint8_t *qh = blk + 128;
+    const int8_t *scales = (const int8_t *)(blk + 192);
+    float d = ko_f16_to_f32(le16(blk + 208));
+    for (int i = 0; i < 256; i++) {
+        uint8_t lo = ql[i / 2];
+        lo = (i % 2 == 0) ? (lo & 0x0F) : (lo >> 4);
+        uint8_t hi = (qh[i / 4] >> ((i % 4) * 2)) & 0x03;
+        uint8_t q = lo | (uint8_t)(hi << 4);
+        float scale = (float)scales[i / 16];
+        out[i] = d * scale * (float)((int)q - 32); /* (d*scale)*(q-32) */
+    }
+}
+
+static void dequant_block(int qtype, const uint8_t *blk, float out[256]) {
+    switch (qtype) {
+    case KO_Q4_K: ko_dequant_block_q4k(blk, out); break;
+    case KO_Q5_K: ko_dequant_block_q5k(blk, out); break;
+    default: ko_dequant_block_q6k(blk, out); break;
+    }
+}
+
+/* DequantizeQ4_KTensor / Q5_K / Q6_K (quant_q4k.go:161-211,
+ * quant_q5k.go:256-307, quant_q6k.go:160-210). */
+int ko_dequantize(int qtype, const uint8_t *data, int64_t nblocks, float *out) {
+    int bb = ko_block_bytes(qtype);
+    if (bb == 0 || nblocks < 0) return -1;
+    for (int64_t b = 0; b < nblocks; b++) dequant_block(qtype, data + b * bb, out + b * 256);
+    return 0;
+}
+
+/* DequantTransposeQ4K/Q5K/Q6K, internal/tensor/dequant_transpose.go:15-157:
+ * numBlocks = M*N/256 (integer division), each block scattered to the
+ * transposed position out[col*M + row] (:44-51). */
+int ko_dequant_transpose(int qtype, const uint8_t *data, int64_t M, int64_t N, float *out) {
+    int bb = ko_block_bytes(qtype);
+    if (bb == 0 || M <= 0 || N <= 0) return -1;
+    int64_t total = M * N;
+    int64_t nblocks = total / 256;
+    memset(out, 0, (size_t)total * sizeof(float));
+    float buf[256];
+    for (int64_t bi = 0; bi < nblocks; bi++) {
+        dequant_block(qtype, data + bi * bb, buf);
+        int64_t g = bi * 256;
+        for (int k = 0; k < 256; k++) {
+            int64_t src = g + k;
+            int64_t row = src / N, col = src % N;
+            out[col * M + row] = buf[k];
+        }
+    }
+    return 0;
+}
+
+/* internal/tensor/simd_ops.go:60-78 */
+float ko_vector_dot(const float *a, const float *b, int64_t n) {
+    float s0 = 0, s1 = 0, s2 = 0, s3 = 0, s4 = 0, s5 = 0, s6 = 0, s7 = 0;
+    int64_t i = 0;
+    for (; i + 7 < n; i += 8) {
+        s0 += a[i] * b[i];
+        s1 += a[i + 1] * b[i + 1];
+        s2 += a[i + 2] * b[i + 2];
+        s3 += a[i + 3] * b[i + 3];
+        s4 += a[i + 4] * b[i + 4];
+        s5 += a[i + 5] * b[i + 5];
+        s6 += a[i + 6] * b[i + 6];
+        s7 += a[i + 7] * b[i + 7];
+    }
+    for (; i < n; i++) s0 += a[i] * b[i];
+    return s0 + s1 + s2 + s3 + s4 + s5 + s6 + s7;
+}
+
+/* internal/tensor/simd_ops.go:82-98 */
+void ko_vector_scale_add(float *dst, const float *src, int64_t n, float scale) {
+    int64_t i = 0;
+    for (; i + 7 < n; i += 8) {
+        dst[i] += src[i] * scale;
+        dst[i + 1] += src[i + 1] * scale;
+        dst[i + 2] += src[i + 2] * scale;
+        dst[i + 3] += src[i + 3] * scale;
+        dst[i + 4] += src[i + 4] * scale;
+        dst[i + 5] += src[i + 5] * scale;
+        dst[i + 6] += src[i + 6] * scale;
+        dst[i + 7] += src[i + 7] * scale;
+    }
+    for (; i < n; i++) dst[i] += src[i] * scale;
+}
+
+/* ---- worker fan-out standing in for the goroutines ---------------------- */
+
+typedef struct {
+    const float *a, *wt;
+    float *c;
+    int64_t M, K, N, lo, hi;
+} ko_job;
+
+static void *single_row_worker(void *p) {
+    ko_job *j = (ko_job *)p;
+    for (int64_t col = j->lo; col < j->hi; col++)
+        j->c[col] = ko_vector_dot(j->a, j->wt + col * j->K, j->K);
+    return NULL;
+}
+
+static void *parallel_rows_worker(void *p) {
+    ko_job *j = (ko_job *)p;
+    for (int64_t i = j->lo; i < j->hi; i++) {
+        const float *arow = j->a + i * j->K;
+        float *crow = j->c + i * j->N;
+        for (int64_t col = 0; col < j->N; col++)
+            crow[col] = ko_vector_dot(arow, j->wt + col * j->K, j->K);
+    }
+    return NULL;
+}
+
+static void run_jobs(void *(*fn)(void *), ko_job *jobs, int n) {
+    if (n == 1) {
+        fn(&jobs[0]);
+        return;
+    }
+    pthread_t *th = (pthread_t *)malloc(sizeof(pthread_t) * (size_t)n);
+    int *started = (int *)calloc((size_t)n, sizeof(int));
+    for (int w = 0; w < n; w++) started[w] = pthread_create(&th[w], NULL, fn, &jobs[w]) == 0;
+    for (int w = 0; w < n; w++) {
+        if (started[w]) pthread_join(th[w], NULL);
+        else fn(&jobs[w]);
+    }
+    free(started);
+    free(th);
+}
+
+/* matmul_simd.go:150-201, transposed branch :165-188.  numWorkers =
+ * min(NumCPU, N); colsPerWorker = ceil(N/numWorkers). */
+void ko_matmul_single_row_t(const float *x, const float *wt, int64_t K, int64_t N, float *y,
+                            int nthreads) {
+    int64_t workers = nthreads < 1 ? 1 : nthreads;
+    if (workers > N) workers = N;
+    int64_t per = (N + workers - 1) / workers;
+    ko_job *jobs = (ko_job *)calloc((size_t)workers, sizeof(ko_job));
+    for (int64_t w = 0; w < workers; w++) {
+        int64_t lo = w * per, hi = lo + per;
+        if (hi > N) hi = N;
+        if (lo > hi) lo = hi;
+        ko_job j = {x, wt, y, 1, K, N, lo, hi};
+        jobs[w] = j;
+    }
+    run_jobs(single_row_worker, jobs, (int)workers);
+    free(jobs);
+}
+
+/* matmul_simd.go:189-199: c starts at zero (Zeros, :157); rows with
+ * x[k] == 0 are skipped. */
+void ko_matmul_single_row_u(const float *x, const float *w, int64_t K, int64_t N, float *y) {
+    memset(y, 0, (size_t)N * sizeof(float));
+    for (int64_t k = 0; k < K; k++) {
+        float av = x[k];
+        if (av == 0) continue;
+        ko_vector_scale_add(y, w + k * N, N, av);
+    }
+}
+
+/* matmul_simd.go:13-69 (B pre-transposed or transposed into the pool buffer;
+ * either way c[i][j] = dot(a_i, bT_j)). */
+void ko_matmul_simd_t(const float *a, const float *wt, int64_t M, int64_t K, int64_t N, float *c) {
+    for (int64_t i = 0; i < M; i++)
+        for (int64_t col = 0; col < N; col++)
+            c[i * N + col] = ko_vector_dot(a + i * K, wt + col * K, K);
+}
+
+/* matmul_simd.go:72-146, transposed branch :91-112: 64-wide blocks over
+ * (i, j, k); each k-chunk's sum is added into c (which starts at zero). */
+void ko_matmul_blocked_t(const float *a, const float *wt, int64_t M, int64_t K, int64_t N, float *c) {
+    const int64_t bs = 64;
+    memset(c, 0, (size_t)(M * N) * sizeof(float));
+    for (int64_t i0 = 0; i0 < M; i0 += bs)
+        for (int64_t j0 = 0; j0 < N; j0 += bs)
+            for (int64_t k0 = 0; k0 < K; k0 += bs) {
+                int64_t iM = i0 + bs < M ? i0 + bs : M;
+                int64_t jM = j0 + bs < N ? j0 + bs : N;
+                int64_t kM = k0 + bs < K ? k0 + bs : K;
+                for (int64_t i = i0; i < iM; i++)
+                    for (int64_t j = j0; j < jM; j++) {
+                        float sum = 0;
+                        for (int64_t k = k0; k < kM; k++) sum += a[i * K + k] * wt[j * K + k];
+                        c[i * N + j] += sum;
+                    }
+            }
+}
+
+/* matmul_simd.go:204-276: rowsPerWorker = ceil(M/NumCPU). */
+void ko_matmul_parallel_t(const float *a, const float *wt, int64_t M, int64_t K, int64_t N, float *c,
+                          int nthreads) {
+    int64_t workers = nthreads < 1 ? 1 : nthreads;
+    int64_t per = (M + workers - 1) / workers;
+    ko_job *jobs = (ko_job *)calloc((size_t)workers, sizeof(ko_job));
+    for (int64_t w = 0; w < workers; w++) {
+        int64_t lo = w * per, hi = lo + per;
+        if (hi > M) hi = M;
+        if (lo > hi) lo = hi;
+        ko_job j = {a, wt, c, M, K, N, lo, hi};
+        jobs[w] = j;
+    }
+    run_jobs(parallel_rows_worker, jobs, (int)workers);
+    free(jobs);
+}
+
+/* The size dispatch of MatMul (matmul.go:75-89) once B is float32 and
+ * transposed ([N,K]); HasAVX2() is always true on amd64 (simd.go:27-34). */
+static void dispatch_transposed(const float *a, const float *wt, int64_t M, int64_t K, int64_t N,
+                                float *c, int nthreads) {
+    if (M == 1) {
+        ko_matmul_single_row_t(a, wt, K, N, c, nthreads);
+        return;
+    }
+    int64_t ops = M * N * K;
+    if (ops < 1024) ko_matmul_simd_t(a, wt, M, K, N, c);
+    else if (ops < 1024 * 1024) ko_matmul_blocked_t(a, wt, M, K, N, c);
+    else ko_matmul_parallel_t(a, wt, M, K, N, c, nthreads);
+}
+
+/* tensor.MatMul with a quantized B, matmul.go:46-99 + GetOrDequantTranspose
+ * tensor.go:535-588 (fused dequant-transpose for 2-D tensors). */
+int ko_matmul_quant(int qtype, const float *a, int64_t M, int64_t K, const uint8_t *bq, int64_t N,
+                    float *c, float *wt_scratch, int nthreads) {
+    if (ko_block_bytes(qtype) == 0 || M <= 0 || K <= 0 || N <= 0) return -1;
+    if (ko_dequant_transpose(qtype, bq, K, N, wt_scratch) != 0) return -1;
+    dispatch_transposed(a, wt_scratch, M, K, N, c, nthreads);
+    return 0;
+}
+
+/* LM-head route, internal/transformer/model.go:389-403: Dequantize
+ * (ops.go:486-530, untransposed [K,N]) then MatMul.  For an untransposed
+ * float32 B, GetOrDequantTranspose returns B unchanged (tensor.go:543-547);
+ * M == 1 takes the outer-product branch (matmul_simd.go:189-199); larger M
+ * transposes B into a pool buffer (matmul_simd.go:36-45, :227-237) or walks
+ * its columns (:113-138) with the same arithmetic as the transposed kernels. */
+int ko_matmul_dequant_untransposed(int qtype, const float *a, int64_t M, int64_t K,
+                                   const uint8_t *bq, int64_t N, float *c, float *w_scratch,
+                                   int nthreads) {
+    if (ko_block_bytes(qtype) == 0 || M <= 0 || K <= 0 || N <= 0) return -1;
+    int64_t nblocks = (K * N + 255) / 256;
+    if (ko_dequantize(qtype, bq, nblocks, w_scratch) != 0) return -1;
+    if (M == 1) {
+        ko_matmul_single_row_u(a, w_scratch, K, N, c);
+        return 0;
+    }
+    float *wt = (float *)malloc((size_t)(K * N) * sizeof(float));
+    if (!wt) return -2;
+    for (int64_t k = 0; k < K; k++)
+        for (int64_t n = 0; n < N; n++) wt[n * K + k] = w_scratch[k * N + n];
+    dispatch_transposed(a, wt, M, K, N, c, nthreads);
+    free(wt);
+    return 0;
+}

@@ -1,0 +1,73 @@
+"""Shared helpers for the parity tests (the oracle is the checker)."""
+from __future__ import annotations
+
+import numpy as np
+
+Q4_K, Q5_K, Q6_K = 12, 13, 14
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
+GEMV_TOL = 1e-5    # max |y - y_ref| / sum_k |x_k W_kn|, fp32-accumulate GEMV
+GEMM_TOL = 2e-2    # same metric, bf16 tensor-core GEMM
+
+
+def matmul_error(y: np.ndarray, x: np.ndarray, w: np.ndarray, y_ref: np.ndarray | None = None,
+                 col_chunk: int = 8192) -> float:
+    """max over (m, n) of |y - y_exact| / sum_k |x[m,k] * W[k,n]|, with y_exact
+    in float64 (or |y - y_ref| when y_ref is given).  w is float32 [K, N]."""
+    x64 = x.astype(np.float64).reshape(-1, w.shape[0])
+    worst = 0.0
+    for c0 in range(0, w.shape[1], col_chunk):
+        wc = w[:, c0:c0 + col_chunk].astype(np.float64)
+        bound = np.abs(x64) @ np.abs(wc)
+        ref = (x64 @ wc) if y_ref is None else y_ref.reshape(x64.shape[0], -1)[:, c0:c0 + col_chunk]
+        err = np.abs(y.reshape(x64.shape[0], -1)[:, c0:c0 + col_chunk].astype(np.float64) - ref)
+        ratio = np.where(bound > 0, err / np.where(bound > 0, bound, 1.0), np.where(err > 0, np.inf, 0.0))
+        worst = max(worst, float(np.max(ratio)))
+    return worst
+
+
+def encode_q6k_exact(values: np.ndarray) -> np.ndarray:
+    """Q6_K blocks holding small integers exactly: d = 1, every scale 1,
+    q = v + 32 (v in [-32, 31])."""
+    v = np.asarray(values, dtype=np.int64).reshape(-1)
+    nb = (v.size + 255) // 256
+    out = np.zeros((nb, 210), np.uint8)
+    q = np.full(nb * 256, 32, np.int64)
+    q[:v.size] = v + 32
+    q = q.reshape(nb, 256)
+    idx = np.arange(256)
+    for i in range(256):
+        lo, hi = q[:, i] & 0xF, q[:, i] >> 4
+        out[:, i // 2] |= (lo << (4 * (i % 2))).astype(np.uint8)
+        out[:, 128 + i // 4] |= (hi << (2 * (i % 4))).astype(np.uint8)
+    del idx
+    out[:, 192:208] = 1
+    out[:, 208], out[:, 209] = 0x00, 0x3C
+    return out.reshape(-1)
+
+
+def encode_q45k_exact(values: np.ndarray, qtype: int) -> np.ndarray:
+    """Q4_K / Q5_K blocks holding small non-negative integers exactly:
+    d = 1, dmin = 0, every sub-block scale 1 (q = v, v < 16 or < 32)."""
+    v = np.asarray(values, dtype=np.int64).reshape(-1)
+    nb = (v.size + 255) // 256
+    bb = BLOCK_BYTES[qtype]
+    out = np.zeros((nb, bb), np.uint8)
+    q = np.zeros(nb * 256, np.int64)
+    q[:v.size] = v
+    q = q.reshape(nb, 256)
+    out[:, 0], out[:, 1] = 0x00, 0x3C          # d = 1.0
+    # scales 0..7 = 1: 24-bit LE groups of four 6-bit fields -> 0x041041
+    for g in range(2):
+        out[:, 4 + 3 * g], out[:, 5 + 3 * g], out[:, 6 + 3 * g] = 0x41, 0x10, 0x04
+    qs0 = 16 if qtype == Q4_K else 48
+    for i in range(256):
+        out[:, qs0 + i // 2] |= ((q[:, i] & 0xF) << (4 * (i % 2))).astype(np.uint8)
+        if qtype == Q5_K:
+            out[:, 16 + i // 8] |= (((q[:, i] >> 4) & 1) << (i % 8)).astype(np.uint8)
+    return out.reshape(-1)
+
+
+def same_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Bitwise equality with NaN as one class."""
+    ab, bb = a.view(np.uint32), b.view(np.uint32)
+    return (ab == bb) | (np.isnan(a) & np.isnan(b))

@@ -1,0 +1,306 @@
+"""Pins the CPU oracle against the reference's own known-answer tests and
+against the fixtures of the independent numpy restatement (tests/golden/).
+
+Known-answer values are transcribed from the reference's test files; each
+test names the file:line it follows (paths relative to xupit3r/vibrant).
+"""
+import glob
+import math
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def bits(f):
+    return int(np.array([f], np.float32).view(np.uint32)[0])
+
+
+def same_f32(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """Bit-identical, with every NaN treated as one class (NaN payloads are
+    not defined by the Go spec and differ between x86 and the GPU)."""
+    a = a_bits.view(np.float32)
+    b = b_bits.view(np.float32)
+    return (a_bits == b_bits) | (np.isnan(a) & np.isnan(b))
+
+
+# ---- float16ToFloat32 -------------------------------------------------------
+
+@pytest.mark.parametrize("h,expected,eps", [
+    (0x00FD, 1.5079975e-5, 1e-8),    # float16_test.go:17-22
+    (0x0001, 5.960464e-8, 1e-10),    # :23-28
+    (0x03FF, 6.097555e-5, 1e-8),     # :29-34
+    (0x8001, -5.960464e-8, 1e-10),   # :35-40
+    (0x3C00, 1.0, 1e-6),             # :64-69
+    (0xBC00, -1.0, 1e-6),            # :70-75
+    (0x3800, 0.5, 1e-6),             # :76-81
+    (0x4000, 2.0, 1e-6),             # :82-87
+])
+def test_f16_known_values(oracle, h, expected, eps):
+    assert abs(oracle.f16_to_f32(h) - expected) <= eps
+
+
+def test_f16_specials(oracle):
+    # float16_test.go:104-150
+    assert oracle.f16_to_f32_bits(0x0000) == 0
+    # 0x8000 -> +0: the Go constant -0.0 is +0 (tensor.go:637-639)
+    assert oracle.f16_to_f32_bits(0x8000) == 0
+    assert math.isinf(oracle.f16_to_f32(0x7C00)) and oracle.f16_to_f32(0x7C00) > 0
+    assert math.isinf(oracle.f16_to_f32(0xFC00)) and oracle.f16_to_f32(0xFC00) < 0
+    assert oracle.f16_to_f32_bits(0x7E00) == 0x7FC00000   # float32(math.NaN())
+    assert oracle.f16_to_f32_bits(0xFE01) == 0x7FC00000
+
+
+def test_f16_all_codes_match_numpy_restatement(oracle):
+    ref = np.load(os.path.join(GOLDEN, "f16_to_f32.npz"))["f32_bits"]
+    got = np.array([oracle.f16_to_f32_bits(h) for h in range(65536)], np.uint32)
+    assert np.array_equal(got, ref)
+
+
+def test_f32_to_f16_codes(oracle):
+    # quant_q5k_test.go:311-329
+    assert oracle.f32_to_f16(0.0) == 0x0000
+    assert oracle.f32_to_f16(1.0) == 0x3C00
+    assert oracle.f32_to_f16(-1.0) == 0xBC00
+
+
+# ---- extractScalesAndMins ---------------------------------------------------
+
+def test_extract_scales_all_ones(oracle):
+    # quant_q5k_test.go:151-169: every 6-bit value is 63
+    sc, m = oracle.extract_scales_mins(b"\xff" * 12)
+    assert list(sc) == [63] * 8 and list(m) == [63] * 8
+
+
+def test_extract_scales_mixed(oracle):
+    # quant_q5k_test.go:121-149: zero scale bytes, 0xFF min bytes
+    sc, m = oracle.extract_scales_mins(b"\x00" * 6 + b"\xff" * 6)
+    assert all(v <= 63 for v in sc)
+    assert all(0 < v <= 63 for v in m)
+
+
+def test_extract_scales_is_24bit_le_packing(oracle):
+    # the packing is four 6-bit fields per little-endian 24-bit group; this is
+    # the identity the CUDA decoder relies on
+    rng = np.random.default_rng(1)
+    for _ in range(200):
+        s = rng.integers(0, 256, 12, dtype=np.uint8)
+        sc, m = oracle.extract_scales_mins(s.tobytes())
+        for grp in range(2):
+            w = int(s[3 * grp]) | int(s[3 * grp + 1]) << 8 | int(s[3 * grp + 2]) << 16
+            wm = int(s[6 + 3 * grp]) | int(s[7 + 3 * grp]) << 8 | int(s[8 + 3 * grp]) << 16
+            for j in range(4):
+                assert sc[4 * grp + j] == (w >> (6 * j)) & 63
+                assert m[4 * grp + j] == (wm >> (6 * j)) & 63
+
+
+# ---- block decoders: known answers --------------------------------------------
+
+def q6k_block(ql=None, qh=None, scales=None, d=0):
+    b = bytearray(210)
+    for i, v in (ql or {}).items():
+        b[i] = v
+    for i, v in (qh or {}).items():
+        b[128 + i] = v
+    for i, v in (scales or {}).items():
+        b[192 + i] = v & 0xFF
+    b[208] = d & 0xFF
+    b[209] = d >> 8
+    return np.frombuffer(bytes(b), np.uint8)
+
+
+def test_q6k_all_bits_set(oracle):
+    # quant_q6k_test.go:27-59: q = 63, scale 1, d 1 -> 31
+    blk = q6k_block(ql={i: 0xFF for i in range(4)}, qh={i: 0xFF for i in range(4)},
+                    scales={i: 1 for i in range(16)}, d=oracle.f32_to_f16(1.0))
+    out = oracle.dequantize(14, blk)
+    assert np.all(out[:8] == 31.0)
+
+
+def test_q6k_element(oracle):
+    # quant_q6k_test.go:134-172: q = 5 | 2<<4 = 37 -> 5.0
+    blk = q6k_block(ql={0: 0x05}, qh={0: 0x02}, scales={i: 1 for i in range(16)},
+                    d=oracle.f32_to_f16(1.0))
+    assert oracle.dequantize(14, blk)[0] == 5.0
+
+
+def test_q6k_integration_tensor_at(oracle):
+    # quant_q6k_integration_test.go:106-145: d 2, scale 3, q 50 -> 108
+    blk = q6k_block(ql={0: 0x02}, qh={0: 0x03}, scales={0: 3}, d=oracle.f32_to_f16(2.0))
+    assert oracle.dequantize(14, blk)[0] == 108.0
+
+
+def test_q6k_zero_block(oracle):
+    # quant_q6k_test.go:9-24
+    assert np.all(oracle.dequantize(14, np.zeros(210, np.uint8)) == 0)
+
+
+def test_q6k_parse_offsets(oracle):
+    # quant_q6k_test.go:187-232: ql at 0, qh at 128, scales at 192, d at 208 (LE)
+    blk = q6k_block(ql={0: 0x12, 1: 0x34}, qh={0: 0xAB, 1: 0xCD}, scales={0: 1, 1: 2}, d=0x3412)
+    out = oracle.dequantize(14, blk)
+    d = oracle.f16_to_f32(0x3412)
+    # value 0: low nibble of 0x12 = 2, qh bits 0-1 of 0xAB = 3 -> q = 50
+    assert out[0] == np.float32(np.float32(d) * np.float32(1)) * np.float32(50 - 32)
+    # value 1: high nibble 1, qh bits 2-3 of 0xAB = 2 -> q = 33
+    assert out[1] == np.float32(d) * np.float32(1)
+    # value 16 uses Scales[1] = 2; ql[8] and qh[4] are zero -> q = 0
+    assert out[16] == np.float32(np.float32(d) * np.float32(2)) * np.float32(-32)
+
+
+def test_q5k_parse_offsets(oracle):
+    # quant_q5k_test.go:217-239: d from bytes 0-1, dmin from bytes 2-3 (LE)
+    b = bytearray(176)
+    b[0], b[1], b[2], b[3] = 0x12, 0x34, 0x56, 0x78
+    b[4] = 1          # sc[0] = 1
+    b[10] = 1         # m[0] = 1
+    b[48] = 0x03      # value 0 low nibble 3
+    b[16] = 0x01      # value 0 high bit
+    out = oracle.dequantize(13, np.frombuffer(bytes(b), np.uint8))
+    d = np.float32(oracle.f16_to_f32(0x3412))
+    dmin = np.float32(oracle.f16_to_f32(0x7856))
+    assert out[0] == np.float32(d * np.float32(1) * np.float32(19)) - np.float32(dmin * np.float32(1))
+
+
+def test_q5k_known_values_nonzero(oracle):
+    # quant_q5k_test.go:26-50 (asserts only a non-zero first value)
+    b = bytearray(176)
+    h = oracle.f32_to_f16(1.0)
+    b[0], b[1] = h & 0xFF, h >> 8
+    b[4:16] = bytes([32, 170, 170, 10, 32, 170, 170, 10, 32, 170, 170, 10])
+    for i in range(4):
+        b[16 + i] = 0xFF
+        b[48 + i] = 0xFF
+    out = oracle.dequantize(13, np.frombuffer(bytes(b), np.uint8))
+    assert out[0] != 0
+    assert out[0] == np.float32(32 * 31)   # sc[0] = 32, q = 31, dmin = 0
+
+
+def test_q4k_dequant_element_equals_batch(oracle):
+    # quant_q4k_test.go:48-91: per-element and batch dequantization agree;
+    # the oracle's batch decoder is checked against an element-wise restatement
+    rng = np.random.default_rng(7)
+    blk = rng.integers(0, 256, 144, dtype=np.uint8)
+    blk[1] = 0x3C
+    blk[3] = 0x38
+    out = oracle.dequantize(12, blk)
+    d = np.float32(oracle.f16_to_f32(int(blk[0]) | int(blk[1]) << 8))
+    dmin = np.float32(oracle.f16_to_f32(int(blk[2]) | int(blk[3]) << 8))
+    sc, m = oracle.extract_scales_mins(blk[4:16].tobytes())
+    for i in range(256):
+        byte = int(blk[16 + i // 2])
+        q = byte & 0xF if i % 2 == 0 else byte >> 4
+        v = np.float32(np.float32(d * np.float32(sc[i // 32])) * np.float32(q)) - \
+            np.float32(dmin * np.float32(m[i // 32]))
+        assert abs(float(out[i]) - float(v)) <= 1e-6
+
+
+# ---- fixtures of the independent restatement ----------------------------------
+
+@pytest.mark.parametrize("name,qtype", [("q4k", 12), ("q5k", 13), ("q6k", 14)])
+def test_dequant_matches_fixture_bit_exact(oracle, name, qtype):
+    f = np.load(os.path.join(GOLDEN, f"dequant_{name}.npz"))
+    got = oracle.dequantize(qtype, f["blocks"]).view(np.uint32)
+    assert np.all(same_f32(got, f["f32_bits"]))
+    # the random-byte fixtures reach subnormal, zero, infinite and NaN scales
+    vals = f["f32_bits"].view(np.float32)
+    assert np.isnan(vals).any() and np.isinf(vals).any()
+
+
+def build_tensor(qtype, M, N):
+    """buildQ4KTestTensor / buildQ5KTestTensor / buildQ6KTestTensor,
+    dequant_transpose_test.go:10-108."""
+    nb = M * N // 256
+    bb = {12: 144, 13: 176, 14: 210}[qtype]
+    raw = np.zeros((nb, bb), np.uint8)
+    j128 = np.arange(128)
+    if qtype == 14:
+        raw[:, 208] = 0x00
+        raw[:, 209] = 0x3C
+        raw[:, 192:208] = np.arange(1, 17, dtype=np.uint8)
+        raw[:, 0:128] = (j128 * 3) & 0xFF
+    else:
+        raw[:, 0], raw[:, 1], raw[:, 2], raw[:, 3] = 0x00, 0x3C, 0x00, 0x38
+        raw[:, 4:16] = np.arange(1, 13, dtype=np.uint8)
+        if qtype == 12:
+            raw[:, 16:144] = (j128 * 5) & 0xFF
+        else:
+            raw[:, 16:48] = (np.arange(32) * 7) & 0xFF
+            raw[:, 48:176] = (j128 * 3) & 0xFF
+    return raw.reshape(-1)
+
+
+@pytest.mark.parametrize("qtype", [12, 13, 14])
+def test_dequant_transpose_equals_separate(oracle, qtype):
+    # dequant_transpose_test.go:110-172: fused == dequant then transpose (<= 1e-6)
+    M = N = 256
+    raw = build_tensor(qtype, M, N)
+    fused = oracle.dequant_transpose(qtype, raw, M, N)
+    sep = oracle.dequantize(qtype, raw).reshape(M, N).T
+    assert fused.shape == (N, M)
+    assert np.max(np.abs(fused - sep)) <= 1e-6
+    assert np.array_equal(fused.view(np.uint32), np.ascontiguousarray(sep).view(np.uint32))
+
+
+def test_dequant_transpose_drops_partial_tail(oracle):
+    # dequant_transpose.go:26: numBlocks = M*N/256 -- a trailing partial block
+    # is not expanded by the fused path (it stays zero)
+    raw = build_tensor(12, 256, 256)[: 144 * 1]
+    raw = np.concatenate([raw, raw])          # two blocks for 4*96 = 384 values
+    out = oracle.dequant_transpose(12, raw, 4, 96)
+    sep = oracle.dequantize(12, raw)[:384].reshape(4, 96).T
+    full = 256
+    flat_idx = np.arange(384).reshape(4, 96).T
+    assert np.array_equal(out[flat_idx < full], sep[flat_idx < full])
+    assert np.all(out[flat_idx >= full] == 0)
+
+
+def _matmul_fixtures():
+    return sorted(glob.glob(os.path.join(GOLDEN, "matmul_*.npz")))
+
+
+@pytest.mark.parametrize("path", _matmul_fixtures(), ids=os.path.basename)
+def test_matmul_matches_fixture_bit_exact(oracle, path):
+    f = np.load(path)
+    qt, K, N = int(f["qtype"]), int(f["K"]), int(f["N"])
+    if path.endswith("_dot.npz"):
+        y = oracle.matmul_quant(qt, f["x"], f["wq"], K, N, nthreads=3)[0]
+    else:
+        y = oracle.matmul_dequant_untransposed(qt, f["x"], f["wq"], K, N)[0]
+    # same arithmetic order as the restatement -> identical bits
+    assert np.array_equal(y.view(np.uint32), f["y"].view(np.uint32))
+    # and within the matmul metric of the exact product
+    err = np.max(np.abs(y.astype(np.float64) - f["y64"]) / f["bound"])
+    assert err <= 1e-5
+
+
+def test_cuda_matmul_golden_values_through_oracle(oracle):
+    # tensor_cuda_test.go:218-266: [1,2,3,4] @ [[1..12]] -> [70, 80, 90];
+    # here with B stored as Q6_K (d = 1, scales 1, q = w + 32 -> exact)
+    vals = np.arange(1, 13)
+    b = bytearray(210)
+    for i, w in enumerate(vals):
+        q = int(w) + 32
+        lo, hi = q & 0xF, q >> 4
+        b[i // 2] |= lo if i % 2 == 0 else lo << 4
+        b[128 + i // 4] |= hi << (2 * (i % 4))
+    for g in range(16):
+        b[192 + g] = 1
+    b[208], b[209] = 0x00, 0x3C
+    y = oracle.matmul_dequant_untransposed(14, np.array([1, 2, 3, 4], np.float32),
+                                           np.frombuffer(bytes(b), np.uint8), 4, 3)
+    assert list(y[0]) == [70.0, 80.0, 90.0]
+    # tensor_cuda_test.go:268-318: [[1,2,3],[4,5,6]] @ [[1,2],[3,4],[5,6]]
+    b2 = bytearray(210)
+    for i, w in enumerate([1, 2, 3, 4, 5, 6]):
+        q = w + 32
+        b2[i // 2] |= (q & 0xF) if i % 2 == 0 else (q & 0xF) << 4
+        b2[128 + i // 4] |= (q >> 4) << (2 * (i % 4))
+    for g in range(16):
+        b2[192 + g] = 1
+    b2[208], b2[209] = 0x00, 0x3C
+    y2 = oracle.matmul_dequant_untransposed(14, np.array([[1, 2, 3], [4, 5, 6]], np.float32),
+                                            np.frombuffer(bytes(b2), np.uint8), 3, 2)
+    assert y2.reshape(-1).tolist() == [22.0, 28.0, 49.0, 64.0]

@@ -1,0 +1,261 @@
+// capi.cu -- extern "C" entry points of libvkq.so (declared in include/vkq.h).
+//
+// Each entry point makes `device` current on the calling thread, validates
+// its arguments the way vibrant's cgo wrappers do before launching
+// (internal/gpu/cuda/library.go:95-100: null pointers and non-positive
+// dimensions are rejected), launches on the caller's stream and reports
+// errors as a status code plus a thread-local message instead of the
+// reference's "return nil and fall back to the CPU" (ops_cuda.go:34-38,75-84):
+// this path has no CPU fallback.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/vkq.h"
+#include "vkq_internal.h"
+
+namespace vkq {
+
+static thread_local char t_err[512] = "";
+
+void set_error(const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+
+int device_sm_count(int device) {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    int dev = device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev >= 64) dev = 63;
+    std::lock_guard<std::mutex> g(mu);
+    if (cache[dev] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        cache[dev] = v;
+    }
+    return cache[dev];
+}
+
+static int block_bytes(int qt) {
+    switch (qt) {
+    case VKQ_Q4_K: return 144;
+    case VKQ_Q5_K: return 176;
+    case VKQ_Q6_K: return 210;
+    default: return 0;
+    }
+}
+
+// Makes the device current and checks it is a compute capability 10.x part
+// (the kernels are built for sm_100a only).
+static int enter(int device) {
+    t_err[0] = '\0';
+    int dev = device;
+    if (device >= 0) {
+        cudaError_t e = cudaSetDevice(device);
+        if (e != cudaSuccess) {
+            set_error("cudaSetDevice(%d): %s", device, cudaGetErrorString(e));
+            return VKQ_ERR_CUDA;
+        }
+    } else if (cudaGetDevice(&dev) != cudaSuccess) {
+        set_error("no current CUDA device");
+        return VKQ_ERR_CUDA;
+    }
+    static int cc_major[64] = {0};
+    int d = dev < 64 ? dev : 63;
+    if (cc_major[d] == 0) {
+        int major = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+            set_error("cannot query device %d", dev);
+            return VKQ_ERR_CUDA;
+        }
+        cc_major[d] = major;
+    }
+    if (cc_major[d] != 10) {
+        set_error("device %d has compute capability %d.x; libvkq is built for sm_100a only", dev, cc_major[d]);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    return VKQ_OK;
+}
+
+static int check_launch(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) {
+        set_error("%s: %s", what, cudaGetErrorString(e));
+        return VKQ_ERR_CUDA;
+    }
+    return VKQ_OK;
+}
+
+static int check_matmul_args(int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
+                             int64_t M, float *y) {
+    int bb = block_bytes(qtype);
+    if (bb == 0) {
+        set_error("unsupported qtype %d (expected 12, 13 or 14)", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!w || !x || !y) {
+        set_error("null pointer passed to matmul");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (K <= 0 || N <= 0 || M <= 0) {
+        set_error("invalid dimensions: M=%lld, N=%lld, K=%lld", (long long)M, (long long)N, (long long)K);
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (K > (int64_t(1) << 40) / N) {
+        set_error("weight too large: K=%lld N=%lld", (long long)K, (long long)N);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    const int64_t need = ((K * N + 255) / 256) * bb;
+    if (w_bytes < need) {
+        set_error("weight buffer holds %lld bytes, a [%lld x %lld] weight needs %lld", (long long)w_bytes,
+                  (long long)K, (long long)N, (long long)need);
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (reinterpret_cast<uintptr_t>(w) & 15u) {
+        set_error("weight pointer must be 16-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 3u) {
+        set_error("x and y must be 4-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return VKQ_OK;
+}
+
+}  // namespace vkq
+
+using namespace vkq;
+
+extern "C" {
+
+int vkq_abi_version(void) { return VKQ_ABI_VERSION; }
+
+const char *vkq_status_string(int status) {
+    switch (status) {
+    case VKQ_OK: return "ok";
+    case VKQ_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case VKQ_ERR_UNSUPPORTED: return "unsupported";
+    case VKQ_ERR_MISALIGNED: return "misaligned pointer";
+    case VKQ_ERR_WORKSPACE: return "workspace missing or too small";
+    case VKQ_ERR_CUDA: return "CUDA error";
+    case VKQ_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case VKQ_ERR_NCCL: return "NCCL error";
+    default: return "unknown status";
+    }
+}
+
+const char *vkq_last_error(void) { return t_err; }
+
+int64_t vkq_block_bytes(int qtype) { return block_bytes(qtype); }
+
+int vkq_weight_bytes(int qtype, int64_t K, int64_t N, int64_t *bytes) {
+    t_err[0] = '\0';
+    int bb = block_bytes(qtype);
+    if (bb == 0) {
+        set_error("unsupported qtype %d", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!bytes || K <= 0 || N <= 0) {
+        set_error("invalid arguments to vkq_weight_bytes");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    *bytes = ((K * N + 255) / 256) * bb;
+    return VKQ_OK;
+}
+
+int vkq_dequantize_f32(int device, int qtype, const void *w, int64_t nblocks, float *out, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (block_bytes(qtype) == 0) {
+        set_error("unsupported qtype %d", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!w || !out || nblocks <= 0) {
+        set_error("invalid arguments to vkq_dequantize_f32");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (reinterpret_cast<uintptr_t>(out) & 3u) {
+        set_error("out must be 4-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(dequantize_f32(qtype, w, nblocks, out, (cudaStream_t)stream, device), "dequantize");
+}
+
+int vkq_dequant_transpose_f32(int device, int qtype, const void *w, int64_t K, int64_t N, float *out,
+                              void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (block_bytes(qtype) == 0) {
+        set_error("unsupported qtype %d", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!w || !out || K <= 0 || N <= 0) {
+        set_error("invalid arguments to vkq_dequant_transpose_f32");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    return check_launch(dequant_transpose_f32(qtype, w, K, N, out, (cudaStream_t)stream, device),
+                        "dequant_transpose");
+}
+
+int vkq_matmul_workspace_bytes(int device, int qtype, int64_t M, int64_t K, int64_t N, size_t *bytes) {
+    int st = enter(device);
+    if (st) return st;
+    if (!bytes || M <= 0 || K <= 0 || N <= 0 || block_bytes(qtype) == 0) {
+        set_error("invalid arguments to vkq_matmul_workspace_bytes");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (M <= 8) {
+        GemvShape s{qtype, K, N, M};
+        *bytes = gemv_workspace_bytes(s, device);
+        return VKQ_OK;
+    }
+    set_error("M=%lld > 8: the tensor-core path is not built in this library", (long long)M);
+    return VKQ_ERR_UNSUPPORTED;
+}
+
+int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
+             int64_t M, float *y, void *workspace, size_t workspace_bytes, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, y);
+    if (st) return st;
+    if (M > 8) {
+        set_error("vkq_gemv serves 1 <= M <= 8 (got %lld)", (long long)M);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    GemvShape s{qtype, K, N, M};
+    return gemv_launch(s, w, w_bytes, x, y, workspace, workspace_bytes, (cudaStream_t)stream, device);
+}
+
+int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
+               int64_t M, float *y, void *workspace, size_t workspace_bytes, void *stream) {
+    if (M <= 8) return vkq_gemv(device, qtype, w, w_bytes, K, N, x, M, y, workspace, workspace_bytes, stream);
+    int st = enter(device);
+    if (st) return st;
+    set_error("M=%lld > 8: the tensor-core path is not built in this library", (long long)M);
+    return VKQ_ERR_UNSUPPORTED;
+}
+
+int vkq_device_status(int device, int *code) {
+    int st = enter(device);
+    if (st) return st;
+    if (!code) {
+        set_error("null code pointer");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return check_launch(e, "cudaDeviceSynchronize");
+    int g = gemv_read_status();
+    if (g < 0) {
+        set_error("cannot read the device status word");
+        return VKQ_ERR_CUDA;
+    }
+    *code = g ? g : VKQ_OK;
+    return VKQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,584 @@
+// gemv.cu -- fused k-quant dequantize + GEMV on sm_100a, fp32 accumulate.
+//
+// Computes y[m][n] = sum_k x[m][k] * W[k][n] for 1 <= M <= 8, where W is a
+// Q4_K / Q5_K / Q6_K weight in vibrant's orientation: W[k][n] is value
+// k*N + n of the super-block stream (internal/gguf/loader.go:24-27,
+// internal/tensor/matmul_quant.go:87-89).  It replaces the fp32 single-row
+// kernel behind matmulGPU (internal/gpu/cuda/kernels.cu:61-77 via
+// internal/tensor/ops_cuda.go:55-63), which needed the weight expanded to
+// float32 on the host first.
+//
+// Design (HBM-bound; algorithmic bytes per call = weight bytes + x + y):
+//  * The output columns are cut into tiles of TN = 32*VPT values; a row
+//    chunk (one k, TN columns) is a contiguous run of super-blocks.  The
+//    (tile, k) space is flattened and split evenly over a grid of 2 CTAs per
+//    SM ("stream-K" over rows), so every shape fills the machine.
+//  * One producer thread per CTA streams row chunks into a shared-memory ring
+//    with cp.async.bulk (no multicast), STAGES x 8 rows deep, tracked by
+//    mbarriers; the weight prefetch starts before griddepcontrol.wait, so it
+//    overlaps the tail of the previous kernel when launched with
+//    programmatic stream serialization.
+//  * 8 consumer warps take one row each per stage; lane l decodes VPT
+//    consecutive values (a 32-value sub-block for M == 1) straight from the
+//    packed bytes: nibbles are moved into byte lanes, turned into floats with
+//    a byte permute into a 2^23 magic exponent and one packed fp32x2 add, and
+//    accumulated with packed fp32x2 FMAs.  For Q4_K/Q5_K the sub-block scale
+//    is applied as a = x*(d*sc) and the min term x*(dmin*m) is summed once per
+//    sub-block instead of per value.
+//  * Partial sums of the 8 warps are added in shared memory in a fixed order;
+//    tiles split over several CTAs go through a small partials buffer and
+//    the last CTA to arrive (an atomic counter per tile, reset after use)
+//    adds the partials in CTA order, so results are deterministic.
+#include <cstdint>
+#include <cstdio>
+
+#include "kq_device.cuh"
+#include "vkq_internal.h"
+
+namespace vkq {
+
+static __device__ int g_gemv_status;
+
+constexpr int kNW = 8;                       // consumer warps
+constexpr int kThreads = (kNW + 1) * 32;     // + one producer warp
+constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
+constexpr int kSmemPerCta = 112 * 1024;      // two CTAs per SM
+
+struct GemvParams {
+    const uint8_t *w;
+    int64_t w_bytes;    // valid bytes of w
+    int64_t w_floor16;  // bytes that bulk copies may read
+    const float *x;
+    float *y;
+    int64_t K, N;
+    int M;
+    int ntiles;
+    int grid;
+    int64_t rows_total;  // ntiles * K
+    int64_t rpc;         // rows (tile, k) per CTA
+    float *partials;     // [grid][2][MR][TN]
+    int *counters;       // [ntiles]
+    int row_cap;         // bytes per ring row slot (multiple of 16)
+    int stages;
+};
+
+__device__ __forceinline__ void set_status(int code) { atomicExch(&g_gemv_status, code); }
+__device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+
+// Float from the byte in lane j of v via the 2^23 exponent trick.
+template <int J>
+__device__ __forceinline__ float byte_as_magic(uint32_t v) {
+    return __uint_as_float(prmt(v, 0x4B000000u, 0x7540u | J));
+}
+
+template <int MR, int NP>
+__device__ __forceinline__ void accum_chunk(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
+                                            const float (&a)[MR], float magic) {
+    const uint64_t negm = pk2(-magic, -magic);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float fe, fo;
+        if (j == 0) { fe = byte_as_magic<0>(E); fo = byte_as_magic<0>(O); }
+        if (j == 1) { fe = byte_as_magic<1>(E); fo = byte_as_magic<1>(O); }
+        if (j == 2) { fe = byte_as_magic<2>(E); fo = byte_as_magic<2>(O); }
+        if (j == 3) { fe = byte_as_magic<3>(E); fo = byte_as_magic<3>(O); }
+        uint64_t q2 = fadd2(pk2(fe, fo), negm);
+#pragma unroll
+        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = ffma2(pk2(a[m], a[m]), q2, acc[m][pair0 + j]);
+    }
+}
+
+// Decode VPT values of one super-block (shared address blk, first value
+// `within`) and accumulate x[m] * W into acc; bias collects x*(dmin*m).
+template <int QT, int MR, int VPT>
+__device__ __forceinline__ void decode_accum(uint32_t blk, int within, const float (&xv)[MR],
+                                             uint64_t (&acc)[MR][VPT / 2], float (&bias)[MR]) {
+    constexpr int NCH = VPT / 8;  // chunks of 8 values
+    if constexpr (QT == kQ4K || QT == kQ5K) {
+        const uint4 hdr = lds128(blk);
+        const float d = hw_f16_to_f32(hdr.x & 0xFFFFu), dmin = hw_f16_to_f32(hdr.x >> 16);
+        const int sb = within >> 5;
+        const uint32_t sc24 = sb < 4 ? hdr.y : __funnelshift_r(hdr.y, hdr.z, 24);
+        const uint32_t m24 = sb < 4 ? __funnelshift_r(hdr.z, hdr.w, 16) : (hdr.w >> 8);
+        const uint32_t sh = 6u * (sb & 3);
+        const float ds = d * (float)((sc24 >> sh) & 63u);
+        const float dm = dmin * (float)((m24 >> sh) & 63u);
+        float a[MR];
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+            a[m] = xv[m] * ds;
+            bias[m] = fmaf(xv[m], dm, bias[m]);
+        }
+        const uint32_t qs = blk + (QT == kQ4K ? 16 : 48) + (within >> 1);
+        uint32_t wq[NCH];
+        if constexpr (NCH == 4) {
+            uint4 t = lds128(qs);
+            wq[0] = t.x; wq[1] = t.y; wq[2] = t.z; wq[3] = t.w;
+        } else if constexpr (NCH == 2) {
+            uint2 t = lds64(qs);
+            wq[0] = t.x; wq[1] = t.y;
+        } else {
+            wq[0] = lds32(qs);
+        }
+        uint32_t qh = 0;
+        if constexpr (QT == kQ5K) {
+            const uint32_t qha = blk + 16 + (within >> 3);
+            if constexpr (NCH == 4) qh = lds32(qha);
+            else if constexpr (NCH == 2) qh = lds16(qha);
+            else qh = lds16(qha & ~1u) >> (8 * (qha & 1u));
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; c++) {
+            uint32_t E = wq[c] & 0x0F0F0F0Fu;
+            uint32_t O = (wq[c] >> 4) & 0x0F0F0F0Fu;
+            if constexpr (QT == kQ5K) {
+                // bit i of hb is the fifth bit of value 8c+i; spread bits
+                // 0,2,4,6 (and 1,3,5,7) to bit 4 of byte lanes 0..3.
+                const uint32_t hb = (qh >> (8 * c)) & 0xFFu;
+                E |= ((hb & 0x55u) * 0x410410u) & 0x10101010u;
+                O |= (((hb >> 1) & 0x55u) * 0x410410u) & 0x10101010u;
+            }
+            accum_chunk<MR, VPT / 2>(acc, 4 * c, E, O, a, 8388608.0f);
+        }
+    } else {  // Q6_K: blk is only 2-byte aligned in shared memory
+        const float d = hw_f16_to_f32(lds16(blk + 208));
+        const int g0 = within >> 4;  // first 16-value scale group
+        const uint32_t sraw = lds16(blk + 192 + (g0 & ~1));
+        const int s0 = (int)(int8_t)((g0 & 1) ? (sraw >> 8) : sraw);
+        const int s1 = (int)(int8_t)(sraw >> 8);
+        float a0[MR], a1[MR];
+        const float ds0 = d * (float)s0, ds1 = d * (float)s1;
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+            a0[m] = xv[m] * ds0;
+            a1[m] = xv[m] * ds1;
+        }
+        const uint32_t ql = blk + (within >> 1);
+        const uint32_t qha = blk + 128 + (within >> 2);
+        uint32_t wq[NCH];
+        {
+            const uint32_t base = ql & ~3u, shf = (ql & 3u) * 8u;
+            uint32_t wv[NCH + 1];
+#pragma unroll
+            for (int i = 0; i <= NCH; i++) wv[i] = lds32(base + 4 * i);
+#pragma unroll
+            for (int i = 0; i < NCH; i++) wq[i] = __funnelshift_r(wv[i], wv[i + 1], shf);
+        }
+        uint32_t qh[(NCH + 1) / 2];
+        if constexpr (NCH == 4) {
+            qh[0] = lds32_a2(qha);
+            qh[1] = lds32_a2(qha + 4);
+        } else if constexpr (NCH == 2) {
+            qh[0] = lds32_a2(qha);
+        } else {
+            qh[0] = lds16(qha);
+        }
+#pragma unroll
+        for (int c = 0; c < NCH; c++) {
+            const uint32_t h16 = (qh[c >> 1] >> (16 * (c & 1))) & 0xFFFFu;
+            // byte lane j of X = nibble j of h16 = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
+            const uint32_t X = prmt(h16, h16 >> 4, 0x5140u) & 0x0F0F0F0Fu;
+            const uint32_t E = (wq[c] & 0x0F0F0F0Fu) | ((X & 0x03030303u) << 4);
+            const uint32_t O = ((wq[c] >> 4) & 0x0F0F0F0Fu) | ((X & 0x0C0C0C0Cu) << 2);
+            if (NCH == 4 && c >= 2) accum_chunk<MR, VPT / 2>(acc, 4 * c, E, O, a1, 8388640.0f);
+            else accum_chunk<MR, VPT / 2>(acc, 4 * c, E, O, a0, 8388640.0f);  // 2^23 + 32
+        }
+    }
+}
+
+template <int VPT>
+__device__ __forceinline__ int red_swz(int lane) {
+    constexpr int F = VPT / 4;  // float4 per lane
+    return (lane / (8 / F)) & (F - 1);
+}
+
+template <int QT, int MR, int VPT>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
+    constexpr int B = QT_<QT>::BYTES;
+    constexpr int TN = 32 * VPT;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = p.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+    uint64_t *empty = full + S;
+    int *flag = reinterpret_cast<int *>(empty + S);
+    const int hdr_bytes = ((16 * S + 16) + 127) & ~127;
+    uint8_t *ring = smem + hdr_bytes;
+    float *red = reinterpret_cast<float *>(ring + (size_t)S * kNW * p.row_cap);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t f0 = (int64_t)blockIdx.x * p.rpc;
+    const int64_t f1 = imin64(f0 + p.rpc, p.rows_total);
+    const int64_t nrows = f1 - f0;
+    const int64_t nst = (nrows + kNW - 1) / kNW;
+    const int64_t K = p.K, N = p.N;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(smem_u32addr(&full[s]), 1);
+            mbar_init(smem_u32addr(&empty[s]), kNW);
+        }
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    if (warp == kNW) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            const uint32_t ring_base = smem_u32addr(ring);
+            bool triggered = false;
+            int64_t tile = f0 / K, k = f0 - (f0 / K) * K;  // position of row s*kNW
+            for (int64_t s = 0; s < nst; s++) {
+                const int slot = (int)(s % S);
+                if (s >= S) {
+                    if (!mbar_wait_bounded(smem_u32addr(&empty[slot]), (uint32_t)(((s / S) - 1) & 1), kWaitNs))
+                        set_status(kStatusTimeout);
+                }
+                const int rows = (int)imin64(kNW, nrows - s * kNW);
+                uint32_t total = 0;
+                int64_t t = tile, kk = k;
+                for (int r = 0; r < rows; r++) {
+                    const int64_t n0 = t * TN, n1 = imin64(n0 + TN, N);
+                    const int64_t byte_lo = ((kk * N + n0) >> 8) * B;
+                    const int64_t byte_hi = ((kk * N + n1 + 255) >> 8) * B;
+                    const int64_t a_lo = byte_lo & ~int64_t(15);
+                    const int64_t c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
+                    const uint32_t dst = ring_base + (uint32_t)((slot * kNW + r) * p.row_cap);
+                    if (c_hi > a_lo) total += (uint32_t)(c_hi - a_lo);
+                    for (int64_t b = c_hi > a_lo ? c_hi : a_lo; b < byte_hi; b++)  // < 16 tail bytes
+                        ring[(slot * kNW + r) * p.row_cap + (b - a_lo)] = p.w[b];
+                    (void)dst;
+                    if (++kk == K) { kk = 0; t++; }
+                }
+                mbar_arrive_expect_tx(smem_u32addr(&full[slot]), total);
+                t = tile; kk = k;
+                for (int r = 0; r < rows; r++) {
+                    const int64_t n0 = t * TN, n1 = imin64(n0 + TN, N);
+                    const int64_t byte_lo = ((kk * N + n0) >> 8) * B;
+                    const int64_t byte_hi = ((kk * N + n1 + 255) >> 8) * B;
+                    const int64_t a_lo = byte_lo & ~int64_t(15);
+                    const int64_t c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
+                    if (c_hi > a_lo)
+                        bulk_g2s(ring_base + (uint32_t)((slot * kNW + r) * p.row_cap), p.w + a_lo,
+                                 (uint32_t)(c_hi - a_lo), smem_u32addr(&full[slot]));
+                    if (++kk == K) { kk = 0; t++; }
+                }
+                tile = t; k = kk;
+                if (!triggered && (s == S - 1 || s == nst - 1)) {
+                    pdl_launch_dependents();
+                    triggered = true;
+                }
+            }
+            if (!triggered) pdl_launch_dependents();
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    const uint32_t ring_base = smem_u32addr(ring);
+    const uint32_t red_base = smem_u32addr(red);
+    const int tid = threadIdx.x;  // 0..255
+    uint64_t acc[MR][VPT / 2];
+    float bias[MR];
+#pragma unroll
+    for (int m = 0; m < MR; m++) {
+        bias[m] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT / 2; i++) acc[m][i] = 0ull;
+    }
+    pdl_wait();  // x, y and the workspace may belong to the preceding kernel
+
+    const int64_t first_tile = f0 / K;
+    const int64_t last_tile = (f1 - 1) / K;
+    int64_t cur_tile = first_tile;
+    int64_t next_boundary = (cur_tile + 1) * K - f0;
+
+    // this warp's row position, tracked incrementally
+    int64_t my_t, my_k;
+    {
+        const int64_t f = f0 + warp;
+        my_t = f / K;
+        my_k = f - my_t * K;
+    }
+
+    auto flush = [&](int64_t tile) {
+        // 1. per-warp partials into shared memory (swizzled float4 slots)
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+#pragma unroll
+            for (int i = 0; i < VPT / 4; i++) {
+                float v0, v1, v2, v3;
+                upk2(acc[m][2 * i], v0, v1);
+                upk2(acc[m][2 * i + 1], v2, v3);
+                if (QT != kQ6K) { v0 -= bias[m]; v1 -= bias[m]; v2 -= bias[m]; v3 -= bias[m]; }
+                const int phys = lane * VPT + 4 * (i ^ red_swz<VPT>(lane));
+                const uint32_t addr = red_base + (uint32_t)(((warp * MR + m) * TN + phys) * 4);
+                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v0), "f"(v1), "f"(v2),
+                             "f"(v3));
+                acc[m][2 * i] = 0ull;
+                acc[m][2 * i + 1] = 0ull;
+            }
+            bias[m] = 0.0f;
+        }
+        named_bar_sync(1, kNW * 32);
+        // 2. fixed-order sum over the warps
+        const int64_t n0 = tile * TN;
+        const int ncols = (int)imin64(TN, N - n0);
+        const bool whole = (tile * K >= f0) && ((tile + 1) * K <= f1);
+        const int slot = (tile == first_tile) ? 0 : 1;
+        for (int idx = tid; idx < MR * TN; idx += kNW * 32) {
+            const int m = idx / TN, c = idx % TN;
+            if (m >= p.M || c >= ncols) continue;
+            const int L = c / VPT, i = (c % VPT) / 4;
+            const int phys = L * VPT + 4 * (i ^ red_swz<VPT>(L)) + (c & 3);
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kNW; w++) s += red[(w * MR + m) * TN + phys];
+            if (whole) p.y[(int64_t)m * N + n0 + c] = s;
+            else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = s;
+        }
+        named_bar_sync(1, kNW * 32);
+        if (!whole) {
+            __threadfence();
+            named_bar_sync(1, kNW * 32);
+            const int64_t cf = (tile * K) / p.rpc;
+            const int64_t cl = imin64(((tile + 1) * K - 1) / p.rpc, p.grid - 1);
+            if (tid == 0) {
+                const int old = atomicAdd(&p.counters[tile], 1);
+                flag[0] = (old == (int)(cl - cf));
+            }
+            named_bar_sync(1, kNW * 32);
+            if (flag[0]) {
+                __threadfence();
+                for (int idx = tid; idx < MR * TN; idx += kNW * 32) {
+                    const int m = idx / TN, c = idx % TN;
+                    if (m >= p.M || c >= ncols) continue;
+                    float s = 0.0f;
+                    for (int64_t cta = cf; cta <= cl; cta++) {
+                        const int sl = ((cta * p.rpc) / K == tile) ? 0 : 1;
+                        s += __ldcg(&p.partials[((cta * 2 + sl) * MR + m) * TN + c]);
+                    }
+                    p.y[(int64_t)m * N + n0 + c] = s;
+                }
+                if (tid == 0) atomicExch(&p.counters[tile], 0);
+            }
+            named_bar_sync(1, kNW * 32);
+        }
+    };
+
+    for (int64_t s = 0; s < nst; s++) {
+        const int slot = (int)(s % S);
+        if (!mbar_wait_bounded(smem_u32addr(&full[slot]), (uint32_t)((s / S) & 1), kWaitNs))
+            set_status(kStatusTimeout);
+        const int64_t pl = s * kNW + warp;
+        if (pl < nrows) {
+            while (pl >= next_boundary) {
+                flush(cur_tile);
+                cur_tile++;
+                next_boundary += K;
+            }
+            const int64_t n0 = my_t * TN;
+            const int64_t nl = n0 + lane * VPT;
+            if (nl < N && lane * VPT < TN) {
+                const int64_t v0 = my_k * N + n0;
+                const int64_t a_lo = ((v0 >> 8) * B) & ~int64_t(15);
+                const int64_t v = v0 + lane * VPT;
+                const uint32_t blk = ring_base + (uint32_t)((slot * kNW + warp) * p.row_cap) +
+                                     (uint32_t)((v >> 8) * B - a_lo);
+                float xv[MR];
+#pragma unroll
+                for (int m = 0; m < MR; m++) xv[m] = (m < p.M) ? __ldg(p.x + (int64_t)m * K + my_k) : 0.0f;
+                decode_accum<QT, MR, VPT>(blk, (int)(v & 255), xv, acc, bias);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32addr(&empty[slot]));
+        my_k += kNW;
+        while (my_k >= K) {
+            my_k -= K;
+            my_t++;
+        }
+    }
+    while (cur_tile <= last_tile) {
+        flush(cur_tile);
+        cur_tile++;
+    }
+}
+
+// -------- generic path (N % 32 != 0): one thread per output column ---------
+template <int QT>
+__device__ __forceinline__ float value_at(const uint8_t *blk, int i) {
+    if constexpr (QT == kQ6K) {
+        uint32_t lo = blk[i >> 1];
+        lo = (i & 1) ? (lo >> 4) : (lo & 0x0Fu);
+        uint32_t hi = (blk[128 + (i >> 2)] >> ((i & 3) * 2)) & 3u;
+        float d = hw_f16_to_f32(blk[208] | (uint32_t)blk[209] << 8);
+        return d * (float)(int8_t)blk[192 + (i >> 4)] * (float)((int)(lo | hi << 4) - 32);
+    } else {
+        float d = hw_f16_to_f32(blk[0] | (uint32_t)blk[1] << 8);
+        float dmin = hw_f16_to_f32(blk[2] | (uint32_t)blk[3] << 8);
+        const int sb = i >> 5, g = sb >> 2, sh = 6 * (sb & 3);
+        const uint8_t *s = blk + 4;
+        uint32_t a = s[3 * g] | (uint32_t)s[3 * g + 1] << 8 | (uint32_t)s[3 * g + 2] << 16;
+        uint32_t b = s[6 + 3 * g] | (uint32_t)s[7 + 3 * g] << 8 | (uint32_t)s[8 + 3 * g] << 16;
+        const uint8_t *qs = blk + (QT == kQ4K ? 16 : 48);
+        uint32_t q = qs[i >> 1];
+        q = (i & 1) ? (q >> 4) : (q & 0x0Fu);
+        if constexpr (QT == kQ5K) q |= ((blk[16 + (i >> 3)] >> (i & 7)) & 1u) << 4;
+        return d * (float)((a >> sh) & 63u) * (float)q - dmin * (float)((b >> sh) & 63u);
+    }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(128) gemv_generic_kernel(const uint8_t *__restrict__ w, const float *__restrict__ x,
+                                                           float *__restrict__ y, int64_t K, int64_t N, int M) {
+    constexpr int B = QT_<QT>::BYTES;
+    pdl_wait();
+    const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= N) return;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t k = 0; k < K; k++) {
+        const int64_t v = k * N + n;
+        const float wv = value_at<QT>(w + (v >> 8) * B, (int)(v & 255));
+#pragma unroll
+        for (int m = 0; m < 8; m++)
+            if (m < M) acc[m] = fmaf(__ldg(x + (int64_t)m * K + k), wv, acc[m]);
+    }
+    for (int m = 0; m < M; m++) y[(int64_t)m * N + n] = acc[m];
+}
+
+// ------------------------------- host side -------------------------------
+struct Plan {
+    int mr, vpt, tn;
+    int ntiles, grid, stages, row_cap;
+    int64_t rpc;
+    size_t smem;
+    size_t partial_bytes, counter_bytes;
+    bool generic;
+};
+
+static int block_bytes(int qt) { return qt == kQ4K ? 144 : qt == kQ5K ? 176 : 210; }
+
+static Plan make_plan(const GemvShape &s, int device) {
+    Plan pl{};
+    pl.generic = (s.N % 32) != 0;
+    if (pl.generic) return pl;
+    if (s.M <= 1) { pl.mr = 1; pl.vpt = 32; }
+    else if (s.M <= 2) { pl.mr = 2; pl.vpt = 16; }
+    else if (s.M <= 4) { pl.mr = 4; pl.vpt = 8; }
+    else { pl.mr = 8; pl.vpt = 8; }
+    pl.tn = 32 * pl.vpt;
+    pl.ntiles = (int)((s.N + pl.tn - 1) / pl.tn);
+    const int64_t rows_total = (int64_t)pl.ntiles * s.K;
+    const int sms = device_sm_count(device);
+    int64_t grid = (int64_t)sms * 2;
+    if (grid > rows_total) grid = rows_total;
+    pl.rpc = (rows_total + grid - 1) / grid;
+    pl.grid = (int)((rows_total + pl.rpc - 1) / pl.rpc);
+    const int B = block_bytes(s.qtype);
+    pl.row_cap = (((pl.tn / 256 + 1) * B + 16 + 16) + 15) & ~15;
+    const size_t red = (size_t)kNW * pl.mr * pl.tn * 4;
+    int stages = 8;
+    auto smem_for = [&](int st) { return (size_t)(((16 * st + 16) + 127) & ~127) + (size_t)st * kNW * pl.row_cap + red; };
+    while (stages > 2 && smem_for(stages) > (size_t)kSmemPerCta) stages--;
+    pl.stages = stages;
+    pl.smem = smem_for(stages);
+    pl.partial_bytes = ((size_t)pl.grid * 2 * pl.mr * pl.tn * 4 + 255) & ~size_t(255);
+    pl.counter_bytes = ((size_t)pl.ntiles * 4 + 255) & ~size_t(255);
+    return pl;
+}
+
+size_t gemv_workspace_bytes(const GemvShape &s, int device) {
+    Plan pl = make_plan(s, device);
+    if (pl.generic) return 0;
+    return pl.counter_bytes + pl.partial_bytes;
+}
+
+template <int QT, int MR, int VPT>
+static cudaError_t launch_fast(const GemvParams &gp, const Plan &pl, cudaStream_t stream) {
+    auto kern = gemv_kernel<QT, MR, VPT>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(pl.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, gp);
+}
+
+template <int QT>
+static cudaError_t dispatch_mr(const GemvParams &gp, const Plan &pl, cudaStream_t st) {
+    switch (pl.mr) {
+    case 1: return launch_fast<QT, 1, 32>(gp, pl, st);
+    case 2: return launch_fast<QT, 2, 16>(gp, pl, st);
+    case 4: return launch_fast<QT, 4, 8>(gp, pl, st);
+    default: return launch_fast<QT, 8, 8>(gp, pl, st);
+    }
+}
+
+int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
+                size_t ws_bytes, cudaStream_t stream, int device) {
+    Plan pl = make_plan(s, device);
+    cudaError_t e;
+    if (pl.generic) {
+        const uint8_t *wp = static_cast<const uint8_t *>(w);
+        dim3 grid((unsigned)((s.N + 127) / 128));
+        switch (s.qtype) {
+        case kQ4K: gemv_generic_kernel<kQ4K><<<grid, 128, 0, stream>>>(wp, x, y, s.K, s.N, (int)s.M); break;
+        case kQ5K: gemv_generic_kernel<kQ5K><<<grid, 128, 0, stream>>>(wp, x, y, s.K, s.N, (int)s.M); break;
+        default: gemv_generic_kernel<kQ6K><<<grid, 128, 0, stream>>>(wp, x, y, s.K, s.N, (int)s.M); break;
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            set_error("gemv (generic) launch failed: %s", cudaGetErrorString(e));
+            return 5;
+        }
+        return 0;
+    }
+    const size_t need = pl.counter_bytes + pl.partial_bytes;
+    if (ws == nullptr || ws_bytes < need) {
+        set_error("gemv needs a workspace of %zu bytes (got %zu)", need, ws_bytes);
+        return 4;
+    }
+    GemvParams gp{};
+    gp.w = static_cast<const uint8_t *>(w);
+    gp.w_bytes = w_bytes;
+    gp.w_floor16 = w_bytes & ~int64_t(15);
+    gp.x = x;
+    gp.y = y;
+    gp.K = s.K;
+    gp.N = s.N;
+    gp.M = (int)s.M;
+    gp.ntiles = pl.ntiles;
+    gp.grid = pl.grid;
+    gp.rows_total = (int64_t)pl.ntiles * s.K;
+    gp.rpc = pl.rpc;
+    gp.counters = static_cast<int *>(ws);
+    gp.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + pl.counter_bytes);
+    gp.row_cap = pl.row_cap;
+    gp.stages = pl.stages;
+    switch (s.qtype) {
+    case kQ4K: e = dispatch_mr<kQ4K>(gp, pl, stream); break;
+    case kQ5K: e = dispatch_mr<kQ5K>(gp, pl, stream); break;
+    default: e = dispatch_mr<kQ6K>(gp, pl, stream); break;
+    }
+    if (e != cudaSuccess) {
+        set_error("gemv launch failed: %s", cudaGetErrorString(e));
+        return 5;
+    }
+    return 0;
+}
+
+int gemv_read_status() {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gemv_status, sizeof(int)) != cudaSuccess) return -1;
+    cudaMemcpyToSymbol(g_gemv_status, &zero, sizeof(int));
+    return v;
+}
+
+}  // namespace vkq

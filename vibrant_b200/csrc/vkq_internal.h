@@ -1,0 +1,31 @@
+// vkq_internal.h -- host-side declarations shared by the translation units of
+// libvkq.so (not part of the public ABI; see include/vkq.h for that).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace vkq {
+
+int device_sm_count(int device);
+
+cudaError_t dequantize_f32(int qtype, const void *w, int64_t nblocks, float *out, cudaStream_t s, int device);
+cudaError_t dequant_transpose_f32(int qtype, const void *w, int64_t K, int64_t N, float *out, cudaStream_t s,
+                                  int device);
+
+// fp32 CUDA-core GEMV (1 <= M <= 8).
+struct GemvShape {
+    int qtype;
+    int64_t K, N, M;
+};
+// Workspace bytes the GEMV plan needs (0 when it needs none).
+size_t gemv_workspace_bytes(const GemvShape &s, int device);
+// Returns a vkq_status code; on failure writes a message with set_error.
+int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
+                size_t ws_bytes, cudaStream_t stream, int device);
+int gemv_read_status();  // reads and clears this TU's device status word (synchronous)
+
+void set_error(const char *fmt, ...);
+
+}  // namespace vkq

@@ -1,0 +1,120 @@
+"""ctypes binding of libvkq.so (include/vkq.h).
+
+This is how the tests and bench.py reach the kernels: through the same C ABI a
+Go cgo shim would bind.  Loading fails loudly when the library is missing;
+there is no CPU fallback anywhere in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "_lib", "libvkq.so")
+
+Q4_K, Q5_K, Q6_K = 12, 13, 14
+BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
+QTYPE_NAMES = {Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+
+OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_MISALIGNED, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE_TIMEOUT, \
+    ERR_NCCL = range(8)
+
+# every symbol declared in include/vkq.h, with (restype, argtypes)
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_sz = ctypes.c_size_t
+SIGNATURES = {
+    "vkq_abi_version": (_int, []),
+    "vkq_status_string": (ctypes.c_char_p, [_int]),
+    "vkq_last_error": (ctypes.c_char_p, []),
+    "vkq_block_bytes": (_i64, [_int]),
+    "vkq_weight_bytes": (_int, [_int, _i64, _i64, ctypes.POINTER(_i64)]),
+    "vkq_dequantize_f32": (_int, [_int, _int, _vp, _i64, _vp, _vp]),
+    "vkq_dequant_transpose_f32": (_int, [_int, _int, _vp, _i64, _i64, _vp, _vp]),
+    "vkq_matmul_workspace_bytes": (_int, [_int, _int, _i64, _i64, _i64, ctypes.POINTER(_sz)]),
+    "vkq_matmul": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "vkq_gemv": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "vkq_device_status": (_int, [_int, ctypes.POINTER(_int)]),
+}
+
+
+class VkqError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"vkq status {status}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libvkq.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} is missing: build it with `python -m vibrant_b200.build` "
+                               "(there is no CPU fallback)")
+        L = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        raise VkqError(status, load().vkq_last_error().decode(errors="replace"))
+
+
+def last_error() -> str:
+    return load().vkq_last_error().decode(errors="replace")
+
+
+def weight_bytes(qtype: int, K: int, N: int) -> int:
+    out = _i64()
+    _check(load().vkq_weight_bytes(qtype, K, N, ctypes.byref(out)))
+    return out.value
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream  # torch.cuda.Stream
+
+
+def dequantize_f32(qtype: int, w_ptr: int, nblocks: int, out_ptr: int, device: int = -1, stream=None) -> None:
+    _check(load().vkq_dequantize_f32(device, qtype, w_ptr, nblocks, out_ptr, _stream_ptr(stream)))
+
+
+def dequant_transpose_f32(qtype: int, w_ptr: int, K: int, N: int, out_ptr: int, device: int = -1,
+                          stream=None) -> None:
+    _check(load().vkq_dequant_transpose_f32(device, qtype, w_ptr, K, N, out_ptr, _stream_ptr(stream)))
+
+
+def matmul_workspace_bytes(qtype: int, M: int, K: int, N: int, device: int = -1) -> int:
+    out = _sz()
+    _check(load().vkq_matmul_workspace_bytes(device, qtype, M, K, N, ctypes.byref(out)))
+    return out.value
+
+
+def matmul(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: int, y_ptr: int,
+           ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
+    _check(load().vkq_matmul(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, ws_ptr, ws_bytes,
+                             _stream_ptr(stream)))
+
+
+def gemv(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: int, y_ptr: int,
+         ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
+    _check(load().vkq_gemv(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, ws_ptr, ws_bytes,
+                           _stream_ptr(stream)))
+
+
+def device_status(device: int = -1) -> int:
+    code = _int()
+    _check(load().vkq_device_status(device, ctypes.byref(code)))
+    return code.value
