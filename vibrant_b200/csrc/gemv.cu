@@ -22,9 +22,10 @@
 //    consecutive values (a 32-value sub-block for M == 1) straight from the
 //    packed bytes: nibbles are moved into byte lanes, turned into floats with
 //    a byte permute into a 2^23 magic exponent and one packed fp32x2 add, and
-//    accumulated with packed fp32x2 FMAs.  For Q4_K/Q5_K the sub-block scale
-//    is applied as a = x*(d*sc) and the min term x*(dmin*m) is summed once per
-//    sub-block instead of per value.
+//    accumulated with packed fp32x2 FMAs.  Q4_K/Q5_K values are formed as
+//    w = (d*sc)*q - dmin*m before the product with x (keeps the error
+//    relative to |x*w| where the two terms cancel); Q6_K applies
+//    a = x*(d*scale) to q - 32.
 //  * Partial sums of the 8 warps are added in shared memory in a fixed order;
 //    tiles split over several CTAs go through a small partials buffer and
 //    the last CTA to arrive (an atomic counter per tile, reset after use)
@@ -71,9 +72,10 @@ __device__ __forceinline__ float byte_as_magic(uint32_t v) {
     return __uint_as_float(prmt(v, 0x4B000000u, 0x7540u | J));
 }
 
+// Q6_K: acc[m] += a[m] * (q - 32) with a = x * (d * scale).
 template <int MR, int NP>
-__device__ __forceinline__ void accum_chunk(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
-                                            const float (&a)[MR], float magic) {
+__device__ __forceinline__ void accum_chunk_scaled(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
+                                                   const float (&a)[MR], float magic) {
     const uint64_t negm = pk2(-magic, -magic);
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -82,17 +84,40 @@ __device__ __forceinline__ void accum_chunk(uint64_t (&acc)[MR][NP], int pair0, 
         if (j == 1) { fe = byte_as_magic<1>(E); fo = byte_as_magic<1>(O); }
         if (j == 2) { fe = byte_as_magic<2>(E); fo = byte_as_magic<2>(O); }
         if (j == 3) { fe = byte_as_magic<3>(E); fo = byte_as_magic<3>(O); }
-        uint64_t q2 = fadd2(pk2(fe, fo), negm);
+        const uint64_t q2 = fadd2(pk2(fe, fo), negm);
 #pragma unroll
         for (int m = 0; m < MR; m++) acc[m][pair0 + j] = ffma2(pk2(a[m], a[m]), q2, acc[m][pair0 + j]);
     }
 }
 
+// Q4_K / Q5_K: w = scale * q - min formed per value (one rounding, as close
+// to the reference's two roundings as one fma gets), then acc[m] += x[m] * w.
+// Forming w first keeps the error relative to |x*w| even where scale*q and
+// min nearly cancel.
+template <int MR, int NP>
+__device__ __forceinline__ void accum_chunk_affine(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
+                                                   float scale, float mn, const float (&xv)[MR]) {
+    const uint64_t negm = pk2(-8388608.0f, -8388608.0f);
+    const uint64_t s2 = pk2(scale, scale), nm2 = pk2(-mn, -mn);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float fe, fo;
+        if (j == 0) { fe = byte_as_magic<0>(E); fo = byte_as_magic<0>(O); }
+        if (j == 1) { fe = byte_as_magic<1>(E); fo = byte_as_magic<1>(O); }
+        if (j == 2) { fe = byte_as_magic<2>(E); fo = byte_as_magic<2>(O); }
+        if (j == 3) { fe = byte_as_magic<3>(E); fo = byte_as_magic<3>(O); }
+        const uint64_t q2 = fadd2(pk2(fe, fo), negm);
+        const uint64_t w2 = ffma2(s2, q2, nm2);
+#pragma unroll
+        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = ffma2(pk2(xv[m], xv[m]), w2, acc[m][pair0 + j]);
+    }
+}
+
 // Decode VPT values of one super-block (shared address blk, first value
-// `within`) and accumulate x[m] * W into acc; bias collects x*(dmin*m).
+// `within`) and accumulate x[m] * W into acc.
 template <int QT, int MR, int VPT>
 __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const float (&xv)[MR],
-                                             uint64_t (&acc)[MR][VPT / 2], float (&bias)[MR]) {
+                                             uint64_t (&acc)[MR][VPT / 2]) {
     constexpr int NCH = VPT / 8;  // chunks of 8 values
     if constexpr (QT == kQ4K || QT == kQ5K) {
         const uint4 hdr = lds128(blk);
@@ -103,12 +128,6 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
         const uint32_t sh = 6u * (sb & 3);
         const float ds = d * (float)((sc24 >> sh) & 63u);
         const float dm = dmin * (float)((m24 >> sh) & 63u);
-        float a[MR];
-#pragma unroll
-        for (int m = 0; m < MR; m++) {
-            a[m] = xv[m] * ds;
-            bias[m] = fmaf(xv[m], dm, bias[m]);
-        }
         const uint32_t qs = blk + (QT == kQ4K ? 16 : 48) + (within >> 1);
         uint32_t wq[NCH];
         if constexpr (NCH == 4) {
@@ -138,7 +157,7 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
                 E |= ((hb & 0x55u) * 0x410410u) & 0x10101010u;
                 O |= (((hb >> 1) & 0x55u) * 0x410410u) & 0x10101010u;
             }
-            accum_chunk<MR, VPT / 2>(acc, 4 * c, E, O, a, 8388608.0f);
+            accum_chunk_affine<MR, VPT / 2>(acc, 4 * c, E, O, ds, dm, xv);
         }
     } else {  // Q6_K: blk is only 2-byte aligned in shared memory
         const float d = hw_f16_to_f32(lds16(blk + 208));
@@ -180,8 +199,8 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
             const uint32_t X = prmt(h16, h16 >> 4, 0x5140u) & 0x0F0F0F0Fu;
             const uint32_t E = (wq[c] & 0x0F0F0F0Fu) | ((X & 0x03030303u) << 4);
             const uint32_t O = ((wq[c] >> 4) & 0x0F0F0F0Fu) | ((X & 0x0C0C0C0Cu) << 2);
-            if (NCH == 4 && c >= 2) accum_chunk<MR, VPT / 2>(acc, 4 * c, E, O, a1, 8388640.0f);
-            else accum_chunk<MR, VPT / 2>(acc, 4 * c, E, O, a0, 8388640.0f);  // 2^23 + 32
+            if (NCH == 4 && c >= 2) accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a1, 8388640.0f);
+            else accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a0, 8388640.0f);  // 2^23 + 32
         }
     }
 }
@@ -278,10 +297,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     const uint32_t red_base = smem_u32addr(red);
     const int tid = threadIdx.x;  // 0..255
     uint64_t acc[MR][VPT / 2];
-    float bias[MR];
 #pragma unroll
     for (int m = 0; m < MR; m++) {
-        bias[m] = 0.0f;
 #pragma unroll
         for (int i = 0; i < VPT / 2; i++) acc[m][i] = 0ull;
     }
@@ -309,7 +326,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 float v0, v1, v2, v3;
                 upk2(acc[m][2 * i], v0, v1);
                 upk2(acc[m][2 * i + 1], v2, v3);
-                if (QT != kQ6K) { v0 -= bias[m]; v1 -= bias[m]; v2 -= bias[m]; v3 -= bias[m]; }
                 const int phys = lane * VPT + 4 * (i ^ red_swz<VPT>(lane));
                 const uint32_t addr = red_base + (uint32_t)(((warp * MR + m) * TN + phys) * 4);
                 asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v0), "f"(v1), "f"(v2),
@@ -317,7 +333,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 acc[m][2 * i] = 0ull;
                 acc[m][2 * i + 1] = 0ull;
             }
-            bias[m] = 0.0f;
         }
         named_bar_sync(1, kNW * 32);
         // 2. fixed-order sum over the warps
@@ -387,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 float xv[MR];
 #pragma unroll
                 for (int m = 0; m < MR; m++) xv[m] = (m < p.M) ? __ldg(p.x + (int64_t)m * K + my_k) : 0.0f;
-                decode_accum<QT, MR, VPT>(blk, (int)(v & 255), xv, acc, bias);
+                decode_accum<QT, MR, VPT>(blk, (int)(v & 255), xv, acc);
             }
         }
         __syncwarp();
