@@ -210,12 +210,13 @@ def time_gemv_graph(torch, vt, weights, x, outs, steps, warmup, stream):
         for i in range(steps):
             vt.matmul(x, weights[i % len(weights)], out=outs[i % len(outs)], stream=stream)
     torch.cuda.synchronize()
-    g.replay()  # untimed replay
-    torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    g.replay()
-    ev1.record(stream)
+    with torch.cuda.stream(stream):   # CUDAGraph.replay launches on the current stream
+        g.replay()  # untimed replay
+        stream.synchronize()
+        ev0.record(stream)
+        g.replay()
+        ev1.record(stream)
     torch.cuda.synchronize()
     return ev0.elapsed_time(ev1) / 1e3 / steps, g
 
@@ -292,17 +293,18 @@ def run_ours(args):
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     sampler.start()
-    t_soak = time.time()
-    while time.time() - t_soak < 1.0:   # bring clocks to their loaded state
-        g.replay()
-        torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if pg is not None:
-        pg.barrier()
-    torch.cuda.synchronize()
-    ev0.record(stream)
-    g.replay()
-    ev1.record(stream)
+    with torch.cuda.stream(stream):   # CUDAGraph.replay launches on the current stream
+        t_soak = time.time()
+        while time.time() - t_soak < 1.0:   # bring clocks to their loaded state
+            g.replay()
+            stream.synchronize()
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        g.replay()
+        ev1.record(stream)
     torch.cuda.synchronize()
     if pg is not None:
         pg.barrier()

@@ -186,7 +186,7 @@ def test_error_paths(tvk):
     buf = torch.zeros(vkq.weight_bytes(12, K, N) + 32, dtype=torch.uint8, device="cuda")
     x = torch.zeros(1, K, device="cuda")
     y = torch.zeros(1, N, device="cuda")
-    ws = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(vkq.matmul_workspace_bytes(12, 1, K, N, device=0), dtype=torch.uint8, device="cuda")
     args = dict(device=0, stream=torch.cuda.current_stream())
 
     def call(**kw):
@@ -209,6 +209,9 @@ def test_error_paths(tvk):
     assert e.value.status == vkq.ERR_MISALIGNED
     with pytest.raises(vkq.VkqError) as e:
         call(ws=None, wsb=0)
+    assert e.value.status == vkq.ERR_WORKSPACE
+    with pytest.raises(vkq.VkqError) as e:
+        call(wsb=ws.numel() - 256)
     assert e.value.status == vkq.ERR_WORKSPACE
     with pytest.raises(vkq.VkqError) as e:
         call(x=0)

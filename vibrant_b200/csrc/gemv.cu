@@ -13,7 +13,7 @@
 //    chunk (one k, TN columns) is a contiguous run of super-blocks.  The
 //    (tile, k) space is flattened and split evenly over a grid of 2 CTAs per
 //    SM ("stream-K" over rows), so every shape fills the machine.
-//  * One producer thread per CTA streams row chunks into a shared-memory ring
+//  * One producer warp per CTA streams row chunks into a shared-memory ring
 //    with cp.async.bulk (no multicast), STAGES x 8 rows deep, tracked by
 //    mbarriers; the weight prefetch starts before griddepcontrol.wait, so it
 //    overlaps the tail of the previous kernel when launched with
@@ -41,6 +41,8 @@ namespace vkq {
 static __device__ int g_gemv_status;
 
 constexpr int kNW = 8;                       // consumer warps
+constexpr int kRPW = 1;                      // rows per consumer warp per stage
+constexpr int kRPS = kRPW * kNW;             // rows per ring stage
 constexpr int kThreads = (kNW + 1) * 32;     // + one producer warp
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
 constexpr int kSmemPerCta = 112 * 1024;      // two CTAs per SM
@@ -222,13 +224,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     int *flag = reinterpret_cast<int *>(empty + S);
     const int hdr_bytes = ((16 * S + 16) + 127) & ~127;
     uint8_t *ring = smem + hdr_bytes;
-    float *red = reinterpret_cast<float *>(ring + (size_t)S * kNW * p.row_cap);
+    float *red = reinterpret_cast<float *>(ring + (size_t)S * kRPS * p.row_cap);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t f0 = (int64_t)blockIdx.x * p.rpc;
     const int64_t f1 = imin64(f0 + p.rpc, p.rows_total);
     const int64_t nrows = f1 - f0;
-    const int64_t nst = (nrows + kNW - 1) / kNW;
+    const int64_t nst = (nrows + kRPS - 1) / kRPS;
     const int64_t K = p.K, N = p.N;
 
     if (threadIdx.x == 0) {
@@ -242,57 +244,72 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
 
     if (warp == kNW) {
         // ------------------------------ producer ------------------------------
-        if (lane == 0) {
-            const uint32_t ring_base = smem_u32addr(ring);
-            bool triggered = false;
-            int64_t tile = f0 / K, k = f0 - (f0 / K) * K;  // position of row s*kNW
-            for (int64_t s = 0; s < nst; s++) {
-                const int slot = (int)(s % S);
-                if (s >= S) {
-                    if (!mbar_wait_bounded(smem_u32addr(&empty[slot]), (uint32_t)(((s / S) - 1) & 1), kWaitNs))
-                        set_status(kStatusTimeout);
-                }
-                const int rows = (int)imin64(kNW, nrows - s * kNW);
-                uint32_t total = 0;
-                int64_t t = tile, kk = k;
-                for (int r = 0; r < rows; r++) {
-                    const int64_t n0 = t * TN, n1 = imin64(n0 + TN, N);
-                    const int64_t byte_lo = ((kk * N + n0) >> 8) * B;
-                    const int64_t byte_hi = ((kk * N + n1 + 255) >> 8) * B;
-                    const int64_t a_lo = byte_lo & ~int64_t(15);
-                    const int64_t c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
-                    const uint32_t dst = ring_base + (uint32_t)((slot * kNW + r) * p.row_cap);
-                    if (c_hi > a_lo) total += (uint32_t)(c_hi - a_lo);
-                    for (int64_t b = c_hi > a_lo ? c_hi : a_lo; b < byte_hi; b++)  // < 16 tail bytes
-                        ring[(slot * kNW + r) * p.row_cap + (b - a_lo)] = p.w[b];
-                    (void)dst;
-                    if (++kk == K) { kk = 0; t++; }
-                }
-                mbar_arrive_expect_tx(smem_u32addr(&full[slot]), total);
-                t = tile; kk = k;
-                for (int r = 0; r < rows; r++) {
-                    const int64_t n0 = t * TN, n1 = imin64(n0 + TN, N);
-                    const int64_t byte_lo = ((kk * N + n0) >> 8) * B;
-                    const int64_t byte_hi = ((kk * N + n1 + 255) >> 8) * B;
-                    const int64_t a_lo = byte_lo & ~int64_t(15);
-                    const int64_t c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
-                    if (c_hi > a_lo)
-                        bulk_g2s(ring_base + (uint32_t)((slot * kNW + r) * p.row_cap), p.w + a_lo,
-                                 (uint32_t)(c_hi - a_lo), smem_u32addr(&full[slot]));
-                    if (++kk == K) { kk = 0; t++; }
-                }
-                tile = t; k = kk;
-                if (!triggered && (s == S - 1 || s == nst - 1)) {
-                    pdl_launch_dependents();
-                    triggered = true;
-                }
-            }
-            if (!triggered) pdl_launch_dependents();
+        // The 32 lanes prepare 32 / kRPS stages of kRPS rows at once: lane l
+        // owns row (l % kRPS) of stage (batch + l / kRPS).  Each stage's byte
+        // count is summed over its lanes, the stage leader posts expect_tx,
+        // then every lane issues its own bulk copy.
+        constexpr int kSPB = 32 / kRPS;  // stages per producer batch
+        const uint32_t ring_base = smem_u32addr(ring);
+        const int r = lane % kRPS, sub = lane / kRPS;
+        const uint32_t Ku = (uint32_t)K;
+        uint32_t t, kk;  // (tile, k) of this lane's row in the current batch
+        {
+            const int64_t f = f0 + lane;
+            t = (uint32_t)(f / K);
+            kk = (uint32_t)(f - (int64_t)t * K);
         }
+        const int nst32 = (int)nst, nrows32 = (int)nrows;
+        int st = sub, slot = sub;  // this lane's stage and its ring slot (S >= kSPB)
+        uint32_t round = 0;        // st / S
+        for (int sb = 0; sb < nst32; sb += kSPB) {
+            const bool stage_ok = st < nst32;
+            if (stage_ok && round > 0) {
+                if (!mbar_wait_bounded(smem_u32addr(&empty[slot]), (round - 1) & 1u, kWaitNs))
+                    set_status(kStatusTimeout);
+            }
+            const bool row_ok = stage_ok && (st * kRPS + r) < nrows32;
+            int64_t a_lo = 0, c_hi = 0, byte_hi = 0;
+            if (row_ok) {
+                const int64_t n0 = (int64_t)t * TN, n1 = imin64(n0 + TN, N);
+                const int64_t base = (int64_t)kk * N;
+                a_lo = (((base + n0) >> 8) * B) & ~int64_t(15);
+                byte_hi = ((base + n1 + 255) >> 8) * B;
+                c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
+                if (c_hi < a_lo) c_hi = a_lo;
+                for (int64_t bb = c_hi; bb < byte_hi; bb++)  // < 16 tail bytes at the very end of w
+                    ring[(slot * kRPS + r) * p.row_cap + (bb - a_lo)] = p.w[bb];
+            }
+            const uint32_t bytes = (uint32_t)(c_hi - a_lo);
+            uint32_t total = bytes;
+            total += __shfl_xor_sync(0xffffffffu, total, 1);
+            total += __shfl_xor_sync(0xffffffffu, total, 2);
+            total += __shfl_xor_sync(0xffffffffu, total, 4);
+            if (kRPS > 8) total += __shfl_xor_sync(0xffffffffu, total, 8);
+            __syncwarp();
+            if (stage_ok && r == 0) mbar_arrive_expect_tx(smem_u32addr(&full[slot]), total);
+            __syncwarp();
+            if (row_ok && bytes > 0)
+                bulk_g2s(ring_base + (uint32_t)((slot * kRPS + r) * p.row_cap), p.w + a_lo, bytes,
+                         smem_u32addr(&full[slot]));
+            if (sb == 0) pdl_launch_dependents();
+            st += kSPB;
+            slot += kSPB;
+            if (slot >= S) {
+                slot -= S;
+                round++;
+            }
+            kk += kSPB * kRPS;
+            while (kk >= Ku) {
+                kk -= Ku;
+                t++;
+            }
+        }
+        if (nst == 0) pdl_launch_dependents();
         return;
     }
 
     // ------------------------------ consumers ------------------------------
+    // Warp w handles rows w, w + 8, ... (kRPW of them) of every stage.
     const uint32_t ring_base = smem_u32addr(ring);
     const uint32_t red_base = smem_u32addr(red);
     const int tid = threadIdx.x;  // 0..255
@@ -308,14 +325,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     const int64_t last_tile = (f1 - 1) / K;
     int64_t cur_tile = first_tile;
     int64_t next_boundary = (cur_tile + 1) * K - f0;
-
-    // this warp's row position, tracked incrementally
-    int64_t my_t, my_k;
-    {
-        const int64_t f = f0 + warp;
-        my_t = f / K;
-        my_k = f - my_t * K;
-    }
 
     auto flush = [&](int64_t tile) {
         // 1. per-warp partials into shared memory (swizzled float4 slots)
@@ -345,11 +354,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if (m >= p.M || c >= ncols) continue;
             const int L = c / VPT, i = (c % VPT) / 4;
             const int phys = L * VPT + 4 * (i ^ red_swz<VPT>(L)) + (c & 3);
-            float s = 0.0f;
+            float sum = 0.0f;
 #pragma unroll
-            for (int w = 0; w < kNW; w++) s += red[(w * MR + m) * TN + phys];
-            if (whole) p.y[(int64_t)m * N + n0 + c] = s;
-            else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = s;
+            for (int w = 0; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
+            if (whole) p.y[(int64_t)m * N + n0 + c] = sum;
+            else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = sum;
         }
         named_bar_sync(1, kNW * 32);
         if (!whole) {
@@ -364,15 +373,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             named_bar_sync(1, kNW * 32);
             if (flag[0]) {
                 __threadfence();
-                for (int idx = tid; idx < MR * TN; idx += kNW * 32) {
-                    const int m = idx / TN, c = idx % TN;
+                // contributor cf starts before the tile (slot 1) unless it
+                // starts exactly on it; every later contributor starts inside
+                // the tile (slot 0).  Sum in CTA order, 4 loads in flight.
+                const int ncon = (int)(cl - cf + 1);
+                const bool cf_slot1 = cf * p.rpc < tile * K;
+                for (int idx4 = tid; idx4 < MR * TN / 4; idx4 += kNW * 32) {
+                    const int m = (idx4 * 4) / TN, c = (idx4 * 4) % TN;
                     if (m >= p.M || c >= ncols) continue;
-                    float s = 0.0f;
-                    for (int64_t cta = cf; cta <= cl; cta++) {
-                        const int sl = ((cta * p.rpc) / K == tile) ? 0 : 1;
-                        s += __ldcg(&p.partials[((cta * 2 + sl) * MR + m) * TN + c]);
+                    const float *base = p.partials + (size_t)m * TN + c;
+                    float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int j0 = 0; j0 < ncon; j0 += 4) {
+                        float4 v[4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int j = j0 + u;
+                            if (j < ncon) {
+                                const int64_t cta = cf + j;
+                                const int sl = (j == 0 && cf_slot1) ? 1 : 0;
+                                v[u] = __ldcg(reinterpret_cast<const float4 *>(base + (size_t)(cta * 2 + sl) * MR * TN));
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            if (j0 + u < ncon) {
+                                acc4.x += v[u].x; acc4.y += v[u].y; acc4.z += v[u].z; acc4.w += v[u].w;
+                            }
+                        }
                     }
-                    p.y[(int64_t)m * N + n0 + c] = s;
+                    float *yo = p.y + (int64_t)m * N + n0 + c;
+                    yo[0] = acc4.x; yo[1] = acc4.y; yo[2] = acc4.z; yo[3] = acc4.w;
                 }
                 if (tid == 0) atomicExch(&p.counters[tile], 0);
             }
@@ -380,37 +410,68 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         }
     };
 
-    for (int64_t s = 0; s < nst; s++) {
-        const int slot = (int)(s % S);
-        if (!mbar_wait_bounded(smem_u32addr(&full[slot]), (uint32_t)((s / S) & 1), kWaitNs))
-            set_status(kStatusTimeout);
-        const int64_t pl = s * kNW + warp;
-        if (pl < nrows) {
-            while (pl >= next_boundary) {
+    // this warp's row: local index pl, (tile, k) = (t, kk); slot/phase of the ring
+    static_assert(kRPW == 1, "one row per consumer warp per stage");
+    const uint32_t Ku = (uint32_t)K;
+    const int nst32 = (int)nst, nrows32 = (int)nrows;
+    uint32_t t, kk;
+    {
+        const int64_t f = f0 + warp;
+        t = (uint32_t)(f / K);
+        kk = (uint32_t)(f - (int64_t)t * K);
+    }
+    int pl = warp;
+    int nb32 = (int)next_boundary;
+    uint32_t slot = 0, phase = 0;
+    auto load_x = [&](int row, uint32_t k, float (&xv)[MR]) {
+#pragma unroll
+        for (int m = 0; m < MR; m++)
+            xv[m] = (row < nrows32 && m < p.M) ? __ldg(p.x + (int64_t)m * K + k) : 0.0f;
+    };
+    float xcur[MR];
+    load_x(pl, kk, xcur);
+    const uint32_t warp_row0 = ring_base + (uint32_t)(warp * p.row_cap);
+    const uint32_t stage_bytes = (uint32_t)(kRPS * p.row_cap);
+
+    for (int s = 0; s < nst32; s++) {
+        uint32_t nt = t, nk = kk + kRPS;
+        while (nk >= Ku) {
+            nk -= Ku;
+            nt++;
+        }
+        float xnext[MR];
+        if constexpr (MR <= 2) load_x(pl + kRPS, nk, xnext);
+        if (!mbar_wait_bounded(smem_u32addr(&full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
+        if (pl < nrows32) {
+            while (pl >= nb32) {
                 flush(cur_tile);
                 cur_tile++;
-                next_boundary += K;
+                nb32 += (int)K;
             }
-            const int64_t n0 = my_t * TN;
-            const int64_t nl = n0 + lane * VPT;
-            if (nl < N && lane * VPT < TN) {
-                const int64_t v0 = my_k * N + n0;
-                const int64_t a_lo = ((v0 >> 8) * B) & ~int64_t(15);
-                const int64_t v = v0 + lane * VPT;
-                const uint32_t blk = ring_base + (uint32_t)((slot * kNW + warp) * p.row_cap) +
-                                     (uint32_t)((v >> 8) * B - a_lo);
-                float xv[MR];
-#pragma unroll
-                for (int m = 0; m < MR; m++) xv[m] = (m < p.M) ? __ldg(p.x + (int64_t)m * K + my_k) : 0.0f;
-                decode_accum<QT, MR, VPT>(blk, (int)(v & 255), xv, acc);
+            const uint32_t n0 = t * TN;
+            if ((int64_t)n0 + lane * VPT < N) {
+                const uint64_t v0 = (uint64_t)kk * (uint64_t)N + n0;
+                const uint32_t b_lo = (uint32_t)(v0 >> 8);
+                const uint32_t lead = (b_lo * B) & 15u;  // a_lo = b_lo*B - lead
+                const uint32_t wl = ((uint32_t)v0 & 255u) + lane * VPT;
+                const uint32_t blk = warp_row0 + slot * stage_bytes + (wl >> 8) * B + lead;
+                decode_accum<QT, MR, VPT>(blk, (int)(wl & 255u), xcur, acc);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32addr(&empty[slot]));
-        my_k += kNW;
-        while (my_k >= K) {
-            my_k -= K;
-            my_t++;
+        if constexpr (MR <= 2) {
+#pragma unroll
+            for (int m = 0; m < MR; m++) xcur[m] = xnext[m];
+        } else {
+            load_x(pl + kRPS, nk, xcur);
+        }
+        t = nt;
+        kk = nk;
+        pl += kRPS;
+        if (++slot == (uint32_t)S) {
+            slot = 0;
+            phase ^= 1u;
         }
     }
     while (cur_tile <= last_tile) {
@@ -475,7 +536,9 @@ static int block_bytes(int qt) { return qt == kQ4K ? 144 : qt == kQ5K ? 176 : 21
 
 static Plan make_plan(const GemvShape &s, int device) {
     Plan pl{};
-    pl.generic = (s.N % 32) != 0;
+    // the fast path keeps byte offsets of the weight in 32 bits
+    const int64_t wbytes = ((s.K * s.N + 255) / 256) * block_bytes(s.qtype);
+    pl.generic = (s.N % 32) != 0 || wbytes >= (int64_t(1) << 32) - 4096;
     if (pl.generic) return pl;
     if (s.M <= 1) { pl.mr = 1; pl.vpt = 32; }
     else if (s.M <= 2) { pl.mr = 2; pl.vpt = 16; }
@@ -493,8 +556,8 @@ static Plan make_plan(const GemvShape &s, int device) {
     pl.row_cap = (((pl.tn / 256 + 1) * B + 16 + 16) + 15) & ~15;
     const size_t red = (size_t)kNW * pl.mr * pl.tn * 4;
     int stages = 8;
-    auto smem_for = [&](int st) { return (size_t)(((16 * st + 16) + 127) & ~127) + (size_t)st * kNW * pl.row_cap + red; };
-    while (stages > 2 && smem_for(stages) > (size_t)kSmemPerCta) stages--;
+    auto smem_for = [&](int st) { return (size_t)(((16 * st + 16) + 127) & ~127) + (size_t)st * kRPS * pl.row_cap + red; };
+    while (stages > 4 && smem_for(stages) > (size_t)kSmemPerCta) stages--;
     pl.stages = stages;
     pl.smem = smem_for(stages);
     pl.partial_bytes = ((size_t)pl.grid * 2 * pl.mr * pl.tn * 4 + 255) & ~size_t(255);
@@ -512,6 +575,9 @@ template <int QT, int MR, int VPT>
 static cudaError_t launch_fast(const GemvParams &gp, const Plan &pl, cudaStream_t stream) {
     auto kern = gemv_kernel<QT, MR, VPT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+    if (e != cudaSuccess) return e;
+    // two CTAs per SM need the largest shared-memory carveout
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);

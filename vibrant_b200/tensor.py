@@ -38,6 +38,17 @@ class QuantWeight:
 
 
 _WS: dict[tuple[int, int], torch.Tensor] = {}
+_WS_NEED: dict[tuple, int] = {}
+
+
+def workspace_bytes(qtype: int, M: int, K: int, N: int, device: int) -> int:
+    """vkq_matmul_workspace_bytes, memoised per shape and device."""
+    key = (qtype, M, K, N, device)
+    v = _WS_NEED.get(key)
+    if v is None:
+        v = vkq.matmul_workspace_bytes(qtype, M, K, N, device=device)
+        _WS_NEED[key] = v
+    return v
 
 
 def workspace(nbytes: int, device: int) -> torch.Tensor | None:
@@ -63,9 +74,8 @@ def matmul(x: torch.Tensor, w: QuantWeight, out: torch.Tensor | None = None, ws:
     dev = w.device_index
     if out is None:
         out = torch.empty((M, w.N), dtype=torch.float32, device=x.device)
-    need = vkq.matmul_workspace_bytes(w.qtype, M, w.K, w.N, device=dev)
     if ws is None:
-        ws = workspace(need, dev)
+        ws = workspace(workspace_bytes(w.qtype, M, w.K, w.N, dev), dev)
     ws_ptr = ws.data_ptr() if ws is not None else None
     ws_bytes = ws.numel() if ws is not None else 0
     st = stream if stream is not None else torch.cuda.current_stream(x.device)
