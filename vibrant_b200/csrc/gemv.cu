@@ -194,13 +194,16 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
         } else {
             qh[0] = lds16(qha);
         }
+        uint32_t qhs[(NCH + 1) / 2];
+#pragma unroll
+        for (int i = 0; i < (NCH + 1) / 2; i++) qhs[i] = qh[i] >> 4;
 #pragma unroll
         for (int c = 0; c < NCH; c++) {
-            const uint32_t h16 = (qh[c >> 1] >> (16 * (c & 1))) & 0xFFFFu;
-            // byte lane j of X = nibble j of h16 = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
-            const uint32_t X = prmt(h16, h16 >> 4, 0x5140u) & 0x0F0F0F0Fu;
+            // byte lane j of X = nibble j of the chunk's 16 qh bits
+            //                  = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
+            const uint32_t X = prmt(qh[c >> 1], qhs[c >> 1], (c & 1) ? 0x7362u : 0x5140u) & 0x0F0F0F0Fu;
             const uint32_t E = (wq[c] & 0x0F0F0F0Fu) | ((X & 0x03030303u) << 4);
-            const uint32_t O = ((wq[c] >> 4) & 0x0F0F0F0Fu) | ((X & 0x0C0C0C0Cu) << 2);
+            const uint32_t O = ((wq[c] >> 4) & 0x0F0F0F0Fu) | ((X << 2) & 0x30303030u);
             if (NCH == 4 && c >= 2) accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a1, 8388640.0f);
             else accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a0, 8388640.0f);  // 2^23 + 32
         }
@@ -225,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     const int hdr_bytes = ((16 * S + 16) + 127) & ~127;
     uint8_t *ring = smem + hdr_bytes;
     float *red = reinterpret_cast<float *>(ring + (size_t)S * kRPS * p.row_cap);
+    float *xbuf = red + kNW * MR * TN;  // [S][kRPS][MR]: x of each ring row
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t f0 = (int64_t)blockIdx.x * p.rpc;
@@ -235,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(smem_u32addr(&full[s]), 1);
+            mbar_init(smem_u32addr(&full[s]), 2);  // bytes posted + x stored
             mbar_init(smem_u32addr(&empty[s]), kNW);
         }
         mbar_init_fence();
@@ -261,6 +265,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
         const int nst32 = (int)nst, nrows32 = (int)nrows;
         int st = sub, slot = sub;  // this lane's stage and its ring slot (S >= kSPB)
         uint32_t round = 0;        // st / S
+        float xr[MR];
         for (int sb = 0; sb < nst32; sb += kSPB) {
             const bool stage_ok = st < nst32;
             if (stage_ok && round > 0) {
@@ -291,7 +296,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if (row_ok && bytes > 0)
                 bulk_g2s(ring_base + (uint32_t)((slot * kRPS + r) * p.row_cap), p.w + a_lo, bytes,
                          smem_u32addr(&full[slot]));
-            if (sb == 0) pdl_launch_dependents();
+            if (sb == 0) {
+                pdl_launch_dependents();
+                pdl_wait();  // x comes from the preceding kernel; weights did not
+#pragma unroll
+                for (int m = 0; m < MR; m++)
+                    xr[m] = (row_ok && m < p.M) ? __ldg(p.x + (int64_t)m * K + kk) : 0.0f;
+            }
+            // x of this row for every m (loaded one batch ahead), then the
+            // stage's second arrival
+            if (stage_ok) {
+#pragma unroll
+                for (int m = 0; m < MR; m++) xbuf[(slot * kRPS + r) * MR + m] = xr[m];
+            }
+            __syncwarp();
+            if (stage_ok && r == 0) mbar_arrive(smem_u32addr(&full[slot]));
             st += kSPB;
             slot += kSPB;
             if (slot >= S) {
@@ -303,8 +322,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 kk -= Ku;
                 t++;
             }
+            {
+                const bool next_ok = st < nst32 && (st * kRPS + r) < nrows32;
+#pragma unroll
+                for (int m = 0; m < MR; m++)
+                    xr[m] = (next_ok && m < p.M) ? __ldg(p.x + (int64_t)m * K + kk) : 0.0f;
+            }
         }
-        if (nst == 0) pdl_launch_dependents();
+        if (nst == 0) {
+            pdl_launch_dependents();
+            pdl_wait();
+        }
         return;
     }
 
@@ -319,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
 #pragma unroll
         for (int i = 0; i < VPT / 2; i++) acc[m][i] = 0ull;
     }
-    pdl_wait();  // x, y and the workspace may belong to the preceding kernel
+    pdl_wait();  // y and the workspace may belong to the preceding kernel
 
     const int64_t first_tile = f0 / K;
     const int64_t last_tile = (f1 - 1) / K;
@@ -423,24 +451,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     int pl = warp;
     int nb32 = (int)next_boundary;
     uint32_t slot = 0, phase = 0;
-    auto load_x = [&](int row, uint32_t k, float (&xv)[MR]) {
-#pragma unroll
-        for (int m = 0; m < MR; m++)
-            xv[m] = (row < nrows32 && m < p.M) ? __ldg(p.x + (int64_t)m * K + k) : 0.0f;
-    };
-    float xcur[MR];
-    load_x(pl, kk, xcur);
     const uint32_t warp_row0 = ring_base + (uint32_t)(warp * p.row_cap);
     const uint32_t stage_bytes = (uint32_t)(kRPS * p.row_cap);
+    const uint32_t Nu = (uint32_t)N;
 
     for (int s = 0; s < nst32; s++) {
-        uint32_t nt = t, nk = kk + kRPS;
-        while (nk >= Ku) {
-            nk -= Ku;
-            nt++;
-        }
-        float xnext[MR];
-        if constexpr (MR <= 2) load_x(pl + kRPS, nk, xnext);
         if (!mbar_wait_bounded(smem_u32addr(&full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
         if (pl < nrows32) {
             while (pl >= nb32) {
@@ -450,24 +465,25 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             }
             const uint32_t n0 = t * TN;
             if ((int64_t)n0 + lane * VPT < N) {
-                const uint64_t v0 = (uint64_t)kk * (uint64_t)N + n0;
-                const uint32_t b_lo = (uint32_t)(v0 >> 8);
-                const uint32_t lead = (b_lo * B) & 15u;  // a_lo = b_lo*B - lead
-                const uint32_t wl = ((uint32_t)v0 & 255u) + lane * VPT;
+                // low 32 bits of v0 = k*N + n0 give the in-block offset of the
+                // row's first value and the 16-byte lead of its first block
+                const uint32_t v0 = kk * Nu + n0;
+                const uint32_t lead = (((v0 >> 8) & 15u) * (uint32_t)B) & 15u;
+                const uint32_t wl = (v0 & 255u) + lane * VPT;
                 const uint32_t blk = warp_row0 + slot * stage_bytes + (wl >> 8) * B + lead;
-                decode_accum<QT, MR, VPT>(blk, (int)(wl & 255u), xcur, acc);
+                float xv[MR];
+#pragma unroll
+                for (int m = 0; m < MR; m++) xv[m] = xbuf[(slot * kRPS + warp) * MR + m];
+                decode_accum<QT, MR, VPT>(blk, (int)(wl & 255u), xv, acc);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32addr(&empty[slot]));
-        if constexpr (MR <= 2) {
-#pragma unroll
-            for (int m = 0; m < MR; m++) xcur[m] = xnext[m];
-        } else {
-            load_x(pl + kRPS, nk, xcur);
+        kk += kRPS;
+        while (kk >= Ku) {
+            kk -= Ku;
+            t++;
         }
-        t = nt;
-        kk = nk;
         pl += kRPS;
         if (++slot == (uint32_t)S) {
             slot = 0;
@@ -556,7 +572,10 @@ static Plan make_plan(const GemvShape &s, int device) {
     pl.row_cap = (((pl.tn / 256 + 1) * B + 16 + 16) + 15) & ~15;
     const size_t red = (size_t)kNW * pl.mr * pl.tn * 4;
     int stages = 8;
-    auto smem_for = [&](int st) { return (size_t)(((16 * st + 16) + 127) & ~127) + (size_t)st * kRPS * pl.row_cap + red; };
+    auto smem_for = [&](int st) {
+        return (size_t)(((16 * st + 16) + 127) & ~127) + (size_t)st * kRPS * pl.row_cap + red +
+               (size_t)st * kRPS * pl.mr * 4;
+    };
     while (stages > 4 && smem_for(stages) > (size_t)kSmemPerCta) stages--;
     pl.stages = stages;
     pl.smem = smem_for(stages);
