@@ -117,6 +117,22 @@ VKQ_API int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int6
              const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
              void *stream);
 
+/* The fp32 GEMV of vkq_gemv without a workspace argument, for callers that
+ * cannot allocate device memory: a host whose allocator owns every byte of
+ * the device (a pool sized to a fixed budget, as vibrant's gpu.BufferPool
+ * is), a plugin whose memory plan is fixed before it runs, or a caller that
+ * must avoid cudaMalloc's device-wide synchronisation.  No counterpart in the
+ * reference.  The split-K scratch lives in a fixed 8 MiB device array inside
+ * the library, which every GPU that loads the library holds until the
+ * process exits; a problem needing more scratch is rejected with
+ * VKQ_ERR_WORKSPACE.  The call allocates nothing.  Its first call on a device
+ * looks the array up (cudaGetSymbolAddress) -- make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (different streams, or different host threads on one device) race
+ * and must be serialised by the caller.  1 <= M <= 8. */
+VKQ_API int vkq_gemv_noalloc(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+                             const float *x, int64_t M, float *y, void *stream);
+
 /* Reads and clears the device-side status word of this library on a device
  * (set when a bounded wait inside a kernel gave up).  Synchronizes with the
  * device.  *code receives VKQ_OK or VKQ_ERR_DEVICE_TIMEOUT. */

@@ -41,6 +41,8 @@ int device_sm_count(int device) {
     return cache[dev];
 }
 
+bool vkq_last_error_empty() { return t_err[0] == '\0'; }
+
 static int block_bytes(int qt) {
     switch (qt) {
     case VKQ_Q4_K: return 144;
@@ -229,6 +231,20 @@ int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, i
     }
     GemvShape s{qtype, K, N, M};
     return gemv_launch(s, w, w_bytes, x, y, workspace, workspace_bytes, (cudaStream_t)stream, device);
+}
+
+int vkq_gemv_noalloc(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
+                     int64_t M, float *y, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, y);
+    if (st) return st;
+    if (M > 8) {
+        set_error("vkq_gemv_noalloc serves 1 <= M <= 8 (got %lld)", (long long)M);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    GemvShape s{qtype, K, N, M};
+    return gemv_launch_noalloc(s, w, w_bytes, x, y, (cudaStream_t)stream, device);
 }
 
 int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,

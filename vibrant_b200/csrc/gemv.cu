@@ -32,6 +32,7 @@
 //    adds the partials in CTA order, so results are deterministic.
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 
 #include "kq_device.cuh"
 #include "vkq_internal.h"
@@ -672,6 +673,60 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
         return 5;
     }
     return 0;
+}
+
+// ---- fixed device-resident scratch (vkq_gemv_noalloc) ----------------------
+// For callers that cannot allocate device memory themselves, the split-K
+// partial sums and tile counters can live in this file-scope array instead of
+// a caller-provided workspace.  It is part of the module image, so every GPU
+// that loads the library keeps these bytes until the process exits.  In host
+// code the name g_gemv_scratch is only a stand-in for the symbol; the device
+// address comes from cudaGetSymbolAddress, looked up once per device.
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) uint8_t g_gemv_scratch[kNoAllocScratchBytes];
+
+static void *noalloc_scratch_address(int device) {
+    static std::mutex mu;
+    static void *addr[64] = {nullptr};
+    int dev = device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    if (dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> g(mu);
+    if (addr[dev] == nullptr) {
+        void *ptr = nullptr;
+        // the device is current here (the entry point made it so)
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_gemv_scratch);
+        if (e != cudaSuccess) {
+            set_error("cudaGetSymbolAddress(scratch) on device %d: %s", dev, cudaGetErrorString(e));
+            return nullptr;
+        }
+        addr[dev] = ptr;
+    }
+    return addr[dev];
+}
+
+int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
+                        cudaStream_t stream, int device) {
+    Plan pl = make_plan(s, device);
+    if (pl.generic) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);
+    const size_t need = pl.counter_bytes + pl.partial_bytes;
+    if (need > kNoAllocScratchBytes) {
+        set_error("this GEMV needs %zu bytes of scratch; the fixed scratch of vkq_gemv_noalloc holds %zu", need,
+                  kNoAllocScratchBytes);
+        return 4;
+    }
+    void *base = noalloc_scratch_address(device);
+    if (base == nullptr) {
+        if (vkq_last_error_empty()) set_error("cannot locate the fixed scratch on device %d", device);
+        return 5;
+    }
+    // the tile counters must start at zero; the array keeps the last call's bytes
+    cudaError_t e = cudaMemsetAsync(base, 0, pl.counter_bytes, stream);
+    if (e != cudaSuccess) {
+        set_error("clearing the fixed scratch: %s", cudaGetErrorString(e));
+        return 5;
+    }
+    return gemv_launch(s, w, w_bytes, x, y, base, kNoAllocScratchBytes, stream, device);
 }
 
 int gemv_read_status() {

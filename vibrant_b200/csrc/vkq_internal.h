@@ -24,8 +24,13 @@ size_t gemv_workspace_bytes(const GemvShape &s, int device);
 // Returns a vkq_status code; on failure writes a message with set_error.
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
                 size_t ws_bytes, cudaStream_t stream, int device);
+// Same GEMV with its scratch in a fixed device array of the library (no
+// workspace argument, nothing allocated); see vkq_gemv_noalloc.
+int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
+                        cudaStream_t stream, int device);
 int gemv_read_status();  // reads and clears this TU's device status word (synchronous)
 
 void set_error(const char *fmt, ...);
+bool vkq_last_error_empty();
 
 }  // namespace vkq
