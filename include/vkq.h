@@ -102,7 +102,8 @@ VKQ_API int vkq_matmul_workspace_bytes(int device, int qtype, int64_t M, int64_t
 /* y[M,N] = x[M,K] . W[K,N] with W quantized (qtype), float32 in and out.
  * Dispatch: M <= 8 runs vkq_gemv (fp32 accumulate, max relative error 1e-5
  * against the reference's float32 CPU MatMul); larger M runs vkq_gemm (bf16
- * tensor cores, 2e-2).  w_bytes is the size of the weight buffer (at least
+ * tensor cores, 2e-2) when N % 32 == 0 and K % 8 == 0, else vkq_gemv over
+ * 8-row chunks.  w_bytes is the size of the weight buffer (at least
  * vkq_weight_bytes).  w must be 16-byte aligned.
  * Replaces matmul_f32_single_row_launch (internal/gpu/cuda/launch.cu:37-48,
  * M == 1) and matmul_f32_launch (launch.cu:25-35, M > 1) as called by
@@ -116,6 +117,15 @@ VKQ_API int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, in
 VKQ_API int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
              const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
              void *stream);
+
+/* The bf16 tensor-core (tcgen05/TMEM) GEMM path of vkq_matmul for any M >= 1:
+ * bf16 operands, fp32 accumulate, max relative error 2e-2 of sum_k |x w|.
+ * Needs N % 32 == 0, K % 8 == 0 and x 8-byte aligned; the workspace holds a
+ * bf16 copy of x.  Replaces matmul_f32 (internal/gpu/cuda/kernels.cu:11-57)
+ * on the prefill path of matmulGPU (internal/tensor/ops_cuda.go:64-73). */
+VKQ_API int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+                     const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
+                     void *stream);
 
 /* The fp32 GEMV of vkq_gemv without a workspace argument, for callers that
  * cannot allocate device memory: a host whose allocator owns every byte of

@@ -210,13 +210,16 @@ int vkq_matmul_workspace_bytes(int device, int qtype, int64_t M, int64_t K, int6
         set_error("invalid arguments to vkq_matmul_workspace_bytes");
         return VKQ_ERR_INVALID_ARGUMENT;
     }
+    GemvShape s{qtype, K, N, M};
     if (M <= 8) {
-        GemvShape s{qtype, K, N, M};
         *bytes = gemv_workspace_bytes(s, device);
         return VKQ_OK;
     }
-    set_error("M=%lld > 8: the tensor-core path is not built in this library", (long long)M);
-    return VKQ_ERR_UNSUPPORTED;
+    // tensor-core GEMM (bf16 copy of x), or 8-row GEMV chunks for shapes it does not serve
+    GemvShape s8{qtype, K, N, 8};
+    size_t a = gemm_workspace_bytes(s), b = gemv_workspace_bytes(s8, device);
+    *bytes = a > b ? a : b;
+    return VKQ_OK;
 }
 
 int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
@@ -247,13 +250,34 @@ int vkq_gemv_noalloc(int device, int qtype, const void *w, int64_t w_bytes, int6
     return gemv_launch_noalloc(s, w, w_bytes, x, y, (cudaStream_t)stream, device);
 }
 
+int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
+             int64_t M, float *y, void *workspace, size_t workspace_bytes, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, y);
+    if (st) return st;
+    GemvShape s{qtype, K, N, M};
+    return gemm_launch(s, w, x, y, workspace, workspace_bytes, (cudaStream_t)stream, device);
+}
+
 int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
                int64_t M, float *y, void *workspace, size_t workspace_bytes, void *stream) {
     if (M <= 8) return vkq_gemv(device, qtype, w, w_bytes, K, N, x, M, y, workspace, workspace_bytes, stream);
     int st = enter(device);
     if (st) return st;
-    set_error("M=%lld > 8: the tensor-core path is not built in this library", (long long)M);
-    return VKQ_ERR_UNSUPPORTED;
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, y);
+    if (st) return st;
+    if (N % 32 == 0 && K % 8 == 0 && (reinterpret_cast<uintptr_t>(x) & 7u) == 0)
+        return vkq_gemm(device, qtype, w, w_bytes, K, N, x, M, y, workspace, workspace_bytes, stream);
+    // shapes the tensor-core kernel does not serve: fp32 GEMV over 8-row chunks
+    for (int64_t m0 = 0; m0 < M; m0 += 8) {
+        const int64_t mc = (M - m0) < 8 ? (M - m0) : 8;
+        GemvShape s{qtype, K, N, mc};
+        st = gemv_launch(s, w, w_bytes, x + m0 * K, y + m0 * N, workspace, workspace_bytes, (cudaStream_t)stream,
+                         device);
+        if (st) return st;
+    }
+    return VKQ_OK;
 }
 
 int vkq_device_status(int device, int *code) {
@@ -266,7 +290,9 @@ int vkq_device_status(int device, int *code) {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return check_launch(e, "cudaDeviceSynchronize");
     int g = gemv_read_status();
-    if (g < 0) {
+    const int g2 = gemm_read_status();
+    if (g == 0) g = g2;
+    if (g < 0 || g2 < 0) {
         set_error("cannot read the device status word");
         return VKQ_ERR_CUDA;
     }

@@ -28,7 +28,13 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
 // workspace argument, nothing allocated); see vkq_gemv_noalloc.
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
                         cudaStream_t stream, int device);
-int gemv_read_status();  // reads and clears this TU's device status word (synchronous)
+int gemv_read_status();
+
+// bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
+size_t gemm_workspace_bytes(const GemvShape &s);
+int gemm_launch(const GemvShape &s, const void *w, const float *x, float *y, void *ws, size_t ws_bytes,
+                cudaStream_t stream, int device);
+int gemm_read_status();  // reads and clears this TU's device status word (synchronous)
 
 void set_error(const char *fmt, ...);
 bool vkq_last_error_empty();

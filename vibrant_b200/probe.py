@@ -42,7 +42,7 @@ def main(argv):
     dt = e0.elapsed_time(e1) / 1e3 / iters
     b = synth.n_blocks(K, N) * synth.BLOCK_BYTES[qt] + 4 * M * (K + N)
     print(f"qt={qt} K={K} N={N} M={M}: {dt * 1e6:.2f} us/launch  {b / dt / 1e9:.1f} GB/s  "
-          f"status={vkq.device_status(0)}")
+          f"{2 * M * K * N / dt / 1e12:.1f} TFLOP/s  status={vkq.device_status(0)}")
 
 
 if __name__ == "__main__":

@@ -75,11 +75,14 @@ def matmul(x: torch.Tensor, w: QuantWeight, out: torch.Tensor | None = None, ws:
     if out is None:
         out = torch.empty((M, w.N), dtype=torch.float32, device=x.device)
     if ws is None:
-        ws = workspace(workspace_bytes(w.qtype, M, w.K, w.N, dev), dev)
+        need = workspace_bytes(w.qtype, M, w.K, w.N, dev)
+        if path == "gemm":
+            need = max(need, workspace_bytes(w.qtype, max(M, 9), w.K, w.N, dev))
+        ws = workspace(need, dev)
     ws_ptr = ws.data_ptr() if ws is not None else None
     ws_bytes = ws.numel() if ws is not None else 0
     st = stream if stream is not None else torch.cuda.current_stream(x.device)
-    fn = vkq.gemv if path == "gemv" else vkq.matmul
+    fn = {"gemv": vkq.gemv, "gemm": vkq.gemm}.get(path, vkq.matmul)
     fn(w.qtype, w.buf.data_ptr(), w.nbytes, w.K, w.N, x.data_ptr(), M, out.data_ptr(), ws_ptr, ws_bytes,
        device=dev, stream=st)
     return out

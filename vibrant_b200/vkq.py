@@ -35,6 +35,7 @@ SIGNATURES = {
     "vkq_matmul_workspace_bytes": (_int, [_int, _int, _i64, _i64, _i64, ctypes.POINTER(_sz)]),
     "vkq_matmul": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
     "vkq_gemv": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
+    "vkq_gemm": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
     "vkq_gemv_noalloc": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "vkq_device_status": (_int, [_int, ctypes.POINTER(_int)]),
 }
@@ -112,6 +113,12 @@ def matmul(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: 
 def gemv(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: int, y_ptr: int,
          ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
     _check(load().vkq_gemv(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, ws_ptr, ws_bytes,
+                           _stream_ptr(stream)))
+
+
+def gemm(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: int, y_ptr: int,
+         ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
+    _check(load().vkq_gemm(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, ws_ptr, ws_bytes,
                            _stream_ptr(stream)))
 
 
