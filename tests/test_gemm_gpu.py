@@ -93,3 +93,25 @@ def test_matmul_dispatch_unaligned_shapes_fall_back_to_gemv(tvk, oracle):
 def test_gemm_status_clean(tvk):
     from vibrant_b200 import vkq
     assert vkq.device_status(0) == vkq.OK
+
+
+def test_gemm_then_gemv_share_one_workspace(tvk):
+    # a GEMM call must leave a shared workspace ready for a GEMV call (whose
+    # split-K tile counters live at its head and must be zero)
+    torch, vt = tvk
+    from vibrant_b200 import synth, vkq
+    qt, K, N = 12, 512, 2048
+    rng = np.random.default_rng(11)
+    vals = rng.integers(0, 16, K * N)
+    w = vt.QuantWeight(qt, K, N, helpers.encode_q45k_exact(vals, qt))
+    need = max(vt.workspace_bytes(qt, 600, K, N, 0), vt.workspace_bytes(qt, 1, K, N, 0))
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    xg = torch.from_numpy(synth.activations(600, K, seed=5)).cuda()
+    x1 = rng.integers(-8, 9, (1, K)).astype(np.float32)
+    ref = (x1.astype(np.int64) @ vals.reshape(K, N).astype(np.int64)).astype(np.float32)
+    for _ in range(2):
+        vt.matmul(xg, w, ws=ws, path="gemm")
+        y1 = vt.matmul(torch.from_numpy(x1).cuda(), w, ws=ws)
+        torch.cuda.synchronize()
+        assert np.array_equal(y1.cpu().numpy(), ref)
+    assert vkq.device_status(0) == vkq.OK

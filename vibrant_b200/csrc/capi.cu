@@ -217,7 +217,7 @@ int vkq_matmul_workspace_bytes(int device, int qtype, int64_t M, int64_t K, int6
     }
     // tensor-core GEMM (bf16 copy of x), or 8-row GEMV chunks for shapes it does not serve
     GemvShape s8{qtype, K, N, 8};
-    size_t a = gemm_workspace_bytes(s), b = gemv_workspace_bytes(s8, device);
+    size_t a = gemm_workspace_bytes(s, device), b = gemv_workspace_bytes(s8, device);
     *bytes = a > b ? a : b;
     return VKQ_OK;
 }
@@ -257,7 +257,7 @@ int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, i
     st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, y);
     if (st) return st;
     GemvShape s{qtype, K, N, M};
-    return gemm_launch(s, w, x, y, workspace, workspace_bytes, (cudaStream_t)stream, device);
+    return gemm_launch(s, w, w_bytes, x, y, workspace, workspace_bytes, (cudaStream_t)stream, device);
 }
 
 int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,

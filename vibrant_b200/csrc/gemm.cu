@@ -9,23 +9,33 @@
 // 2e-2 of sum_k |x w|).
 //
 // The product is computed transposed, D[n][m] = W^T[n][k] . X^T[k][m], so
-// that the operand built on the fly (the dequantized weight) is the MMA's A:
-//  * A tile: 128 n x 64 k bf16, written by the dequant warps straight from the
-//    packed blocks into the MN-major 128-byte-swizzled layout (atoms of 64 n x
-//    8 k, 1024 bytes; the two 64-n halves 1024 B apart, k groups 2048 B apart).
-//    A super-block row gives 256 consecutive n of one k, so MN-major is the
-//    natural orientation.
-//  * B tile: X converted to bf16 once per call (workspace), loaded by TMA as
-//    [mma_n rows of m] x [64 k] with the 128-byte swizzle (K-major, 8-row
-//    atoms, SBO 1024 B).  No multicast.
-//  * D: fp32 in TMEM, 128 lanes (n) x mma_n columns (m) per accumulator; two
-//    accumulators cover 512 rows of X per CTA, so each dequantized W tile
-//    feeds 2 x 4 MMAs (128 x 256 x 16) per 64-k step.
-// Warp roles (192 threads): warp 0 issues the TMA loads of X, warp 1 owns TMEM
-// and issues tcgen05.mma from one thread, warps 2..5 dequantize W into the A
-// ring and afterwards drain TMEM to Y (warp w reads TMEM lanes 32*(w%4)..).
-// Every mbarrier wait is bounded and reports a timeout through a device
-// status word; TMEM is always released.
+// that the operand built on the fly (the dequantized weight) is the MMA's A
+// (M = 128 rows of n) and X is the MMA's B (N = bm columns of m):
+//  * raw ring: the super-blocks under a 128 n x 64 k tile (one or two blocks
+//    per k row) are streamed from HBM into shared memory by one producer warp,
+//    several stages deep: as one 2D TMA tile copy per stage when the k rows
+//    have a 16-byte byte pitch (N % 256 == 0 and N/256 * B % 16 == 0), else
+//    with 16-byte cp.async, consecutive lanes on consecutive bytes of a row
+//    (one bulk copy per 144..420-byte row would be limited by the bulk-copy
+//    request rate, ~40 ns per request per SM);
+//  * A ring: sixteen dequant warps turn a raw stage into the bf16 A tile, written
+//    straight into the MN-major 128-byte-swizzled layout (atoms of 64 n x 8 k,
+//    1024 bytes; the two 64-n halves 1024 B apart, k groups 2048 B apart);
+//  * B ring: X is converted to bf16 once per call (workspace) and loaded by
+//    TMA as [bm rows of m] x [64 k] with the 128-byte swizzle (K-major, 8-row
+//    atoms, SBO 1024 B).  No multicast;
+//  * D: fp32 in TMEM, 128 lanes (n) x bm columns (m), double-buffered so the
+//    epilogue warps drain tile i to Y while the MMA warp accumulates tile i+1.
+// The grid is persistent (at most one CTA per SM); work units are
+// (n tile, m tile, k split) taken round-robin.  When the output tiles alone
+// cannot fill the machine (narrow N), K is split and the partial products go
+// to a workspace that a second kernel adds up in split order (deterministic).
+// Warp roles (736 threads): 0 raw-weight producer, 1 X TMA producer, 2 TMEM
+// owner + MMA issuer (one thread), 3..18 dequant (one 32-value unit per
+// thread per k step; four warps per scheduler hide the decode's latency),
+// 19..22 epilogue (warp w reads TMEM lanes 32*(w%4)..+31).  Every mbarrier wait is bounded; a wait that runs
+// out sets the device status word and an abort flag that ends every role's
+// loop, copies in flight are waited for (bounded) and TMEM is always released.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -40,29 +50,33 @@ namespace vkq {
 
 static __device__ int g_gemm_status;
 
-constexpr int kGBN = 128;                     // n rows per CTA (MMA M)
+constexpr int kGBN = 256;                     // n per tile: one super-block per k row
+constexpr int kMmaM = 128;                    // n rows per MMA (two MMAs per tile and 16-k step)
 constexpr int kGBK = 64;                      // k per stage: one 128-byte swizzle row of bf16
-constexpr int kGThreads = 192;                // 6 warps
-constexpr int kGDeq = 128;                    // dequant / epilogue threads (warps 2..5)
-constexpr int kAStage = kGBN * kGBK * 2;      // 16 KB
-constexpr uint64_t kGWaitNs = 2000000000ull;  // bounded waits: 2 s
+constexpr int kAHalf = kMmaM * kGBK * 2;      // 16 KB: the A operand of one MMA
+constexpr int kAStage = 2 * kAHalf;           // 32 KB
+constexpr int kWRaw = 0, kWX = 1, kWMma = 2, kWDeq = 3, kNDeq = 16, kWEpi = 19, kNEpi = 4;
+constexpr int kGThreads = (kWEpi + kNEpi) * 32;  // 736
+constexpr uint64_t kGWaitNs = 2000000000ull;     // bounded waits: 2 s
+constexpr uint64_t kDrainNs = 20000000ull;       // waits for copies in flight at teardown: 20 ms
+constexpr int kMaxStages = 8;
 
 struct GemmParams {
     const uint8_t *w;
-    float *y;
+    int64_t w_bytes;    // valid bytes of w (copies never read past them)
+    float *y;           // Y [M][N], or partials [splits][M][N] when splits > 1
     int64_t K, N, M;
-    int mma_n;   // m columns per accumulator (multiple of 32, <= 256: the epilogue drains 32 at a time)
-    int nacc;    // accumulators per CTA (1 or 2)
-    int stages;  // ring depth
-    int ksteps;  // ceil(K / 64)
-    int tmem_cols;
+    int bm;             // m per tile = MMA N (multiple of 16, <= 256)
+    int m_tiles, splits, units;
+    int ksteps, kper;   // k steps in all, per split
+    int sr, sa, sb;     // raw / A / B ring depths
+    int raw_slot;       // bytes per raw row slot (multiple of 16)
+    int raw_tma;        // raw stages are 2D tile copies (k rows with a 16-byte pitch)
+    int tmem_cols, acc_stride;
+    int nbuf;           // TMEM accumulator buffers (2: the epilogue overlaps the next unit)
 };
 
 __device__ __forceinline__ void g_set_status(int c) { atomicExch(&g_gemm_status, c); }
-
-__device__ __forceinline__ void g_wait(uint32_t bar, uint32_t parity) {
-    if (!mbar_wait_bounded(bar, parity, kGWaitNs)) g_set_status(kStatusTimeout);
-}
 
 // ---- UMMA descriptors ---------------------------------------------------
 // Shared-memory matrix descriptor: start >> 4 in bits [0,14), leading byte
@@ -110,47 +124,58 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return r;
 }
 
-// ---- raw super-block fetch for one 32-value unit --------------------------
-// A unit is 32 consecutive n of one k (one sub-block of one super-block,
-// since N and n0 are multiples of 32).
+// ---- raw super-block words for one 32-value unit --------------------------
+// A unit is 32 consecutive n of one k: one sub-block of one super-block,
+// since N and the tile origin are multiples of 32.
 struct RawUnit {
     uint32_t v[10];
-    uint32_t shf;  // Q6_K: byte misalignment of ql/qh words (0 or 16 bits)
+    uint32_t shf;  // Q6_K: byte misalignment of the ql/qh words (0 or 16 bits)
     uint32_t within;
     bool valid;
 };
 
+// Reads a unit from a super-block held in shared memory at `blk` (16-byte
+// aligned for Q4_K/Q5_K, 2-byte aligned for Q6_K).
 template <int QT>
-__device__ __forceinline__ void fetch_unit(const uint8_t *__restrict__ w, int64_t vidx, bool valid, RawUnit &u) {
-    constexpr int B = QT_<QT>::BYTES;
+__device__ __forceinline__ void load_unit(uint32_t blk, uint32_t within, bool valid, RawUnit &u) {
     u.valid = valid;
-    u.within = (uint32_t)(vidx & 255);
+    u.within = within;
     if (!valid) return;
-    const uint8_t *blk = w + (vidx >> 8) * B;
     if constexpr (QT == kQ4K || QT == kQ5K) {
-        const uint4 h = __ldg(reinterpret_cast<const uint4 *>(blk));
-        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(blk + (QT == kQ4K ? 16 : 48) + (u.within >> 1)));
+        const uint4 h = lds128(blk);
+        const uint4 q = lds128(blk + (QT == kQ4K ? 16u : 48u) + (within >> 1));
         u.v[0] = h.x; u.v[1] = h.y; u.v[2] = h.z; u.v[3] = h.w;
         u.v[4] = q.x; u.v[5] = q.y; u.v[6] = q.z; u.v[7] = q.w;
-        if constexpr (QT == kQ5K) u.v[8] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16 + (u.within >> 3)));
+        if constexpr (QT == kQ5K) u.v[8] = lds32(blk + 16u + (within >> 3));
     } else {
-        // blocks are 2-byte aligned: fetch aligned words and shift later
-        const uintptr_t ql = reinterpret_cast<uintptr_t>(blk) + (u.within >> 1);
-        const uintptr_t qh = reinterpret_cast<uintptr_t>(blk) + 128 + (u.within >> 2);
-        u.shf = (uint32_t)(ql & 3u) * 8u;  // ql and qh share the misalignment (both offsets are even multiples of 4)
-        const uint32_t *qlw = reinterpret_cast<const uint32_t *>(ql & ~uintptr_t(3));
-        const uint32_t *qhw = reinterpret_cast<const uint32_t *>(qh & ~uintptr_t(3));
+        // ql (offset within/2) and qh (offset 128 + within/4) are multiples of
+        // 4 bytes into the block, so both share the block's misalignment
+        const uint32_t ql = blk + (within >> 1);
+        const uint32_t qh = blk + 128u + (within >> 2);
+        u.shf = (ql & 3u) * 8u;
 #pragma unroll
-        for (int i = 0; i < 5; i++) u.v[i] = __ldg(qlw + i);
+        for (int i = 0; i < 5; i++) u.v[i] = lds32((ql & ~3u) + 4u * i);
 #pragma unroll
-        for (int i = 0; i < 3; i++) u.v[5 + i] = __ldg(qhw + i);
-        const uint16_t sraw = __ldg(reinterpret_cast<const uint16_t *>(blk + 192 + (u.within >> 4)));
-        const uint16_t draw = __ldg(reinterpret_cast<const uint16_t *>(blk + 208));
-        u.v[8] = (uint32_t)sraw | ((uint32_t)draw << 16);
+        for (int i = 0; i < 3; i++) u.v[5 + i] = lds32((qh & ~3u) + 4u * i);
+        const uint32_t sraw = lds16(blk + 192u + (within >> 4));
+        const uint32_t draw = lds16(blk + 208u);
+        u.v[8] = sraw | (draw << 16);
     }
 }
 
-// Decode one unit into 32 fp32 values, rounded to bf16 pairs (16 words).
+// A pair of fp32 values rounded to a bf16 pair.
+__device__ __forceinline__ uint32_t pair_bf16(float2 w2) { return bf16x2(w2.x, w2.y); }
+template <int J>
+__device__ __forceinline__ float2 magic_pair(uint32_t E, uint32_t O) {
+    return make_float2(byte_as_magic<J>(E), byte_as_magic<J>(O));
+}
+
+// Decode one unit into 32 values, rounded to bf16 pairs (16 words).  The
+// values come out of the packed bytes as in the fp32 GEMV: nibbles of even
+// and odd values are moved into byte lanes E and O, a byte permute into the
+// exponent of 2^23 turns each into a float, one packed add removes 2^23.
+// Q4_K/Q5_K: w = fma(d*sc, q, -dmin*m), equal to the reference's
+// (d*sc)*q - dmin*m because (d*sc)*q is exact; Q6_K: w = (d*s) * (q - 32).
 template <int QT>
 __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&out)[16]) {
     if (!u.valid) {
@@ -166,70 +191,134 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
         const uint32_t sh = 6u * (sb & 3);
         const float ds = d * (float)((sc24 >> sh) & 63u);
         const float dm = dmin * (float)((m24 >> sh) & 63u);
-        const uint32_t qh = (QT == kQ5K) ? u.v[8] : 0u;
+        const float2 negmag = make_float2(-8388608.0f, -8388608.0f), s2 = make_float2(ds, ds), nm2 = make_float2(-dm, -dm);
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int v0 = 2 * i, v1 = 2 * i + 1;
-            uint32_t q0 = (u.v[4 + (v0 >> 3)] >> (4 * (v0 & 7))) & 15u;
-            uint32_t q1 = (u.v[4 + (v1 >> 3)] >> (4 * (v1 & 7))) & 15u;
+        for (int c = 0; c < 4; c++) {
+            uint32_t E = u.v[4 + c] & 0x0F0F0F0Fu;
+            uint32_t O = (u.v[4 + c] >> 4) & 0x0F0F0F0Fu;
             if constexpr (QT == kQ5K) {
-                q0 |= ((qh >> v0) & 1u) << 4;
-                q1 |= ((qh >> v1) & 1u) << 4;
+                // bit i of hb is the fifth bit of value 8c+i; bits 0,2,4,6
+                // (and 1,3,5,7) go to bit 4 of byte lanes 0..3
+                const uint32_t hb = (u.v[8] >> (8 * c)) & 0xFFu;
+                E |= ((hb & 0x55u) * 0x410410u) & 0x10101010u;
+                O |= (((hb >> 1) & 0x55u) * 0x410410u) & 0x10101010u;
             }
-            out[i] = bf16x2(fmaf(ds, (float)q0, -dm), fmaf(ds, (float)q1, -dm));
+            out[4 * c + 0] = pair_bf16(f2fma(s2, f2add(magic_pair<0>(E, O), negmag), nm2));
+            out[4 * c + 1] = pair_bf16(f2fma(s2, f2add(magic_pair<1>(E, O), negmag), nm2));
+            out[4 * c + 2] = pair_bf16(f2fma(s2, f2add(magic_pair<2>(E, O), negmag), nm2));
+            out[4 * c + 3] = pair_bf16(f2fma(s2, f2add(magic_pair<3>(E, O), negmag), nm2));
         }
     } else {
-        uint32_t ql[4], qh[2];
+        uint32_t ql[4], qh[2], qhs[2];
 #pragma unroll
         for (int i = 0; i < 4; i++) ql[i] = __funnelshift_r(u.v[i], u.v[i + 1], u.shf);
 #pragma unroll
-        for (int i = 0; i < 2; i++) qh[i] = __funnelshift_r(u.v[5 + i], u.v[6 + i], u.shf);
+        for (int i = 0; i < 2; i++) {
+            qh[i] = __funnelshift_r(u.v[5 + i], u.v[6 + i], u.shf);
+            qhs[i] = qh[i] >> 4;
+        }
         const float d = hw_f16_to_f32(u.v[8] >> 16);
         const float ds0 = d * (float)(int)(int8_t)(u.v[8] & 0xFFu);
         const float ds1 = d * (float)(int)(int8_t)((u.v[8] >> 8) & 0xFFu);
+        const float2 neg = make_float2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-            const int v0 = 2 * i, v1 = 2 * i + 1;
-            const int q0 = (int)(((ql[v0 >> 3] >> (4 * (v0 & 7))) & 15u) | (((qh[v0 >> 4] >> (2 * (v0 & 15))) & 3u) << 4));
-            const int q1 = (int)(((ql[v1 >> 3] >> (4 * (v1 & 7))) & 15u) | (((qh[v1 >> 4] >> (2 * (v1 & 15))) & 3u) << 4));
-            const float s = (v0 < 16) ? ds0 : ds1;
-            out[i] = bf16x2(s * (float)(q0 - 32), s * (float)(q1 - 32));
+        for (int c = 0; c < 4; c++) {
+            // byte lane j of X = nibble j of the chunk's 16 qh bits
+            //                  = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
+            const uint32_t X = prmt(qh[c >> 1], qhs[c >> 1], (c & 1) ? 0x7362u : 0x5140u) & 0x0F0F0F0Fu;
+            const uint32_t E = (ql[c] & 0x0F0F0F0Fu) | ((X & 0x03030303u) << 4);
+            const uint32_t O = ((ql[c] >> 4) & 0x0F0F0F0Fu) | ((X << 2) & 0x30303030u);
+            const float2 s2 = c < 2 ? make_float2(ds0, ds0) : make_float2(ds1, ds1);
+            out[4 * c + 0] = pair_bf16(f2mul(s2, f2add(magic_pair<0>(E, O), neg)));
+            out[4 * c + 1] = pair_bf16(f2mul(s2, f2add(magic_pair<1>(E, O), neg)));
+            out[4 * c + 2] = pair_bf16(f2mul(s2, f2add(magic_pair<2>(E, O), neg)));
+            out[4 * c + 3] = pair_bf16(f2mul(s2, f2add(magic_pair<3>(E, O), neg)));
         }
     }
 }
 
+// Work unit u -> (n tile, m tile, k split); units of one n tile are adjacent
+// so that CTAs running at the same time share the weight rows in L2.
+struct Unit {
+    int64_t n0;
+    int m0;
+    int kb, ke;  // k steps [kb, ke)
+    int split;
+};
+__device__ __forceinline__ Unit unit_of(const GemmParams &p, int u) {
+    Unit r;
+    const int split = u % p.splits;
+    const int tile = u / p.splits;
+    r.n0 = (int64_t)(tile / p.m_tiles) * kGBN;
+    r.m0 = (tile % p.m_tiles) * p.bm;
+    r.kb = split * p.kper;
+    r.ke = min(r.kb + p.kper, p.ksteps);
+    r.split = split;
+    return r;
+}
+
+// Position in a ring of n stages: the stage index, the parity of the phase a
+// consumer waits for next (a producer waits for the other one) and the number
+// of uses so far; advancing takes no integer division.
+struct RingPos {
+    uint32_t idx = 0, phase = 0, uses = 0;
+    __device__ __forceinline__ void next(uint32_t n) {
+        uses++;
+        if (++idx == n) {
+            idx = 0;
+            phase ^= 1u;
+        }
+    }
+};
+
 template <int QT>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                            const __grid_constant__ CUtensorMap tmw,
                                                             const GemmParams p) {
+    constexpr int B = QT_<QT>::BYTES;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32addr(smem_raw);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
-    const int S = p.stages;
-    const uint32_t a_ring = base;                                           // S x 16 KB
-    const uint32_t b_stage = (uint32_t)(p.nacc * p.mma_n * 128);             // bytes per B stage
-    const uint32_t b_ring = a_ring + (uint32_t)(S * kAStage);
-    const uint32_t bars = b_ring + (uint32_t)S * b_stage;                    // a_full, b_full, empty [S], acc_full
-    auto a_full = [&](int s) { return bars + 8u * (uint32_t)s; };
-    auto b_full = [&](int s) { return bars + 8u * (uint32_t)(S + s); };
-    auto st_empty = [&](int s) { return bars + 8u * (uint32_t)(2 * S + s); };
-    const uint32_t acc_full = bars + 8u * (uint32_t)(3 * S);
-    const uint32_t tmem_slot = acc_full + 8u;
+    uint8_t *const gbase = smem_raw + (base - raw_base);  // generic pointer to `base`
+    const uint32_t b_stage = (uint32_t)(p.bm * 128);
+    const uint32_t raw_stage = (uint32_t)(kGBK * p.raw_slot);
+    const uint32_t a_ring = base;                                    // sa x 16 KB
+    const uint32_t b_ring = a_ring + (uint32_t)(p.sa * kAStage);     // sb x bm*128
+    const uint32_t r_ring = b_ring + (uint32_t)p.sb * b_stage;       // sr x 64*raw_slot
+    const uint32_t bars = r_ring + (uint32_t)p.sr * raw_stage;
+    auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+    // barrier indices
+    const int RF = 0, RE = kMaxStages, AF = 2 * kMaxStages, AE = 3 * kMaxStages, BF = 4 * kMaxStages,
+              BE = 5 * kMaxStages, CF = 6 * kMaxStages, CE = CF + 2, DR = CF + 4;
+    const uint32_t tmem_slot = bar(DR + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(gbase + (tmem_slot - base) + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t n0 = (int64_t)blockIdx.x * kGBN;
-    const int64_t m0 = (int64_t)blockIdx.y * p.nacc * p.mma_n;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(a_full(s), 4);   // one arrival per dequant warp
-            mbar_init(b_full(s), 1);   // TMA expect_tx
-            mbar_init(st_empty(s), 1); // tcgen05.commit
+        for (int s = 0; s < p.sr; s++) {
+            mbar_init(bar(RF + s), p.raw_tma ? 1 : 32);  // TMA expect_tx, or one cp.async arrival per lane
+            mbar_init(bar(RE + s), kNDeq);  // one arrival per dequant warp
         }
-        mbar_init(acc_full, 1);
+        for (int s = 0; s < p.sa; s++) {
+            mbar_init(bar(AF + s), kNDeq);
+            mbar_init(bar(AE + s), 1);  // tcgen05.commit
+        }
+        for (int s = 0; s < p.sb; s++) {
+            mbar_init(bar(BF + s), 1);  // TMA expect_tx
+            mbar_init(bar(BE + s), 1);  // tcgen05.commit
+        }
+        for (int s = 0; s < 2; s++) {
+            mbar_init(bar(CF + s), 1);      // tcgen05.commit after a unit's last MMA
+            mbar_init(bar(CE + s), kNEpi);  // one arrival per epilogue warp
+        }
+        mbar_init(bar(DR), 1);
+        *abort_flag = 0;
         mbar_init_fence();
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmx) : "memory");
+        if (p.raw_tma) asm volatile("prefetch.tensormap [%0];" ::"l"(&tmw) : "memory");
     }
-    if (warp == 1) {  // TMEM allocation (whole warp)
+    if (warp == kWMma) {  // TMEM allocation (whole warp)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
                      "r"(p.tmem_cols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -239,134 +328,288 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = lds32(tmem_slot);
 
-    // weights do not depend on the preceding kernel; X and Y do
-    pdl_launch_dependents();
-    pdl_wait();
+    // A wait that runs out records the timeout and stops every role.  Waits
+    // on the per-step critical path (dequant and MMA) poll; the others let
+    // the thread sleep so that they take no issue slots from the dequant warps.
+    auto wait = [&](uint32_t b, uint32_t parity, bool poll = false) -> bool {
+        if (poll ? mbar_wait_spin(b, parity, kGWaitNs) : mbar_wait_bounded(b, parity, kGWaitNs)) return true;
+        g_set_status(kStatusTimeout);
+        *abort_flag = 1;
+        return false;
+    };
 
-    if (warp == 0) {
-        // ---------------- TMA producer: bf16 X tiles ----------------
-        if (lane == 0) {
-            for (int ks = 0; ks < p.ksteps; ks++) {
-                const int s = ks % S;
-                if (ks >= S) g_wait(st_empty(s), (uint32_t)(((ks / S) - 1) & 1));
-                mbar_arrive_expect_tx(b_full(s), b_stage);
-                for (int a = 0; a < p.nacc; a++)
-                    tma_load_2d(b_ring + (uint32_t)s * b_stage + (uint32_t)(a * p.mma_n * 128), &tmx, ks * kGBK,
-                                (int)(m0 + a * p.mma_n), b_full(s));
+    // Drains the TMEM accumulator of unit `un` (buffer ab) to Y, or to the
+    // split's partials: 16-column chunks of both MMA halves, chunk ci taken by
+    // the warp of rank ci % nrank among the warps reading lane quarter q.
+    auto drain = [&](const Unit &un, uint32_t ab, int q, int rank, int nrank) {
+        float *yb = p.y + (int64_t)un.split * p.M * p.N;
+        const int nch = (p.bm + 15) / 16;  // 16-column chunks per MMA half
+        for (int ci = rank; ci < 2 * nch; ci += nrank) {
+            const int h = ci >= nch ? 1 : 0, c = 16 * (ci - h * nch);
+            uint32_t r[16];
+            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + ab * (uint32_t)p.acc_stride +
+                                   (uint32_t)(h * p.bm + c);
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                "[%16];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                  "=r"(r[15])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            const int64_t n = un.n0 + kMmaM * h + 32 * q + lane;
+            const int64_t mb = un.m0 + c;
+            const int mv = (int)min((int64_t)16, p.M - mb);
+            if (n < p.N && mv > 0) {
+                float *yp = yb + mb * p.N + n;  // walks down the m rows of this column
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    if (j < mv) *yp = __uint_as_float(r[j]);
+                    yp += p.N;
+                }
             }
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            const uint32_t idesc = idesc_bf16_f32(kGBN, p.mma_n);
-            for (int ks = 0; ks < p.ksteps; ks++) {
-                const int s = ks % S;
-                const uint32_t par = (uint32_t)((ks / S) & 1);
-                g_wait(a_full(s), par);
-                g_wait(b_full(s), par);
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint32_t a_s = a_ring + (uint32_t)(s * kAStage);
-                const uint32_t b_s = b_ring + (uint32_t)s * b_stage;
-#pragma unroll
-                for (int kk = 0; kk < kGBK / 16; kk++) {
-                    // A: 2 k-groups of 8 per 16-k step (k-group stride 2048 B), n halves 1024 B apart
-                    const uint64_t da = smem_desc_sw128(a_s + (uint32_t)(kk * 4096), 1024u, 2048u);
-                    for (int a = 0; a < p.nacc; a++) {
-                        // B: K-major, 16 k = 32 bytes into each 128-byte row, 8-row atoms 1024 B apart
-                        const uint64_t db =
-                            smem_desc_sw128(b_s + (uint32_t)(a * p.mma_n * 128) + (uint32_t)(kk * 32), 16u, 1024u);
-                        umma_bf16(tmem + (uint32_t)(a * p.mma_n), da, db, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+    };
+
+    pdl_launch_dependents();
+
+    if (warp == kWRaw) {
+        // ------------- raw weight producer: two k rows per lane per stage -------------
+        // weights do not depend on the preceding kernel: no griddepcontrol.wait
+        RingPos rp;
+        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+            const Unit un = unit_of(p, u);
+            const int64_t nv = min((int64_t)kGBN, p.N - un.n0);
+            bool ok = true;
+            for (int ks = un.kb; ks < un.ke; ks++, rp.next((uint32_t)p.sr)) {
+                const int s = (int)rp.idx;
+                if (rp.uses >= (uint32_t)p.sr && !wait(bar(RE + s), rp.phase ^ 1u)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t st_base = r_ring + (uint32_t)s * raw_stage;
+                if (p.raw_tma) {
+                    // rows of k have a 16-byte pitch: one 2D tile copy of 64 rows x raw_slot bytes
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(bar(RF + s), raw_stage);
+                        tma_load_2d(st_base, &tmw, (int)(((un.n0 >> 8) * B) & ~int64_t(15)), ks * kGBK, bar(RF + s));
                     }
-                }
-                umma_commit(st_empty(s));  // frees the stage once these MMAs have read it
-            }
-            umma_commit(acc_full);
-        }
-    } else {
-        // ---------------- dequant warps: W -> bf16 A tiles ----------------
-        const int dt = threadIdx.x - 64;  // 0..127
-        RawUnit cur[2], nxt[2];
-        auto unit_of = [&](int ks, int j, int64_t &vidx) -> bool {
-            const int u = dt + j * kGDeq;  // 0..255
-            const int kl = u >> 2, sb4 = u & 3;
-            const int64_t k = (int64_t)ks * kGBK + kl;
-            const int64_t n = n0 + 32 * sb4;
-            vidx = k * p.N + n;
-            return k < p.K && n < p.N;
-        };
-        for (int j = 0; j < 2; j++) {
-            int64_t vi;
-            const bool ok = unit_of(0, j, vi);
-            fetch_unit<QT>(p.w, vi, ok, cur[j]);
-        }
-        for (int ks = 0; ks < p.ksteps; ks++) {
-            const int s = ks % S;
-            // fetch the next step's raw bytes first (latency overlaps this step)
-            if (ks + 1 < p.ksteps) {
-                for (int j = 0; j < 2; j++) {
-                    int64_t vi;
-                    const bool ok = unit_of(ks + 1, j, vi);
-                    fetch_unit<QT>(p.w, vi, ok, nxt[j]);
-                }
-            }
-            if (ks >= S) g_wait(st_empty(s), (uint32_t)(((ks / S) - 1) & 1));
-            const uint32_t a_s = a_ring + (uint32_t)(s * kAStage);
+                } else {
+                    // lane l owns the byte ranges of rows l and l + 32; each row is
+                    // then copied by consecutive lanes (16 bytes each, coalesced)
+                    int64_t lo[2];
+                    uint32_t nb[2];
 #pragma unroll
-            for (int j = 0; j < 2; j++) {
+                    for (int h = 0; h < 2; h++) {
+                        const int64_t k = (int64_t)ks * kGBK + lane + 32 * h;
+                        lo[h] = 0;
+                        nb[h] = 0;
+                        if (k < p.K) {
+                            const int64_t v0 = k * p.N + un.n0;
+                            const int64_t blk0 = v0 >> 8, blk1 = (v0 + nv - 1) >> 8;
+                            lo[h] = (blk0 * B) & ~int64_t(15);
+                            nb[h] = (uint32_t)((blk1 + 1) * B - lo[h]);  // <= raw_slot <= 32 * 16
+                        }
+                    }
+                    const uint32_t c = (uint32_t)lane * 16u;
+#pragma unroll 4
+                    for (int r = 0; r < kGBK; r++) {
+                        const int64_t a = __shfl_sync(0xffffffffu, r < 32 ? lo[0] : lo[1], r & 31);
+                        const uint32_t n = __shfl_sync(0xffffffffu, r < 32 ? nb[0] : nb[1], r & 31);
+                        if (c < n) {
+                            const int64_t rem = p.w_bytes - (a + c);  // never reads past the end of w
+                            cp_async16(st_base + (uint32_t)(r * p.raw_slot) + c, p.w + a + c,
+                                       rem < 16 ? (uint32_t)rem : 16u);
+                        }
+                    }
+                    cp_async_arrive_noinc(bar(RF + s));
+                }
+            }
+            if (!ok) break;
+        }
+        // copies still in flight land before the CTA exits
+        const uint32_t it = rp.uses;
+        for (int s = 0; s < p.sr && it > 0; s++) {
+            const uint32_t uses = it / (uint32_t)p.sr + ((uint32_t)s < it % (uint32_t)p.sr ? 1u : 0u);
+            if (uses > 0) mbar_wait_bounded(bar(RF + s), (uses - 1) & 1u, kDrainNs);
+        }
+    } else if (warp == kWX) {
+        // ------------- X producer: TMA tiles of bf16 X -------------
+        if (lane == 0) {
+            RingPos rp;
+            pdl_wait();  // the bf16 copy of X comes from the preceding kernel
+            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+                const Unit un = unit_of(p, u);
+                bool ok = true;
+                for (int ks = un.kb; ks < un.ke; ks++, rp.next((uint32_t)p.sb)) {
+                    const int s = (int)rp.idx;
+                    if (rp.uses >= (uint32_t)p.sb && !wait(bar(BE + s), rp.phase ^ 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(bar(BF + s), b_stage);
+                    tma_load_2d(b_ring + (uint32_t)s * b_stage, &tmx, ks * kGBK, un.m0, bar(BF + s));
+                }
+                if (!ok) break;
+            }
+            const uint32_t it = rp.uses;
+            for (int s = 0; s < p.sb && it > 0; s++) {
+                const uint32_t uses = it / (uint32_t)p.sb + ((uint32_t)s < it % (uint32_t)p.sb ? 1u : 0u);
+                if (uses > 0) mbar_wait_bounded(bar(BF + s), (uses - 1) & 1u, kDrainNs);
+            }
+        }
+    } else if (warp == kWMma) {
+        // ------------- MMA issuer -------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_bf16_f32(kMmaM, p.bm);
+            // Descriptors of stage 0; a stage, a 16-k step or an MMA half is
+            // reached by adding (byte offset >> 4) to the start-address field
+            // (bits 0..13, no carry: shared addresses stay below 256 KB).
+            const uint64_t da0 = smem_desc_sw128(a_ring, 1024u, 2048u);
+            const uint64_t db0 = smem_desc_sw128(b_ring, 16u, 1024u);
+            RingPos pa, pb;
+            uint32_t lu = 0;
+            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, lu++) {
+                const Unit un = unit_of(p, u);
+                const uint32_t ab = p.nbuf == 2 ? (lu & 1u) : 0u, use = p.nbuf == 2 ? (lu >> 1) : lu;
+                if (use > 0 && !wait(bar(CE + ab), (use - 1) & 1u)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t dt0 = tmem + ab * (uint32_t)p.acc_stride, dt1 = dt0 + (uint32_t)p.bm;
+                bool ok = true;
+                for (int ks = un.kb; ks < un.ke; ks++, pa.next((uint32_t)p.sa), pb.next((uint32_t)p.sb)) {
+                    const int sa = (int)pa.idx, sb = (int)pb.idx;
+                    if (!wait(bar(AF + sa), pa.phase, true) || !wait(bar(BF + sb), pb.phase, true)) {
+                        ok = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint64_t da = da0 + (uint64_t)((uint32_t)(sa * kAStage) >> 4);
+                    const uint64_t db = db0 + (uint64_t)(((uint32_t)sb * b_stage) >> 4);
+                    const uint32_t acc0 = ks > un.kb ? 1u : 0u;
+                    // A half h (n 128h..128h+127): two k groups of 8 per 16-k step
+                    // (2048 B apart), 64-n halves 1024 B apart.  B: K-major, 16 k =
+                    // 32 bytes into each 128-byte row, 8-row atoms 1024 B apart.
+                    umma_bf16(dt0, da, db, idesc, acc0);
+                    umma_bf16(dt1, da + (kAHalf >> 4), db, idesc, acc0);
+#pragma unroll
+                    for (int kk = 1; kk < kGBK / 16; kk++) {
+                        umma_bf16(dt0, da + (uint64_t)(kk * 4096 >> 4), db + (uint64_t)(kk * 32 >> 4), idesc, 1u);
+                        umma_bf16(dt1, da + (uint64_t)((kAHalf + kk * 4096) >> 4), db + (uint64_t)(kk * 32 >> 4),
+                                  idesc, 1u);
+                    }
+                    umma_commit(bar(AE + sa));  // frees the stages once these MMAs have read them
+                    umma_commit(bar(BE + sb));
+                }
+                if (!ok) break;
+                umma_commit(bar(CF + ab));
+            }
+            // every MMA issued has completed before TMEM is released
+            umma_commit(bar(DR));
+            mbar_wait_bounded(bar(DR), 0, kDrainNs);
+        }
+    } else if (warp < kWEpi) {
+        // ------------- dequant warps: raw stage -> bf16 A tile -------------
+        const int dt = threadIdx.x - kWDeq * 32;  // 0..511
+        // the thread's unit in every stage: k row 8 * (dt / 64) + dt % 8, 32 n
+        // starting at 32 * ((dt / 8) % 8); the 8 lanes of a shared-memory phase
+        // take the 8 k rows of one swizzle atom, so their 16-byte A stores land
+        // in 8 different bank groups
+        const int kl = 8 * (dt >> 6) + (dt & 7), c8 = (dt >> 3) & 7;
+        const int h = c8 >> 2, c32 = c8 & 3, g = kl >> 3, kin = kl & 7;
+        uint32_t a_off[4];  // the unit's four 16-byte chunks within an A stage
+#pragma unroll
+        for (int c4 = 0; c4 < 4; c4++) {
+            const int nl = 32 * c32 + 8 * c4;  // first n of the chunk within the MMA half
+            const int hh = nl >> 6, c = (nl & 63) >> 3;
+            a_off[c4] = (uint32_t)(h * kAHalf + (g * 2 + hh) * 1024 + kin * 128 + ((c ^ kin) << 4));
+        }
+        RingPos pr, pa;
+        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+            const Unit un = unit_of(p, u);
+            const bool n_ok = un.n0 + 32 * c8 < p.N;
+            // TMA stages: one block per k row at the row's slot plus the block's lead
+            const uint32_t tma_off = (uint32_t)(kl * p.raw_slot) + (uint32_t)(((un.n0 >> 8) * B) & 15);
+            bool ok = true;
+            for (int ks = un.kb; ks < un.ke; ks++, pr.next((uint32_t)p.sr), pa.next((uint32_t)p.sa)) {
+                const int sr = (int)pr.idx, sa = (int)pa.idx;
+                if (!wait(bar(RF + sr), pr.phase, true)) {
+                    ok = false;
+                    break;
+                }
+                RawUnit ru;
+                {
+                    const int64_t k = (int64_t)ks * kGBK + kl;
+                    const bool valid = n_ok && k < p.K;
+                    uint32_t blk = 0, within = 0;
+                    if (valid) {
+                        if (p.raw_tma) {
+                            blk = r_ring + (uint32_t)sr * raw_stage + tma_off;
+                            within = 32u * (uint32_t)c8;
+                        } else {
+                            const int64_t v0 = k * p.N + un.n0;
+                            const int64_t blk0 = v0 >> 8;
+                            const int64_t vi = v0 + 32 * c8;
+                            const uint32_t lead = (uint32_t)((blk0 * B) & 15);
+                            blk = r_ring + (uint32_t)sr * raw_stage + (uint32_t)(kl * p.raw_slot) + lead +
+                                  (uint32_t)((vi >> 8) - blk0) * B;
+                            within = (uint32_t)(vi & 255);
+                        }
+                    }
+                    load_unit<QT>(blk, within, valid, ru);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(RE + sr));
                 uint32_t wv[16];
-                decode_unit_bf16<QT>(cur[j], wv);
-                const int u = dt + j * kGDeq;
-                const int kl = u >> 2, sb4 = u & 3;
-                const int g = kl >> 3, kin = kl & 7;
+                decode_unit_bf16<QT>(ru, wv);  // before the wait: overlaps the MMAs still reading the stage
+                if (pa.uses >= (uint32_t)p.sa && !wait(bar(AE + sa), pa.phase ^ 1u, true)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t a_s = a_ring + (uint32_t)(sa * kAStage);
 #pragma unroll
-                for (int c4 = 0; c4 < 4; c4++) {
-                    const int nl = 32 * sb4 + 8 * c4;  // first n of this 16-byte chunk
-                    const int h = nl >> 6, c = (nl & 63) >> 3;
-                    const uint32_t addr =
-                        a_s + (uint32_t)((g * 2 + h) * 1024 + kin * 128 + ((c ^ kin) << 4));
-                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(wv[4 * c4]),
+                for (int c4 = 0; c4 < 4; c4++)
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a_s + a_off[c4]), "r"(wv[4 * c4]),
                                  "r"(wv[4 * c4 + 1]), "r"(wv[4 * c4 + 2]), "r"(wv[4 * c4 + 3])
                                  : "memory");
-                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(AF + sa));
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(a_full(s));
-            cur[0] = nxt[0];
-            cur[1] = nxt[1];
+            if (!ok) break;
         }
-
-        // ---------------- epilogue: TMEM -> Y ----------------
-        g_wait(acc_full, 0);
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        const int q = warp & 3;  // TMEM lane quarter this warp may read
-        const int64_t n = n0 + 32 * q + lane;
-        for (int a = 0; a < p.nacc; a++) {
-            for (int c = 0; c < p.mma_n / 32; c++) {
-                uint32_t r[32];
-                const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * p.mma_n + 32 * c);
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                      "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-                      "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-                      "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-                      "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                    : "r"(taddr));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (n < p.N) {
-                    const int64_t mb = m0 + a * p.mma_n + 32 * c;
-#pragma unroll
-                    for (int j = 0; j < 32; j++)
-                        if (mb + j < p.M) p.y[(mb + j) * p.N + n] = __uint_as_float(r[j]);
-                }
+        // help drain this CTA's last unit
+        const int nunits = p.units > (int)blockIdx.x ? (p.units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        if (nunits > 0 && !*abort_flag) {
+            const uint32_t lu = (uint32_t)(nunits - 1);
+            const uint32_t ab = p.nbuf == 2 ? (lu & 1u) : 0u;
+            if (wait(bar(CF + ab), (p.nbuf == 2 ? (lu >> 1) : lu) & 1u)) {
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                pdl_wait();  // Y may still be read by the preceding kernel
+                const Unit un = unit_of(p, (int)blockIdx.x + (int)lu * (int)gridDim.x);
+                drain(un, ab, warp & 3, 1 + (warp - kWDeq) / 4, 1 + kNDeq / 4);
             }
+        }
+    } else {
+        // ------------- epilogue: TMEM -> Y (or the split's partials) -------------
+        pdl_wait();  // Y may still be read by the preceding kernel
+        const int q = warp & 3;  // TMEM lane quarter this warp may read
+        uint32_t lu = 0;
+        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, lu++) {
+            const Unit un = unit_of(p, u);
+            const uint32_t ab = p.nbuf == 2 ? (lu & 1u) : 0u;
+            if (!wait(bar(CF + ab), (p.nbuf == 2 ? (lu >> 1) : lu) & 1u)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            // the dequant warps help with the CTA's last unit (they are idle by then)
+            const bool last = u + (int)gridDim.x >= p.units;
+            drain(un, ab, q, 0, last ? 1 + kNDeq / 4 : 1);
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(CE + ab));
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kWMma) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols));
     }
@@ -380,6 +623,24 @@ __global__ void __launch_bounds__(256) x_to_bf16_kernel(const float *__restrict_
          i += (int64_t)gridDim.x * blockDim.x) {
         const float2 v = reinterpret_cast<const float2 *>(x)[i];
         xb[i] = bf16x2(v.x, v.y);
+    }
+    pdl_launch_dependents();
+}
+
+// Y = sum over the k splits of the partial products, in split order.
+__global__ void __launch_bounds__(256) split_sum_kernel(const float4 *__restrict__ part, float4 *__restrict__ y,
+                                                        int64_t n4, int splits) {
+    pdl_wait();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        float4 a = __ldcs(part + i);
+        for (int s = 1; s < splits; s++) {
+            const float4 b = __ldcs(part + (int64_t)s * n4 + i);
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        y[i] = a;
     }
     pdl_launch_dependents();
 }
@@ -404,49 +665,113 @@ static EncodeTiledFn encode_fn() {
 }
 
 struct GemmPlan {
-    int mma_n, nacc, stages, ksteps, tmem_cols;
-    int64_t xb_bytes;  // bf16 copy of X in the workspace
+    int bm, m_tiles, n_tiles, splits, units, ksteps, kper;
+    int sr, sa, sb, raw_slot, raw_tma, tmem_cols, nbuf;
+    int64_t xb_bytes, part_bytes;  // workspace after the counter head: bf16 X, then the split partials
     size_t smem;
-    dim3 grid;
+    int grid;
 };
 
-static GemmPlan gemm_plan(const GemvShape &s) {
+static int block_bytes_of(int qt) { return qt == kQ4K ? 144 : qt == kQ5K ? 176 : 210; }
+
+// Cost model in SM cycles for one 256 n x bm m unit and one 64-k step: the
+// two MMAs 128 x bm x 16 of each 16-k step take about bm / 2 cycles each
+// (4 * bm per step); dequantizing 256 x 64 values takes about kDeqCycles; the
+// SM pulls the raw stage and the X tile out of L2 at about kL2Bytes per cycle.
+// Units run in waves of `sms`; the epilogue writes 256 x bm floats per unit at
+// about kYBytes per cycle and is hidden behind the next unit only when two
+// accumulator buffers fit in TMEM (4 * bm <= 512 columns).  Split partials
+// cost a write and a read of splits * M * N floats.
+static GemmPlan gemm_plan(const GemvShape &s, int sms) {
+    constexpr double kDeqCycles = 600.0, kL2Bytes = 55.0, kYBytes = 40.0, kUnitOverhead = 1500.0,
+                     kBytesPerCycle = 3000.0;
     GemmPlan g{};
-    if (s.M >= 512) {
-        g.mma_n = 256;
-        g.nacc = 2;
-    } else if (s.M > 256) {
-        g.mma_n = (int)((((s.M + 1) / 2) + 31) / 32 * 32);
-        g.nacc = 2;
-    } else {
-        g.mma_n = (int)((s.M + 31) / 32 * 32);
-        g.nacc = 1;
-    }
-    const int cols = g.mma_n * g.nacc;
-    g.tmem_cols = 32;
-    while (g.tmem_cols < cols) g.tmem_cols <<= 1;
+    const int B = block_bytes_of(s.qtype);
+    // k rows whose byte pitch is a multiple of 16 (N % 256 == 0 and N/256*B % 16
+    // == 0) are TMA-copyable as a 2D tile: one block per row (plus the lead of
+    // a 2-byte aligned Q6_K block); otherwise up to two blocks plus the lead.
+    g.raw_tma = (s.N % 256 == 0) && ((s.N / 256 * B) % 16 == 0);
+    if (g.raw_tma) g.raw_slot = (B % 16 == 0) ? B : ((B + 14 + 15) & ~15);
+    else g.raw_slot = (2 * B + 15 + 15) & ~15;
+    const double raw_stage = (double)kGBK * g.raw_slot;
     g.ksteps = (int)((s.K + kGBK - 1) / kGBK);
-    const size_t stage = (size_t)kAStage + (size_t)g.nacc * g.mma_n * 128;
-    g.stages = 4;
-    while (g.stages > 2 && 1024 + g.stages * stage + 256 > (size_t)220 * 1024) g.stages--;
-    g.smem = 1024 + g.stages * stage + 256;
+    g.n_tiles = (int)((s.N + kGBN - 1) / kGBN);
+    double best = 1e300;
+    for (int bm = 16; bm <= 256; bm += 16) {
+        const int64_t mt = (s.M + bm - 1) / bm;
+        if (bm > 16 && (s.M + bm - 17) / (bm - 16) == mt) continue;  // bm - 16 gives the same m tiles
+        const int64_t tiles = mt * g.n_tiles;
+        const double step = std::max({4.0 * bm, kDeqCycles, (raw_stage + 128.0 * bm) / kL2Bytes});
+        const double epi = (double)kGBN * bm * 4.0 / kYBytes;
+        const bool two_bufs = 4 * bm <= 512;
+        for (int sp : {1, 2, 3, 4, 6, 8}) {
+            if (sp > g.ksteps) break;
+            const int kper = (g.ksteps + sp - 1) / sp;
+            if ((int64_t)(sp - 1) * kper >= g.ksteps) continue;  // every split gets k steps
+            const int64_t units = tiles * sp;
+            const int64_t waves = (units + sms - 1) / sms;
+            double cost = (double)waves * (kper * step + kUnitOverhead) + (two_bufs ? epi : (double)waves * epi);
+            if (sp > 1) cost += 2.0 * sp * (double)s.M * (double)s.N * 4.0 / kBytesPerCycle + kUnitOverhead;
+            if (cost < best * 0.999) {
+                best = cost;
+                g.bm = bm;
+                g.m_tiles = (int)mt;
+                g.splits = sp;
+                g.kper = kper;
+                g.units = (int)units;
+            }
+        }
+    }
+    g.nbuf = 4 * g.bm <= 512 ? 2 : 1;
+    g.grid = std::min(g.units, sms);
+    const size_t a_st = kAStage, b_st = (size_t)g.bm * 128, r_st = (size_t)kGBK * g.raw_slot;
+    const size_t fixed = 1024 + 8 * (6 * kMaxStages + 8) + 16;
+    const size_t budget = 227 * 1024 - fixed;
+    // Ring depths: every stage makes a round trip through several mbarrier
+    // hand-offs (about 4000 cycles for the A ring: dequant, MMA issue, MMA
+    // execution, commit, dequant again), so two stages leave the tensor cores
+    // idle half the time.  Grow A, then X, then the raw weights, round-robin.
+    g.sa = 2;
+    g.sb = 2;
+    g.sr = 2;
+    auto used = [&]() { return g.sa * a_st + g.sb * b_st + g.sr * r_st; };
+    for (bool grown = true; grown;) {
+        grown = false;
+        if (g.sa < 4 && used() + a_st <= budget) {
+            g.sa++;
+            grown = true;
+        }
+        if (g.sb < 4 && used() + b_st <= budget) {
+            g.sb++;
+            grown = true;
+        }
+        if (g.sr < 6 && used() + r_st <= budget) {
+            g.sr++;
+            grown = true;
+        }
+    }
+    g.smem = fixed + used();
+    g.tmem_cols = 32;
+    while (g.tmem_cols < g.nbuf * 2 * g.bm) g.tmem_cols <<= 1;
     g.xb_bytes = ((s.M * s.K * 2) + 255) & ~int64_t(255);
-    g.grid = dim3((unsigned)((s.N + kGBN - 1) / kGBN), (unsigned)((s.M + (int64_t)cols - 1) / cols));
+    g.part_bytes = g.splits > 1 ? (int64_t)g.splits * s.M * s.N * 4 : 0;
     return g;
 }
 
-size_t gemm_workspace_bytes(const GemvShape &s) {
+size_t gemm_workspace_bytes(const GemvShape &s, int device) {
     if (s.N % 32 != 0) return 0;
-    return (size_t)gemm_plan(s).xb_bytes;
+    const GemmPlan g = gemm_plan(s, device_sm_count(device));
+    return kWorkspaceCounterHead + (size_t)(g.xb_bytes + g.part_bytes);
 }
 
 template <int QT>
-static cudaError_t launch_gemm(const CUtensorMap &tm, const GemmParams &gp, const GemmPlan &g, cudaStream_t st) {
+static cudaError_t launch_gemm(const CUtensorMap &tm, const CUtensorMap &tw, const GemmParams &gp, const GemmPlan &g,
+                               cudaStream_t st) {
     auto kern = gemm_kernel<QT>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = g.grid;
+    cfg.gridDim = dim3((unsigned)g.grid);
     cfg.blockDim = dim3(kGThreads);
     cfg.dynamicSmemBytes = g.smem;
     cfg.stream = st;
@@ -455,12 +780,25 @@ static cudaError_t launch_gemm(const CUtensorMap &tm, const GemmParams &gp, cons
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, tm, gp);
+    return cudaLaunchKernelEx(&cfg, kern, tm, tw, gp);
 }
 
-int gemm_launch(const GemvShape &s, const void *w, const float *x, float *y, void *ws, size_t ws_bytes,
-                cudaStream_t stream, int device) {
-    (void)device;
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), int grid, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)std::max(grid, 1));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+int gemm_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
+                size_t ws_bytes, cudaStream_t stream, int device) {
     if (s.N % 32 != 0) {
         set_error("the tensor-core GEMM needs N %% 32 == 0 (got N=%lld)", (long long)s.N);
         return 2;
@@ -474,9 +812,11 @@ int gemm_launch(const GemvShape &s, const void *w, const float *x, float *y, voi
         set_error("the tensor-core GEMM needs x 8-byte aligned");
         return 3;
     }
-    const GemmPlan g = gemm_plan(s);
-    if (ws == nullptr || ws_bytes < (size_t)g.xb_bytes) {
-        set_error("gemm needs a workspace of %lld bytes (got %zu)", (long long)g.xb_bytes, ws_bytes);
+    const int sms = device_sm_count(device);
+    const GemmPlan g = gemm_plan(s, sms);
+    const size_t need = kWorkspaceCounterHead + (size_t)(g.xb_bytes + g.part_bytes);
+    if (ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) {
+        set_error("gemm needs a 256-byte aligned workspace of %zu bytes (got %zu)", need, ws_bytes);
         return 4;
     }
     EncodeTiledFn enc = encode_fn();
@@ -484,31 +824,24 @@ int gemm_launch(const GemvShape &s, const void *w, const float *x, float *y, voi
         set_error("cuTensorMapEncodeTiled is not available from the driver");
         return 5;
     }
-    uint32_t *xb = static_cast<uint32_t *>(ws);
+    // after the GEMV's counter head, which this call leaves untouched
+    uint32_t *xb = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) + kWorkspaceCounterHead);
+    float *part = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kWorkspaceCounterHead + g.xb_bytes);
     // 1. X -> bf16
     {
         const int64_t npairs = s.M * s.K / 2;
-        const int grid = (int)std::min<int64_t>((npairs + 255) / 256, (int64_t)device_sm_count(device) * 8);
-        cudaLaunchConfig_t cfg{};
-        cfg.gridDim = dim3((unsigned)std::max(grid, 1));
-        cfg.blockDim = dim3(256);
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, x_to_bf16_kernel, x, xb, npairs);
+        const int grid = (int)std::min<int64_t>((npairs + 255) / 256, (int64_t)sms * 8);
+        cudaError_t e = launch_pdl(x_to_bf16_kernel, grid, stream, x, xb, npairs);
         if (e != cudaSuccess) {
             set_error("x to bf16 launch failed: %s", cudaGetErrorString(e));
             return 5;
         }
     }
-    // 2. tensor map over the bf16 X: dims {K, M}, box {64, mma_n}, 128-byte swizzle
+    // 2. tensor map over the bf16 X: dims {K, M}, box {64, bm}, 128-byte swizzle
     CUtensorMap tm;
     const cuuint64_t dims[2] = {(cuuint64_t)s.K, (cuuint64_t)s.M};
     const cuuint64_t strides[1] = {(cuuint64_t)(s.K * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)kGBK, (cuuint32_t)g.mma_n};
+    const cuuint32_t box[2] = {(cuuint32_t)kGBK, (cuuint32_t)g.bm};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -517,26 +850,61 @@ int gemm_launch(const GemvShape &s, const void *w, const float *x, float *y, voi
         set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
         return 5;
     }
+    // tensor map over the weight bytes as [K rows][N/256*B bytes], box {raw_slot, 64}
+    CUtensorMap tw = tm;  // unused unless raw_tma
+    if (g.raw_tma) {
+        const int B = block_bytes_of(s.qtype);
+        const cuuint64_t wd[2] = {(cuuint64_t)(s.N / 256 * B), (cuuint64_t)s.K};
+        const cuuint64_t ws_[1] = {(cuuint64_t)(s.N / 256 * B)};
+        const cuuint32_t wbox[2] = {(cuuint32_t)g.raw_slot, (cuuint32_t)kGBK};
+        r = enc(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), wd, ws_, wbox, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            set_error("cuTensorMapEncodeTiled (weights) failed (%d)", (int)r);
+            return 5;
+        }
+    }
     GemmParams gp{};
     gp.w = static_cast<const uint8_t *>(w);
-    gp.y = y;
+    gp.w_bytes = w_bytes;
+    gp.y = g.splits > 1 ? part : y;
     gp.K = s.K;
     gp.N = s.N;
     gp.M = s.M;
-    gp.mma_n = g.mma_n;
-    gp.nacc = g.nacc;
-    gp.stages = g.stages;
+    gp.bm = g.bm;
+    gp.m_tiles = g.m_tiles;
+    gp.splits = g.splits;
+    gp.units = g.units;
     gp.ksteps = g.ksteps;
+    gp.kper = g.kper;
+    gp.sr = g.sr;
+    gp.sa = g.sa;
+    gp.sb = g.sb;
+    gp.raw_slot = g.raw_slot;
+    gp.raw_tma = g.raw_tma;
     gp.tmem_cols = g.tmem_cols;
+    gp.acc_stride = 2 * g.bm;
+    gp.nbuf = g.nbuf;
     cudaError_t e;
     switch (s.qtype) {
-    case kQ4K: e = launch_gemm<kQ4K>(tm, gp, g, stream); break;
-    case kQ5K: e = launch_gemm<kQ5K>(tm, gp, g, stream); break;
-    default: e = launch_gemm<kQ6K>(tm, gp, g, stream); break;
+    case kQ4K: e = launch_gemm<kQ4K>(tm, tw, gp, g, stream); break;
+    case kQ5K: e = launch_gemm<kQ5K>(tm, tw, gp, g, stream); break;
+    default: e = launch_gemm<kQ6K>(tm, tw, gp, g, stream); break;
     }
     if (e != cudaSuccess) {
         set_error("gemm launch failed: %s", cudaGetErrorString(e));
         return 5;
+    }
+    if (g.splits > 1) {
+        const int64_t n4 = s.M * s.N / 4;
+        const int grid = (int)std::min<int64_t>((n4 + 255) / 256, (int64_t)sms * 8);
+        e = launch_pdl(split_sum_kernel, grid, stream, reinterpret_cast<const float4 *>(part),
+                       reinterpret_cast<float4 *>(y), n4, g.splits);
+        if (e != cudaSuccess) {
+            set_error("split-K sum launch failed: %s", cudaGetErrorString(e));
+            return 5;
+        }
     }
     return 0;
 }

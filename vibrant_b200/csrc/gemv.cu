@@ -69,12 +69,6 @@ struct GemvParams {
 __device__ __forceinline__ void set_status(int code) { atomicExch(&g_gemv_status, code); }
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
-// Float from the byte in lane j of v via the 2^23 exponent trick.
-template <int J>
-__device__ __forceinline__ float byte_as_magic(uint32_t v) {
-    return __uint_as_float(prmt(v, 0x4B000000u, 0x7540u | J));
-}
-
 // Q6_K: acc[m] += a[m] * (q - 32) with a = x * (d * scale).
 template <int MR, int NP>
 __device__ __forceinline__ void accum_chunk_scaled(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
@@ -562,6 +556,10 @@ static Plan make_plan(const GemvShape &s, int device) {
     else if (s.M <= 4) { pl.mr = 4; pl.vpt = 8; }
     else { pl.mr = 8; pl.vpt = 8; }
     pl.tn = 32 * pl.vpt;
+    if ((s.N + pl.tn - 1) / pl.tn > (int64_t)(kWorkspaceCounterHead / 4)) {
+        pl.generic = true;  // more tile counters than the workspace head holds
+        return pl;
+    }
     pl.ntiles = (int)((s.N + pl.tn - 1) / pl.tn);
     const int64_t rows_total = (int64_t)pl.ntiles * s.K;
     const int sms = device_sm_count(device);

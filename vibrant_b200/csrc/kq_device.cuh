@@ -73,11 +73,23 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
     return d;
 }
+// The same operations on float2 through the compiler's builtins, which keep
+// each pair in an aligned register pair without moves around every use.
+__device__ __forceinline__ float2 f2add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 f2fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 f2mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     uint32_t r;
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
     return r;
+}
+
+// 2^23 + (byte in lane J of v), as a float: a byte permute into the exponent
+// of 2^23; subtracting 2^23 then gives the byte's value exactly.
+template <int J>
+__device__ __forceinline__ float byte_as_magic(uint32_t v) {
+    return __uint_as_float(prmt(v, 0x4B000000u, 0x7540u | J));
 }
 
 // ---- shared memory access -----------------------------------------------
@@ -160,12 +172,55 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     }
 }
 
+// Bounded wait that polls instead of sleeping: for hand-offs on the
+// critical path of a pipeline, where the time a suspended thread takes to
+// resume would be paid on every step.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && globaltimer_ns() - t0 > budget_ns) return false;
+    }
+}
+
+// Non-blocking test of a phase (mbarrier.test_wait never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait that polls with test_wait: no suspension, so the thread sees
+// the phase complete within a few cycles (a suspended try_wait can take far
+// longer to resume).  For hand-offs on the per-step critical path.
+__device__ __forceinline__ bool mbar_wait_poll(uint32_t bar, uint32_t parity, uint64_t budget_ns) {
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((i & 255u) == 0 && globaltimer_ns() - t0 > budget_ns) return false;
+    }
+}
+
 // One-dimensional bulk copy global -> shared (no multicast), completing
 // `bytes` of transaction count on `bar`.  dst, src and bytes are multiples of 16.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+// 16-byte cp.async global -> shared that reads only `src_bytes` (1..16) of
+// the source and zero-fills the rest; src and dst 16-byte aligned.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// Arrive on `bar` once every cp.async this thread issued so far has landed
+// (the arrival is part of the barrier's expected count).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 // Programmatic dependent launch: wait for the preceding grid's memory, and

@@ -14,6 +14,13 @@ cudaError_t dequantize_f32(int qtype, const void *w, int64_t nblocks, float *out
 cudaError_t dequant_transpose_f32(int qtype, const void *w, int64_t K, int64_t N, float *out, cudaStream_t s,
                                   int device);
 
+// Layout of a caller's matmul workspace: the first kWorkspaceCounterHead bytes
+// hold the GEMV's split-K tile counters, which every call leaves at zero (the
+// GEMV fast path serves at most kWorkspaceCounterHead / 4 tiles); every other
+// kernel keeps its scratch after them, so any call may follow any other on
+// one workspace.
+constexpr size_t kWorkspaceCounterHead = 64 * 1024;
+
 // fp32 CUDA-core GEMV (1 <= M <= 8).
 struct GemvShape {
     int qtype;
@@ -31,9 +38,9 @@ int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, cons
 int gemv_read_status();
 
 // bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
-size_t gemm_workspace_bytes(const GemvShape &s);
-int gemm_launch(const GemvShape &s, const void *w, const float *x, float *y, void *ws, size_t ws_bytes,
-                cudaStream_t stream, int device);
+size_t gemm_workspace_bytes(const GemvShape &s, int device);
+int gemm_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
+                size_t ws_bytes, cudaStream_t stream, int device);
 int gemm_read_status();  // reads and clears this TU's device status word (synchronous)
 
 void set_error(const char *fmt, ...);
