@@ -509,26 +509,38 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         }
     } else if (warp < kWEpi) {
         // ------------- dequant warps: raw stage -> bf16 A tile -------------
-        const int dt = threadIdx.x - kWDeq * 32;  // 0..511
-        // the thread's unit in every stage: k row 8 * (dt / 64) + dt % 8, 32 n
-        // starting at 32 * ((dt / 8) % 8); the 8 lanes of a shared-memory phase
-        // take the 8 k rows of one swizzle atom, so their 16-byte A stores land
-        // in 8 different bank groups
-        const int kl = 8 * (dt >> 6) + (dt & 7), c8 = (dt >> 3) & 7;
-        const int h = c8 >> 2, c32 = c8 & 3, g = kl >> 3, kin = kl & 7;
-        uint32_t a_off[4];  // the unit's four 16-byte chunks within an A stage
+        constexpr int UPT = kGBK * (kGBN / 32) / (kNDeq * 32);  // units per thread per stage
+        const int dt = threadIdx.x - kWDeq * 32;
+        // unit j of the thread in every stage: uu = dt + j * 32 * kNDeq is k row
+        // 8 * (uu / 64) + uu % 8 and 32 n starting at 32 * ((uu / 8) % 8); the 8
+        // lanes of a shared-memory phase take the 8 k rows of one swizzle atom,
+        // so their 16-byte A stores land in 8 different bank groups
+        int kl[UPT], c8[UPT];
+        uint32_t a_off[UPT][4];  // the unit's four 16-byte chunks within an A stage
 #pragma unroll
-        for (int c4 = 0; c4 < 4; c4++) {
-            const int nl = 32 * c32 + 8 * c4;  // first n of the chunk within the MMA half
-            const int hh = nl >> 6, c = (nl & 63) >> 3;
-            a_off[c4] = (uint32_t)(h * kAHalf + (g * 2 + hh) * 1024 + kin * 128 + ((c ^ kin) << 4));
+        for (int j = 0; j < UPT; j++) {
+            const int uu = dt + j * 32 * kNDeq;
+            kl[j] = 8 * (uu >> 6) + (uu & 7);
+            c8[j] = (uu >> 3) & 7;
+            const int h = c8[j] >> 2, c32 = c8[j] & 3, g = kl[j] >> 3, kin = kl[j] & 7;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; c4++) {
+                const int nl = 32 * c32 + 8 * c4;  // first n of the chunk within the MMA half
+                const int hh = nl >> 6, c = (nl & 63) >> 3;
+                a_off[j][c4] = (uint32_t)(h * kAHalf + (g * 2 + hh) * 1024 + kin * 128 + ((c ^ kin) << 4));
+            }
         }
         RingPos pr, pa;
         for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
             const Unit un = unit_of(p, u);
-            const bool n_ok = un.n0 + 32 * c8 < p.N;
-            // TMA stages: one block per k row at the row's slot plus the block's lead
-            const uint32_t tma_off = (uint32_t)(kl * p.raw_slot) + (uint32_t)(((un.n0 >> 8) * B) & 15);
+            bool n_ok[UPT];
+            uint32_t tma_off[UPT];
+#pragma unroll
+            for (int j = 0; j < UPT; j++) {
+                n_ok[j] = un.n0 + 32 * c8[j] < p.N;
+                // TMA stages: one block per k row at the row's slot plus the block's lead
+                tma_off[j] = (uint32_t)(kl[j] * p.raw_slot) + (uint32_t)(((un.n0 >> 8) * B) & 15);
+            }
             bool ok = true;
             for (int ks = un.kb; ks < un.ke; ks++, pr.next((uint32_t)p.sr), pa.next((uint32_t)p.sa)) {
                 const int sr = (int)pr.idx, sa = (int)pa.idx;
@@ -536,41 +548,47 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                     ok = false;
                     break;
                 }
-                RawUnit ru;
-                {
-                    const int64_t k = (int64_t)ks * kGBK + kl;
-                    const bool valid = n_ok && k < p.K;
+                const uint32_t st_r = r_ring + (uint32_t)sr * raw_stage;
+                RawUnit ru[UPT];
+#pragma unroll
+                for (int j = 0; j < UPT; j++) {
+                    const int64_t k = (int64_t)ks * kGBK + kl[j];
+                    const bool valid = n_ok[j] && k < p.K;
                     uint32_t blk = 0, within = 0;
                     if (valid) {
                         if (p.raw_tma) {
-                            blk = r_ring + (uint32_t)sr * raw_stage + tma_off;
-                            within = 32u * (uint32_t)c8;
+                            blk = st_r + tma_off[j];
+                            within = 32u * (uint32_t)c8[j];
                         } else {
                             const int64_t v0 = k * p.N + un.n0;
                             const int64_t blk0 = v0 >> 8;
-                            const int64_t vi = v0 + 32 * c8;
+                            const int64_t vi = v0 + 32 * c8[j];
                             const uint32_t lead = (uint32_t)((blk0 * B) & 15);
-                            blk = r_ring + (uint32_t)sr * raw_stage + (uint32_t)(kl * p.raw_slot) + lead +
-                                  (uint32_t)((vi >> 8) - blk0) * B;
+                            blk = st_r + (uint32_t)(kl[j] * p.raw_slot) + lead + (uint32_t)((vi >> 8) - blk0) * B;
                             within = (uint32_t)(vi & 255);
                         }
                     }
-                    load_unit<QT>(blk, within, valid, ru);
+                    load_unit<QT>(blk, within, valid, ru[j]);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(RE + sr));
-                uint32_t wv[16];
-                decode_unit_bf16<QT>(ru, wv);  // before the wait: overlaps the MMAs still reading the stage
+                uint32_t wv[UPT][16];
+#pragma unroll
+                for (int j = 0; j < UPT; j++)
+                    decode_unit_bf16<QT>(ru[j], wv[j]);  // before the wait: overlaps the MMAs still reading the stage
                 if (pa.uses >= (uint32_t)p.sa && !wait(bar(AE + sa), pa.phase ^ 1u, true)) {
                     ok = false;
                     break;
                 }
                 const uint32_t a_s = a_ring + (uint32_t)(sa * kAStage);
 #pragma unroll
-                for (int c4 = 0; c4 < 4; c4++)
-                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a_s + a_off[c4]), "r"(wv[4 * c4]),
-                                 "r"(wv[4 * c4 + 1]), "r"(wv[4 * c4 + 2]), "r"(wv[4 * c4 + 3])
-                                 : "memory");
+                for (int j = 0; j < UPT; j++)
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; c4++)
+                        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a_s + a_off[j][c4]),
+                                     "r"(wv[j][4 * c4]), "r"(wv[j][4 * c4 + 1]), "r"(wv[j][4 * c4 + 2]),
+                                     "r"(wv[j][4 * c4 + 3])
+                                     : "memory");
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(AF + sa));
