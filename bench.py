@@ -7,8 +7,9 @@ One step = one pass of the hot path over one batch of synthetic input: the
 Q6_K vocabulary projection (LM head) GEMV, x fp32 [1, 2048] . W [2048 x 151936]
 Q6_K -> logits fp32 [1, 151936] (255,868,416 algorithmic bytes: weight +
 x + y).  With N > 1 GPUs (one process per GPU under torchrun) the weight is
-row-sharded by output columns, each rank runs the GEMV on its shard and an
-NCCL all-gather assembles the logits on every rank (strong scaling).
+row-sharded by output columns and each rank runs one kernel that computes
+its shard and stores it into every rank's logits buffer through peer memory
+over NVLink (`--gather nccl` uses an NCCL all-gather instead; strong scaling).
 
 Rank 0 prints one JSON line.  `value` is GB/s of algorithmic bytes for the
 whole job with the weight resident in HBM; `e2e` is the same metric through
@@ -43,6 +44,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-secondary", action="store_true", help="skip the extra workloads at N == 1")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: all-gather fused into the GEMV through peer memory, or an NCCL all-gather")
     return ap.parse_args()
 
 
@@ -187,18 +190,6 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-# --------------------------------------------------------------------------------------------
-def shard_columns(N: int, world: int):
-    """Equal-width column shards (multiples of 32); the last one may be short."""
-    width = ((N + world - 1) // world + 31) // 32 * 32
-    bounds = []
-    for r in range(world):
-        lo = min(N, r * width)
-        hi = min(N, lo + width)
-        bounds.append((lo, hi))
-    return width, bounds
-
-
 def time_gemv_graph(torch, vt, weights, x, outs, steps, warmup, stream):
     """CUDA-event time of `steps` launches (rotating weight copies) replayed
     from one CUDA graph; returns (seconds per launch, graph)."""
@@ -285,21 +276,35 @@ def run_ours(args):
     hbm_peak, bf16_peak, peak_kind = peaks()
     wl = synth.WORKLOADS[WORKLOAD]
     qt, K, N = wl["qtype"], wl["K"], wl["N"]
-    width, bounds = shard_columns(N, world)
+    width, bounds = vt.shard_columns(N, world)
     lo, hi = bounds[rank]
-    n_local = width  # every rank computes a full-width shard; the last one's tail is padding
-    # the shard's weight: a canonical [K, width] Q6_K matrix with the workload's distribution
-    wq = synth.weights(qt, K, n_local, seed=wl["seed"] * 1000 + rank)
-    w0 = vt.QuantWeight(qt, K, n_local, wq, device=dev)
-    w1 = vt.QuantWeight(qt, K, n_local, w0.buf.clone(), device=dev)
-    weights = [w0, w1]     # two copies: 2 x 255 MB at N == 1, larger than the 126 MB L2
+    peer = world > 1 and args.gather == "peer"
+    if world == 1 or peer:
+        # the whole [K, N] weight (every rank keeps it; a rank reads only its columns)
+        n_local = N if world == 1 else hi - lo
+        wq = synth.weights(qt, K, N, seed=wl["seed"])
+        w0 = vt.QuantWeight(qt, K, N, wq, device=dev)
+    else:
+        # NCCL baseline: a canonical [K, width] shard per rank (the last rank's tail is padding)
+        n_local = width
+        wq = synth.weights(qt, K, n_local, seed=wl["seed"] * 1000 + rank)
+        w0 = vt.QuantWeight(qt, K, n_local, wq, device=dev)
+    w1 = vt.QuantWeight(w0.qtype, w0.K, w0.N, w0.buf.clone(), device=dev)
+    weights = [w0, w1]     # two copies: 2 x 255 MB per GPU, larger than the 126 MB L2
     x_host = torch.from_numpy(synth.activations(1, K, seed=11)).pin_memory()
     x = x_host.to(dev)
-    y_local = torch.empty(1, n_local, device=dev)
+    y_local = torch.empty(1, n_local if not (world == 1) else N, device=dev)
     y_full = torch.empty(world * n_local, device=dev)
     stream = torch.cuda.Stream(device=dev)
+    gather = None
+    if peer:
+        gather = vt.PeerGather(pg.group.WORLD, rank, world, local, N, m_max=1)
+        y_full = gather.out[0]
 
     def step(wt):
+        if gather is not None:   # one kernel: shard GEMV + stores into every rank's logits
+            gather.gemv(x, wt, stream=stream)
+            return
         vt.matmul(x, wt, out=y_local, stream=stream)
         if pg is not None:
             with torch.cuda.stream(stream):
@@ -341,13 +346,32 @@ def run_ours(args):
         dt = float(t.item())
     del g
 
-    # kernel-only timing of the GEMV alone (for the roofline of the dominant kernel)
-    outs = [y_local]
-    k_dt, kg = time_gemv_graph(torch, vt, weights, x, outs, args.steps, 3, stream)
+    # kernel-only timing of the dominant kernel (for its roofline): the GEMV,
+    # or at N > 1 with the peer all-gather the fused kernel
+    if gather is not None:
+        for i in range(3):
+            gather.gemv(x, weights[i % 2], stream=stream)
+        torch.cuda.synchronize()
+        kg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(kg, stream=stream):
+            for i in range(args.steps):
+                gather.gemv(x, weights[i % 2], stream=stream)
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            kg.replay()
+            stream.synchronize()
+            pg.barrier()
+            k0.record(stream)
+            kg.replay()
+            k1.record(stream)
+        torch.cuda.synchronize()
+        k_dt = k0.elapsed_time(k1) / 1e3 / args.steps
+    else:
+        k_dt, kg = time_gemv_graph(torch, vt, weights, x, [y_local], args.steps, 3, stream)
     del kg
 
     # end to end through the C ABI: x from pinned host memory, logits back to pinned host memory
-    y_host = torch.empty(world * n_local, dtype=torch.float32).pin_memory()
+    y_host = torch.empty(y_full.numel() if pg is not None else n_local, dtype=torch.float32).pin_memory()
     y_src = y_full if pg is not None else y_local.view(-1)
     e_steps = max(10, min(args.steps, 500))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -378,7 +402,7 @@ def run_ours(args):
     shard_bytes = algorithmic_bytes(qt, K, n_local, 1)
     achieved = shard_bytes / k_dt / 1e9
     traffic = committed_traffic(WORKLOAD) if world == 1 else None
-    launches_per_step = 1
+    launches_per_step = 1    # the GEMV (with the all-gather fused in when N > 1)
     line = None
     if rank == 0:
         secondary = {}
@@ -405,11 +429,13 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
             "data": "synthetic (seeded, BASELINE distributions)",
             "config": {"workload": WORKLOAD, "qtype": "Q6_K", "K": K, "N": N, "M": 1,
-                       "shard_width": n_local,
+                       "columns_per_rank": n_local,
                        "parallelism": "single GPU" if world == 1 else
-                       f"row-sharded output columns over {world} GPUs + NCCL all-gather",
+                       f"row-sharded output columns over {world} GPUs, " + (
+                           "all-gather fused into the GEMV (stores into every rank's logits over NVLink)"
+                           if gather is not None else "NCCL all-gather"),
                        "l2": "inputs larger than L2: two rotated copies of the weight "
-                             f"({2 * vkq.weight_bytes(qt, K, n_local) / 1e6:.0f} MB per GPU)"},
+                             f"({2 * w0.nbytes / 1e6:.0f} MB per GPU)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                          "peak_kind": peak_kind, "kernel": "vkq::gemv_kernel<Q6_K,1,32>",
@@ -417,12 +443,14 @@ def run_ours(args):
                          "us_per_launch": round(k_dt * 1e6, 3)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(total_bytes / e_dt / 1e9, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * world * n_local,
+                    "h2d_bytes_per_step": 4 * K, "d2h_bytes_per_step": 4 * y_host.numel(),
                     "ms_per_step": round(e_dt * 1e3, 5), "path": "vkq_matmul via ctypes, eager launches"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": sampler.summary(),
             "secondary": secondary,
         }
+    if gather is not None:
+        gather.close()
     if pg is not None:
         pg.barrier()
         pg.destroy_process_group()

@@ -143,6 +143,44 @@ VKQ_API int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int6
 VKQ_API int vkq_gemv_noalloc(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                              const float *x, int64_t M, float *y, void *stream);
 
+/* ---- Row-sharded matmul across the GPUs of one node (one process per GPU) ----
+ * The reference runs on a single device (internal/gpu/cuda/cuda.go:33-46);
+ * these entry points implement the multi-GPU layout of the same MatMul:
+ * each rank holds the weight columns [rank * N_shard, (rank + 1) * N_shard)
+ * and the result is all-gathered through peer memory over NVLink.
+ *
+ * Device buffers shared between processes: vkq_ipc_alloc allocates `bytes`
+ * of zero-filled device memory and returns a 64-byte handle another process
+ * passes to vkq_ipc_open to map the same buffer (peer access is enabled on
+ * the mapping).  vkq_ipc_close unmaps, vkq_ipc_free releases the owner's
+ * buffer (after every mapping of it has been closed). */
+VKQ_API int vkq_ipc_alloc(int device, size_t bytes, void **ptr, unsigned char handle[64]);
+VKQ_API int vkq_ipc_open(int device, const unsigned char handle[64], void **ptr);
+VKQ_API int vkq_ipc_close(int device, void *ptr);
+VKQ_API int vkq_ipc_free(int device, void *ptr);
+
+/* y[M, N] = x[M, K] . W[K, N] computed across `world` ranks, rank `rank`
+ * computing output columns [col_lo, col_hi) (multiples of 32) with the fp32
+ * GEMV of vkq_gemv, fused with the all-gather: each value is stored into
+ * every rank's output buffer y[M][N] through peer memory, with no collective
+ * library call.  Every rank passes the same full weight W (the raw
+ * super-blocks, resident on every GPU; a rank reads only the blocks under its
+ * columns, so shards need no re-encoding when N % 256 != 0).  peer_out and
+ * peer_flags are DEVICE arrays of `world` pointers: this process's mappings
+ * of every rank's output buffer and flag array (own entry included); a flag
+ * array holds 2 * world uint32 and starts at zero; sync points to this rank's
+ * 2 uint32 (zero at first) that count its calls.  Every rank makes the same
+ * sequence of calls.  A call stores into another rank's buffer only after
+ * that rank has started the same call, and when it completes on the stream
+ * every rank's columns are in this rank's output.  The waits inside are
+ * bounded: a rank that never arrives makes the others give up after about
+ * 2 s with VKQ_ERR_DEVICE_TIMEOUT (read with vkq_device_status).
+ * 1 <= M <= 8; the workspace is vkq_matmul_workspace_bytes(M, K, col_hi - col_lo). */
+VKQ_API int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+                               int64_t col_lo, int64_t col_hi, const float *x, int64_t M, void *const *peer_out,
+                               void *const *peer_flags, void *sync, int world, int rank, void *workspace,
+                               size_t workspace_bytes, void *stream);
+
 /* Reads and clears the device-side status word of this library on a device
  * (set when a bounded wait inside a kernel gave up).  Synchronizes with the
  * device.  *code receives VKQ_OK or VKQ_ERR_DEVICE_TIMEOUT. */

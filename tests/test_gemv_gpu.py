@@ -218,3 +218,24 @@ def test_error_paths(tvk):
     assert e.value.status == vkq.ERR_INVALID_ARGUMENT
     call()  # and a valid call still works afterwards
     torch.cuda.synchronize()
+
+
+def test_plans_of_different_tile_counts_share_one_workspace(tvk, oracle):
+    # calls whose plans differ (M = 2: 512-wide tiles, M = 8: 256-wide tiles)
+    # on one workspace: a call's split-K counters must start at zero whatever
+    # the previous call left in the workspace (N = 37984 gives more than 128
+    # of the 256-wide tiles)
+    torch, vt = tvk
+    from vibrant_b200 import synth, vkq
+    qt, K, N = 14, 512, 37984
+    wq = synth.weights(qt, K, N, seed=21)
+    w = vt.QuantWeight(qt, K, N, wq)
+    wd = oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+    Ms = [2, 8, 1, 4, 2, 8]
+    ws = torch.zeros(max(vt.workspace_bytes(qt, M, K, N, 0) for M in Ms), dtype=torch.uint8, device="cuda")
+    for i, M in enumerate(Ms):
+        x = synth.activations(M, K, seed=30 + i)
+        y = vt.matmul(torch.from_numpy(x).cuda(), w, ws=ws)
+        torch.cuda.synchronize()
+        assert helpers.matmul_error(y.cpu().numpy(), x, wd) <= helpers.GEMV_TOL, (i, M)
+    assert vkq.device_status(0) == vkq.OK

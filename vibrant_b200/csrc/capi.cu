@@ -280,6 +280,76 @@ int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K,
     return VKQ_OK;
 }
 
+int vkq_ipc_alloc(int device, size_t bytes, void **ptr, unsigned char handle[64]) {
+    int st = enter(device);
+    if (st) return st;
+    if (!ptr || !handle || bytes == 0) {
+        set_error("invalid arguments to vkq_ipc_alloc");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        return check_launch(e, "vkq_ipc_alloc");
+    }
+    static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+    memcpy(handle, &h, 64);
+    *ptr = p;
+    return VKQ_OK;
+}
+
+int vkq_ipc_open(int device, const unsigned char handle[64], void **ptr) {
+    int st = enter(device);
+    if (st) return st;
+    if (!ptr || !handle) {
+        set_error("invalid arguments to vkq_ipc_open");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, 64);
+    return check_launch(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "vkq_ipc_open");
+}
+
+int vkq_ipc_close(int device, void *ptr) {
+    int st = enter(device);
+    if (st) return st;
+    return check_launch(cudaIpcCloseMemHandle(ptr), "vkq_ipc_close");
+}
+
+int vkq_ipc_free(int device, void *ptr) {
+    int st = enter(device);
+    if (st) return st;
+    return check_launch(cudaFree(ptr), "vkq_ipc_free");
+}
+
+int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, int64_t col_lo,
+                       int64_t col_hi, const float *x, int64_t M, void *const *peer_out, void *const *peer_flags,
+                       void *sync, int world, int rank, void *workspace, size_t workspace_bytes, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, reinterpret_cast<float *>(sync));
+    if (st) return st;
+    if (M > 8) {
+        set_error("vkq_gemv_allgather serves 1 <= M <= 8 (got %lld)", (long long)M);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!peer_out || !peer_flags || world < 1 || rank < 0 || rank >= world || N % 32 != 0 || col_lo < 0 ||
+        col_hi > N || col_hi <= col_lo || col_lo % 32 != 0 || col_hi % 32 != 0) {
+        set_error("vkq_gemv_allgather: invalid peer arrays, world/rank (%d/%d) or columns [%lld, %lld) of N=%lld "
+                  "(multiples of 32 needed)",
+                  world, rank, (long long)col_lo, (long long)col_hi, (long long)N);
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    GemvShape s{qtype, K, col_hi - col_lo, M};
+    GatherArgs g{reinterpret_cast<float *const *>(peer_out), reinterpret_cast<unsigned *const *>(peer_flags),
+                 static_cast<unsigned *>(sync), world, rank, N, col_lo, N, col_lo};
+    return gemv_launch(s, w, w_bytes, x, nullptr, workspace, workspace_bytes, (cudaStream_t)stream, device, &g);
+}
+
 int vkq_device_status(int device, int *code) {
     int st = enter(device);
     if (st) return st;

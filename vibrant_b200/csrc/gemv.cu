@@ -54,7 +54,8 @@ struct GemvParams {
     int64_t w_floor16;  // bytes that bulk copies may read
     const float *x;
     float *y;
-    int64_t K, N;
+    int64_t K, N;        // N: the output columns this launch computes
+    int64_t ld, n_base;  // W[k][n_base + n] is value k * ld + n_base + n (ld = N, n_base = 0 unsharded)
     int M;
     int ntiles;
     int grid;
@@ -64,9 +65,56 @@ struct GemvParams {
     int *counters;       // [ntiles]
     int row_cap;         // bytes per ring row slot (multiple of 16)
     int stages;
+    // Row-sharded all-gather (world > 1): column n of this rank's shard is
+    // stored into every rank's output [M][y_ld] at column col_off + n.
+    float *const *peer_y;          // [world] output buffers (this process's mappings)
+    unsigned *const *peer_flags;   // [world] flag arrays: [0, world) started, [world, 2 world) done
+    unsigned *sync;                // this rank's [call counter, finished-CTA counter]
+    int world, rank;
+    int64_t y_ld, col_off;
 };
 
 __device__ __forceinline__ void set_status(int code) { atomicExch(&g_gemv_status, code); }
+
+// Output stores: the local y, or (all-gather) the same position of every
+// rank's output buffer through peer memory (plain stores over NVLink).
+__device__ __forceinline__ void store_y(const GemvParams &p, int64_t m, int64_t c, float v) {
+    if (p.peer_y == nullptr) {
+        p.y[m * p.N + c] = v;
+        return;
+    }
+    const int64_t off = m * p.y_ld + p.col_off + c;
+    for (int r = 0; r < p.world; r++) p.peer_y[r][off] = v;
+}
+__device__ __forceinline__ void store_y4(const GemvParams &p, int64_t m, int64_t c, float4 v) {
+    if (p.peer_y == nullptr) {
+        float *yo = p.y + m * p.N + c;
+        yo[0] = v.x; yo[1] = v.y; yo[2] = v.z; yo[3] = v.w;
+        return;
+    }
+    const int64_t off = m * p.y_ld + p.col_off + c;  // 16-byte aligned: widths and offsets are multiples of 32
+    for (int r = 0; r < p.world; r++) *reinterpret_cast<float4 *>(p.peer_y[r] + off) = v;
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned *a, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+// Bounded wait until flags f[0..count) have all reached seq (32-bit counters
+// compared by signed difference); false when the budget runs out.
+__device__ __forceinline__ bool wait_flags(const unsigned *f, int count, unsigned seq, uint64_t budget_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        bool all = true;
+        for (int r = 0; r < count && all; r++) all = (int)(ld_acquire_sys(f + r) - seq) >= 0;
+        if (all) return true;
+        if (globaltimer_ns() - t0 > budget_ns) return false;
+        __nanosleep(100);
+    }
+}
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 // Q6_K: acc[m] += a[m] * (q - 32) with a = x * (d * scale).
@@ -271,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             int64_t a_lo = 0, c_hi = 0, byte_hi = 0;
             if (row_ok) {
                 const int64_t n0 = (int64_t)t * TN, n1 = imin64(n0 + TN, N);
-                const int64_t base = (int64_t)kk * N;
+                const int64_t base = (int64_t)kk * p.ld + p.n_base;
                 a_lo = (((base + n0) >> 8) * B) & ~int64_t(15);
                 byte_hi = ((base + n1 + 255) >> 8) * B;
                 c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
@@ -344,6 +392,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     }
     pdl_wait();  // y and the workspace may belong to the preceding kernel
 
+    // All-gather: this call's number, and (CTA 0) the "started" flag on every
+    // rank.  A CTA's first output store waits until every rank has started
+    // this call (so it has finished reading the previous result).
+    unsigned seq = 0;
+    bool peers_started = p.world <= 1;
+    if (p.world > 1) {
+        if (tid == 0) {
+            seq = *reinterpret_cast<volatile unsigned *>(&p.sync[0]) + 1u;
+            if (blockIdx.x == 0)
+                for (int r = 0; r < p.world; r++) st_release_sys(p.peer_flags[r] + p.rank, seq);
+            flag[1] = (int)seq;
+        }
+        named_bar_sync(1, kNW * 32);
+        seq = (unsigned)flag[1];
+    }
+
     const int64_t first_tile = f0 / K;
     const int64_t last_tile = (f1 - 1) / K;
     int64_t cur_tile = first_tile;
@@ -366,6 +430,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 acc[m][2 * i + 1] = 0ull;
             }
         }
+        if (!peers_started) {  // first output store of this CTA in an all-gather call
+            if (tid == 0 && !wait_flags(p.peer_flags[p.rank], p.world, seq, kWaitNs)) set_status(kStatusTimeout);
+            peers_started = true;
+        }
         named_bar_sync(1, kNW * 32);
         // 2. fixed-order sum over the warps
         const int64_t n0 = tile * TN;
@@ -380,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             float sum = 0.0f;
 #pragma unroll
             for (int w = 0; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
-            if (whole) p.y[(int64_t)m * N + n0 + c] = sum;
+            if (whole) store_y(p, m, n0 + c, sum);
             else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = sum;
         }
         named_bar_sync(1, kNW * 32);
@@ -424,8 +492,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                             }
                         }
                     }
-                    float *yo = p.y + (int64_t)m * N + n0 + c;
-                    yo[0] = acc4.x; yo[1] = acc4.y; yo[2] = acc4.z; yo[3] = acc4.w;
+                    store_y4(p, m, n0 + c, acc4);
                 }
                 if (tid == 0) atomicExch(&p.counters[tile], 0);
             }
@@ -448,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     uint32_t slot = 0, phase = 0;
     const uint32_t warp_row0 = ring_base + (uint32_t)(warp * p.row_cap);
     const uint32_t stage_bytes = (uint32_t)(kRPS * p.row_cap);
-    const uint32_t Nu = (uint32_t)N;
+    const uint32_t LDu = (uint32_t)p.ld, NBu = (uint32_t)p.n_base;
 
     for (int s = 0; s < nst32; s++) {
         if (!mbar_wait_bounded(smem_u32addr(&full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
@@ -460,9 +527,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             }
             const uint32_t n0 = t * TN;
             if ((int64_t)n0 + lane * VPT < N) {
-                // low 32 bits of v0 = k*N + n0 give the in-block offset of the
-                // row's first value and the 16-byte lead of its first block
-                const uint32_t v0 = kk * Nu + n0;
+                // low 32 bits of v0 = k*ld + n_base + n0 give the in-block offset
+                // of the row's first value and the 16-byte lead of its first block
+                const uint32_t v0 = kk * LDu + NBu + n0;
                 const uint32_t lead = (((v0 >> 8) & 15u) * (uint32_t)B) & 15u;
                 const uint32_t wl = (v0 & 255u) + lane * VPT;
                 const uint32_t blk = warp_row0 + slot * stage_bytes + (wl >> 8) * B + lead;
@@ -488,6 +555,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     while (cur_tile <= last_tile) {
         flush(cur_tile);
         cur_tile++;
+    }
+    // All-gather: the last CTA to finish tells every rank this rank's shard
+    // is in place, then waits until every rank's shard is in its own buffer.
+    if (p.world > 1) {
+        __threadfence_system();
+        named_bar_sync(1, kNW * 32);
+        if (tid == 0) {
+            const unsigned old = atomicAdd(&p.sync[1], 1u);
+            if (old == (unsigned)p.grid - 1u) {
+                p.sync[1] = 0u;
+                p.sync[0] = seq;
+                __threadfence_system();
+                for (int r = 0; r < p.world; r++) st_release_sys(p.peer_flags[r] + p.world + p.rank, seq);
+                if (!wait_flags(p.peer_flags[p.rank] + p.world, p.world, seq, kWaitNs)) set_status(kStatusTimeout);
+            }
+        }
     }
 }
 
@@ -586,7 +669,7 @@ static Plan make_plan(const GemvShape &s, int device) {
 size_t gemv_workspace_bytes(const GemvShape &s, int device) {
     Plan pl = make_plan(s, device);
     if (pl.generic) return 0;
-    return pl.counter_bytes + pl.partial_bytes;
+    return kWorkspaceCounterHead + pl.partial_bytes;
 }
 
 template <int QT, int MR, int VPT>
@@ -621,9 +704,13 @@ static cudaError_t dispatch_mr(const GemvParams &gp, const Plan &pl, cudaStream_
 }
 
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
-                size_t ws_bytes, cudaStream_t stream, int device) {
+                size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather) {
     Plan pl = make_plan(s, device);
     cudaError_t e;
+    if (pl.generic && gather) {
+        set_error("the all-gather GEMV needs a shard width that is a multiple of 32 (got %lld)", (long long)s.N);
+        return 2;
+    }
     if (pl.generic) {
         const uint8_t *wp = static_cast<const uint8_t *>(w);
         dim3 grid((unsigned)((s.N + 127) / 128));
@@ -639,7 +726,7 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
         }
         return 0;
     }
-    const size_t need = pl.counter_bytes + pl.partial_bytes;
+    const size_t need = kWorkspaceCounterHead + pl.partial_bytes;
     if (ws == nullptr || ws_bytes < need) {
         set_error("gemv needs a workspace of %zu bytes (got %zu)", need, ws_bytes);
         return 4;
@@ -652,15 +739,29 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
     gp.y = y;
     gp.K = s.K;
     gp.N = s.N;
+    gp.ld = gather ? gather->w_ld : s.N;
+    gp.n_base = gather ? gather->n_base : 0;
     gp.M = (int)s.M;
     gp.ntiles = pl.ntiles;
     gp.grid = pl.grid;
     gp.rows_total = (int64_t)pl.ntiles * s.K;
     gp.rpc = pl.rpc;
     gp.counters = static_cast<int *>(ws);
-    gp.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + pl.counter_bytes);
+    // partials after the fixed counter head: a later call with more tiles
+    // must find its counters at zero, never overwritten by these partials
+    gp.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kWorkspaceCounterHead);
     gp.row_cap = pl.row_cap;
     gp.stages = pl.stages;
+    gp.world = 1;
+    if (gather) {
+        gp.peer_y = gather->peer_y;
+        gp.peer_flags = gather->peer_flags;
+        gp.sync = gather->sync;
+        gp.world = gather->world;
+        gp.rank = gather->rank;
+        gp.y_ld = gather->y_ld;
+        gp.col_off = gather->col_off;
+    }
     switch (s.qtype) {
     case kQ4K: e = dispatch_mr<kQ4K>(gp, pl, stream); break;
     case kQ5K: e = dispatch_mr<kQ5K>(gp, pl, stream); break;
@@ -707,7 +808,7 @@ int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, cons
                         cudaStream_t stream, int device) {
     Plan pl = make_plan(s, device);
     if (pl.generic) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);
-    const size_t need = pl.counter_bytes + pl.partial_bytes;
+    const size_t need = kWorkspaceCounterHead + pl.partial_bytes;
     if (need > kNoAllocScratchBytes) {
         set_error("this GEMV needs %zu bytes of scratch; the fixed scratch of vkq_gemv_noalloc holds %zu", need,
                   kNoAllocScratchBytes);

@@ -28,9 +28,21 @@ struct GemvShape {
 };
 // Workspace bytes the GEMV plan needs (0 when it needs none).
 size_t gemv_workspace_bytes(const GemvShape &s, int device);
+// Row-sharded all-gather through peer memory: the launch computes columns
+// [n_base, n_base + N) of a weight with rows of w_ld values and stores column
+// n_base + n of the result into every rank's output [M][y_ld] at column
+// col_off + n; see vkq_gemv_allgather.
+struct GatherArgs {
+    float *const *peer_y;          // device array of `world` output pointers
+    unsigned *const *peer_flags;   // device array of `world` flag arrays (2 * world words each)
+    unsigned *sync;                // this rank's two counters
+    int world, rank;
+    int64_t y_ld, col_off;
+    int64_t w_ld, n_base;
+};
 // Returns a vkq_status code; on failure writes a message with set_error.
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
-                size_t ws_bytes, cudaStream_t stream, int device);
+                size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather = nullptr);
 // Same GEMV with its scratch in a fixed device array of the library (no
 // workspace argument, nothing allocated); see vkq_gemv_noalloc.
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,

@@ -104,3 +104,96 @@ def dequant_transpose(w: QuantWeight, stream=None) -> torch.Tensor:
     vkq.dequant_transpose_f32(w.qtype, w.buf.data_ptr(), w.K, w.N, out.data_ptr(), device=w.device_index,
                               stream=st)
     return out
+
+
+# ---- row-sharded matmul across the GPUs of one node (one process per GPU) ----
+
+def shard_columns(N: int, world: int) -> tuple[int, list[tuple[int, int]]]:
+    """Equal shard width (a multiple of 32, as the fast GEMV and the peer
+    all-gather need) and each rank's [lo, hi) output columns; the last
+    rank's range may be shorter than the width (its tail is padding)."""
+    width = -(-N // world)
+    width = -(-width // 32) * 32
+    bounds = [(min(r * width, N), min((r + 1) * width, N)) for r in range(world)]
+    return width, bounds
+
+
+class _DeviceArray:
+    """A raw device pointer seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "strides": None, "version": 3}
+
+
+class PeerGather:
+    """Output buffers and flags for vkq_gemv_allgather, created collectively
+    by every rank of a process group (one process per GPU).
+
+    Every rank keeps the full quantized weight [K, N]; rank r computes output
+    columns bounds[r] = [lo, hi) of shard_columns(N, world) and the kernel
+    stores them into every rank's output [m_max, N].  Each rank allocates its
+    output and a flag array with vkq_ipc_alloc, the 64-byte handles are
+    exchanged over the group and every rank maps every other rank's buffers
+    (vkq_ipc_open).  `gemv` then leaves the whole x @ W in `out` on every
+    rank, with no collective library call on the data path."""
+
+    def __init__(self, group, rank: int, world: int, device: int, N: int, m_max: int = 8):
+        import torch.distributed as dist
+        if N % 32:
+            raise ValueError("N must be a multiple of 32")
+        self.width, self.bounds = shard_columns(N, world)
+        if any(hi <= lo for lo, hi in self.bounds):
+            raise ValueError(f"N={N} leaves a rank of {world} without columns")
+        self.group, self.rank, self.world, self.device, self.N, self.m_max = group, rank, world, device, N, m_max
+        self.out_ptr, h_out = vkq.ipc_alloc(m_max * N * 4, device)
+        self.flags_ptr, h_flags = vkq.ipc_alloc(max(256, 8 * world), device)
+        self.sync_ptr, _ = vkq.ipc_alloc(256, device)
+        handles: list = [None] * world
+        dist.all_gather_object(handles, (h_out, h_flags), group=group)
+        self._mapped: list[int] = []
+        outs, flags = [], []
+        for r, (ho, hf) in enumerate(handles):
+            if r == rank:
+                outs.append(self.out_ptr)
+                flags.append(self.flags_ptr)
+                continue
+            po, pf = vkq.ipc_open(ho, device), vkq.ipc_open(hf, device)
+            self._mapped += [po, pf]
+            outs.append(po)
+            flags.append(pf)
+        dev = f"cuda:{device}"
+        self.peer_out = torch.tensor(outs, dtype=torch.int64, device=dev)
+        self.peer_flags = torch.tensor(flags, dtype=torch.int64, device=dev)
+        self.out = torch.as_tensor(_DeviceArray(self.out_ptr, (m_max, N)), device=dev)
+
+    def gemv(self, x: torch.Tensor, w: QuantWeight, ws: torch.Tensor | None = None,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """x @ W across the group: returns out[:M] (vkq_gemv_allgather)."""
+        if w.N != self.N or x.shape[1] != w.K or x.dtype != torch.float32:
+            raise ValueError("the weight or x does not match the group")
+        M = x.shape[0]
+        if M > self.m_max:
+            raise ValueError(f"M={M} exceeds the group's m_max={self.m_max}")
+        x = x.contiguous()
+        lo, hi = self.bounds[self.rank]
+        if ws is None:
+            ws = workspace(workspace_bytes(w.qtype, M, w.K, hi - lo, self.device), self.device)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device)
+        vkq.gemv_allgather(w.qtype, w.buf.data_ptr(), w.nbytes, w.K, w.N, lo, hi, x.data_ptr(), M,
+                           self.peer_out.data_ptr(), self.peer_flags.data_ptr(), self.sync_ptr, self.world,
+                           self.rank, ws.data_ptr() if ws is not None else None,
+                           ws.numel() if ws is not None else 0, device=self.device, stream=st)
+        return self.out[:M]
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free this rank's."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self._mapped:
+            vkq.ipc_close(p, self.device)
+        self._mapped = []
+        dist.barrier(group=self.group)
+        for p in (self.out_ptr, self.flags_ptr, self.sync_ptr):
+            vkq.ipc_free(p, self.device)

@@ -38,6 +38,12 @@ SIGNATURES = {
     "vkq_gemm": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
     "vkq_gemv_noalloc": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "vkq_device_status": (_int, [_int, ctypes.POINTER(_int)]),
+    "vkq_ipc_alloc": (_int, [_int, _sz, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_ubyte * 64)]),
+    "vkq_ipc_open": (_int, [_int, ctypes.POINTER(ctypes.c_ubyte * 64), ctypes.POINTER(_vp)]),
+    "vkq_ipc_close": (_int, [_int, _vp]),
+    "vkq_ipc_free": (_int, [_int, _vp]),
+    "vkq_gemv_allgather": (_int, [_int, _int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _int,
+                                  _int, _vp, _sz, _vp]),
 }
 
 
@@ -132,3 +138,37 @@ def device_status(device: int = -1) -> int:
     code = _int()
     _check(load().vkq_device_status(device, ctypes.byref(code)))
     return code.value
+
+
+def ipc_alloc(nbytes: int, device: int = -1) -> tuple[int, bytes]:
+    """vkq_ipc_alloc: zero-filled device memory another process can map;
+    returns (device pointer, 64-byte handle)."""
+    ptr, h = _vp(), (ctypes.c_ubyte * 64)()
+    _check(load().vkq_ipc_alloc(device, nbytes, ctypes.byref(ptr), ctypes.byref(h)))
+    return ptr.value, bytes(h)
+
+
+def ipc_open(handle: bytes, device: int = -1) -> int:
+    """vkq_ipc_open: this process's mapping of another process's buffer."""
+    h = (ctypes.c_ubyte * 64).from_buffer_copy(handle)
+    ptr = _vp()
+    _check(load().vkq_ipc_open(device, ctypes.byref(h), ctypes.byref(ptr)))
+    return ptr.value
+
+
+def ipc_close(ptr: int, device: int = -1) -> None:
+    _check(load().vkq_ipc_close(device, ptr))
+
+
+def ipc_free(ptr: int, device: int = -1) -> None:
+    _check(load().vkq_ipc_free(device, ptr))
+
+
+def gemv_allgather(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, col_lo: int, col_hi: int, x_ptr: int,
+                   M: int, peer_out_ptr: int, peer_flags_ptr: int, sync_ptr: int, world: int, rank: int,
+                   ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
+    """vkq_gemv_allgather: columns [col_lo, col_hi) of x @ W on this rank,
+    stored into every rank's output [M, N] through peer memory (include/vkq.h)."""
+    _check(load().vkq_gemv_allgather(device, qtype, w_ptr, w_bytes, K, N, col_lo, col_hi, x_ptr, M, peer_out_ptr,
+                                     peer_flags_ptr, sync_ptr, world, rank, ws_ptr, ws_bytes,
+                                     _stream_ptr(stream)))
