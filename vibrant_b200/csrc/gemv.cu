@@ -55,7 +55,6 @@ struct GemvParams {
     const float *x;
     float *y;
     int64_t K, N;        // N: the output columns this launch computes
-    int64_t ld, n_base;  // W[k][n_base + n] is value k * ld + n_base + n (ld = N, n_base = 0 unsharded)
     int M;
     int ntiles;
     int grid;
@@ -65,35 +64,31 @@ struct GemvParams {
     int *counters;       // [ntiles]
     int row_cap;         // bytes per ring row slot (multiple of 16)
     int stages;
-    // Row-sharded all-gather (world > 1): column n of this rank's shard is
-    // stored into every rank's output [M][y_ld] at column col_off + n.
+};
+
+// Row-sharded all-gather: column n of this launch's columns is stored into
+// every rank's output [M][y_ld] at column col_off + n.  A separate kernel
+// parameter (growing GemvParams changes the plain kernel's code generation).
+struct GatherParams {
     float *const *peer_y;          // [world] output buffers (this process's mappings)
     unsigned *const *peer_flags;   // [world] flag arrays: [0, world) started, [world, 2 world) done
     unsigned *sync;                // this rank's [call counter, finished-CTA counter]
     int world, rank;
     int64_t y_ld, col_off;
+    int64_t ld, n_base;  // W[k][n_base + n] is value k * ld + n_base + n
 };
 
 __device__ __forceinline__ void set_status(int code) { atomicExch(&g_gemv_status, code); }
 
 // Output stores: the local y, or (all-gather) the same position of every
 // rank's output buffer through peer memory (plain stores over NVLink).
-__device__ __forceinline__ void store_y(const GemvParams &p, int64_t m, int64_t c, float v) {
-    if (p.peer_y == nullptr) {
-        p.y[m * p.N + c] = v;
-        return;
-    }
-    const int64_t off = m * p.y_ld + p.col_off + c;
-    for (int r = 0; r < p.world; r++) p.peer_y[r][off] = v;
+__device__ __forceinline__ void store_peers(const GatherParams &g, int64_t m, int64_t c, float v) {
+    const int64_t off = m * g.y_ld + g.col_off + c;
+    for (int r = 0; r < g.world; r++) g.peer_y[r][off] = v;
 }
-__device__ __forceinline__ void store_y4(const GemvParams &p, int64_t m, int64_t c, float4 v) {
-    if (p.peer_y == nullptr) {
-        float *yo = p.y + m * p.N + c;
-        yo[0] = v.x; yo[1] = v.y; yo[2] = v.z; yo[3] = v.w;
-        return;
-    }
-    const int64_t off = m * p.y_ld + p.col_off + c;  // 16-byte aligned: widths and offsets are multiples of 32
-    for (int r = 0; r < p.world; r++) *reinterpret_cast<float4 *>(p.peer_y[r] + off) = v;
+__device__ __forceinline__ void store_peers4(const GatherParams &g, int64_t m, int64_t c, float4 v) {
+    const int64_t off = m * g.y_ld + g.col_off + c;  // 16-byte aligned: widths and offsets are multiples of 32
+    for (int r = 0; r < g.world; r++) *reinterpret_cast<float4 *>(g.peer_y[r] + off) = v;
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
     unsigned v;
@@ -259,8 +254,10 @@ __device__ __forceinline__ int red_swz(int lane) {
     return (lane / (8 / F)) & (F - 1);
 }
 
-template <int QT, int MR, int VPT>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
+// G: the all-gather variant (outputs stored into every rank's buffer, with
+// the start / done handshakes); the plain kernel carries none of it.
+template <int QT, int MR, int VPT, bool G>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, const GatherParams gq) {
     constexpr int B = QT_<QT>::BYTES;
     constexpr int TN = 32 * VPT;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -319,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             int64_t a_lo = 0, c_hi = 0, byte_hi = 0;
             if (row_ok) {
                 const int64_t n0 = (int64_t)t * TN, n1 = imin64(n0 + TN, N);
-                const int64_t base = (int64_t)kk * p.ld + p.n_base;
+                const int64_t base = G ? (int64_t)kk * gq.ld + gq.n_base : (int64_t)kk * N;
                 a_lo = (((base + n0) >> 8) * B) & ~int64_t(15);
                 byte_hi = ((base + n1 + 255) >> 8) * B;
                 c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
@@ -396,12 +393,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     // rank.  A CTA's first output store waits until every rank has started
     // this call (so it has finished reading the previous result).
     unsigned seq = 0;
-    bool peers_started = p.world <= 1;
-    if (p.world > 1) {
+    bool peers_started = !(G && gq.world > 1);
+    if (G && gq.world > 1) {
         if (tid == 0) {
-            seq = *reinterpret_cast<volatile unsigned *>(&p.sync[0]) + 1u;
+            seq = *reinterpret_cast<volatile unsigned *>(&gq.sync[0]) + 1u;
             if (blockIdx.x == 0)
-                for (int r = 0; r < p.world; r++) st_release_sys(p.peer_flags[r] + p.rank, seq);
+                for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.rank, seq);
             flag[1] = (int)seq;
         }
         named_bar_sync(1, kNW * 32);
@@ -430,9 +427,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                 acc[m][2 * i + 1] = 0ull;
             }
         }
-        if (!peers_started) {  // first output store of this CTA in an all-gather call
-            if (tid == 0 && !wait_flags(p.peer_flags[p.rank], p.world, seq, kWaitNs)) set_status(kStatusTimeout);
-            peers_started = true;
+        if constexpr (G) {
+            if (!peers_started) {  // first output store of this CTA in an all-gather call
+                if (tid == 0 && !wait_flags(gq.peer_flags[gq.rank], gq.world, seq, kWaitNs)) set_status(kStatusTimeout);
+                peers_started = true;
+            }
         }
         named_bar_sync(1, kNW * 32);
         // 2. fixed-order sum over the warps
@@ -448,7 +447,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             float sum = 0.0f;
 #pragma unroll
             for (int w = 0; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
-            if (whole) store_y(p, m, n0 + c, sum);
+            if (whole) {
+                if constexpr (G) store_peers(gq, m, n0 + c, sum);
+                else p.y[(int64_t)m * N + n0 + c] = sum;
+            }
             else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = sum;
         }
         named_bar_sync(1, kNW * 32);
@@ -492,7 +494,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
                             }
                         }
                     }
-                    store_y4(p, m, n0 + c, acc4);
+                    if constexpr (G) {
+                        store_peers4(gq, m, n0 + c, acc4);
+                    } else {
+                        float *yo = p.y + (int64_t)m * N + n0 + c;
+                        yo[0] = acc4.x; yo[1] = acc4.y; yo[2] = acc4.z; yo[3] = acc4.w;
+                    }
                 }
                 if (tid == 0) atomicExch(&p.counters[tile], 0);
             }
@@ -515,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     uint32_t slot = 0, phase = 0;
     const uint32_t warp_row0 = ring_base + (uint32_t)(warp * p.row_cap);
     const uint32_t stage_bytes = (uint32_t)(kRPS * p.row_cap);
-    const uint32_t LDu = (uint32_t)p.ld, NBu = (uint32_t)p.n_base;
+    const uint32_t Nu = (uint32_t)N;
 
     for (int s = 0; s < nst32; s++) {
         if (!mbar_wait_bounded(smem_u32addr(&full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
@@ -529,7 +536,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
             if ((int64_t)n0 + lane * VPT < N) {
                 // low 32 bits of v0 = k*ld + n_base + n0 give the in-block offset
                 // of the row's first value and the 16-byte lead of its first block
-                const uint32_t v0 = kk * LDu + NBu + n0;
+                uint32_t v0;
+                if constexpr (G) v0 = kk * (uint32_t)gq.ld + (uint32_t)gq.n_base + n0;
+                else v0 = kk * Nu + n0;
                 const uint32_t lead = (((v0 >> 8) & 15u) * (uint32_t)B) & 15u;
                 const uint32_t wl = (v0 & 255u) + lane * VPT;
                 const uint32_t blk = warp_row0 + slot * stage_bytes + (wl >> 8) * B + lead;
@@ -558,17 +567,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p) {
     }
     // All-gather: the last CTA to finish tells every rank this rank's shard
     // is in place, then waits until every rank's shard is in its own buffer.
-    if (p.world > 1) {
-        __threadfence_system();
-        named_bar_sync(1, kNW * 32);
+    if (G && gq.world > 1) {
+        named_bar_sync(1, kNW * 32);  // every store of this CTA is issued
         if (tid == 0) {
-            const unsigned old = atomicAdd(&p.sync[1], 1u);
+            __threadfence_system();   // ... and, cumulatively, visible before the count
+            const unsigned old = atomicAdd(&gq.sync[1], 1u);
             if (old == (unsigned)p.grid - 1u) {
-                p.sync[1] = 0u;
-                p.sync[0] = seq;
+                gq.sync[1] = 0u;
+                gq.sync[0] = seq;
                 __threadfence_system();
-                for (int r = 0; r < p.world; r++) st_release_sys(p.peer_flags[r] + p.world + p.rank, seq);
-                if (!wait_flags(p.peer_flags[p.rank] + p.world, p.world, seq, kWaitNs)) set_status(kStatusTimeout);
+                for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, seq);
+                if (!wait_flags(gq.peer_flags[gq.rank] + gq.world, gq.world, seq, kWaitNs))
+                    set_status(kStatusTimeout);
             }
         }
     }
@@ -672,9 +682,9 @@ size_t gemv_workspace_bytes(const GemvShape &s, int device) {
     return kWorkspaceCounterHead + pl.partial_bytes;
 }
 
-template <int QT, int MR, int VPT>
-static cudaError_t launch_fast(const GemvParams &gp, const Plan &pl, cudaStream_t stream) {
-    auto kern = gemv_kernel<QT, MR, VPT>;
+template <int QT, int MR, int VPT, bool G>
+static cudaError_t launch_fast(const GemvParams &gp, const GatherParams &gq, const Plan &pl, cudaStream_t stream) {
+    auto kern = gemv_kernel<QT, MR, VPT, G>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
     if (e != cudaSuccess) return e;
     // two CTAs per SM need the largest shared-memory carveout
@@ -690,16 +700,16 @@ static cudaError_t launch_fast(const GemvParams &gp, const Plan &pl, cudaStream_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, gp);
+    return cudaLaunchKernelEx(&cfg, kern, gp, gq);
 }
 
 template <int QT>
-static cudaError_t dispatch_mr(const GemvParams &gp, const Plan &pl, cudaStream_t st) {
+static cudaError_t dispatch_mr(const GemvParams &gp, const GatherParams &gq, const Plan &pl, cudaStream_t st) {
     switch (pl.mr) {
-    case 1: return launch_fast<QT, 1, 32>(gp, pl, st);
-    case 2: return launch_fast<QT, 2, 16>(gp, pl, st);
-    case 4: return launch_fast<QT, 4, 8>(gp, pl, st);
-    default: return launch_fast<QT, 8, 8>(gp, pl, st);
+    case 1: return gq.peer_y ? launch_fast<QT, 1, 32, true>(gp, gq, pl, st) : launch_fast<QT, 1, 32, false>(gp, gq, pl, st);
+    case 2: return gq.peer_y ? launch_fast<QT, 2, 16, true>(gp, gq, pl, st) : launch_fast<QT, 2, 16, false>(gp, gq, pl, st);
+    case 4: return gq.peer_y ? launch_fast<QT, 4, 8, true>(gp, gq, pl, st) : launch_fast<QT, 4, 8, false>(gp, gq, pl, st);
+    default: return gq.peer_y ? launch_fast<QT, 8, 8, true>(gp, gq, pl, st) : launch_fast<QT, 8, 8, false>(gp, gq, pl, st);
     }
 }
 
@@ -739,8 +749,6 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
     gp.y = y;
     gp.K = s.K;
     gp.N = s.N;
-    gp.ld = gather ? gather->w_ld : s.N;
-    gp.n_base = gather ? gather->n_base : 0;
     gp.M = (int)s.M;
     gp.ntiles = pl.ntiles;
     gp.grid = pl.grid;
@@ -752,20 +760,23 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
     gp.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kWorkspaceCounterHead);
     gp.row_cap = pl.row_cap;
     gp.stages = pl.stages;
-    gp.world = 1;
+    GatherParams gq{};
+    gq.world = 1;
     if (gather) {
-        gp.peer_y = gather->peer_y;
-        gp.peer_flags = gather->peer_flags;
-        gp.sync = gather->sync;
-        gp.world = gather->world;
-        gp.rank = gather->rank;
-        gp.y_ld = gather->y_ld;
-        gp.col_off = gather->col_off;
+        gq.peer_y = gather->peer_y;
+        gq.peer_flags = gather->peer_flags;
+        gq.sync = gather->sync;
+        gq.world = gather->world;
+        gq.rank = gather->rank;
+        gq.y_ld = gather->y_ld;
+        gq.col_off = gather->col_off;
+        gq.ld = gather->w_ld;
+        gq.n_base = gather->n_base;
     }
     switch (s.qtype) {
-    case kQ4K: e = dispatch_mr<kQ4K>(gp, pl, stream); break;
-    case kQ5K: e = dispatch_mr<kQ5K>(gp, pl, stream); break;
-    default: e = dispatch_mr<kQ6K>(gp, pl, stream); break;
+    case kQ4K: e = dispatch_mr<kQ4K>(gp, gq, pl, stream); break;
+    case kQ5K: e = dispatch_mr<kQ5K>(gp, gq, pl, stream); break;
+    default: e = dispatch_mr<kQ6K>(gp, gq, pl, stream); break;
     }
     if (e != cudaSuccess) {
         set_error("gemv launch failed: %s", cudaGetErrorString(e));
