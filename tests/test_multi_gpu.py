@@ -67,3 +67,52 @@ def test_allgather_through_peer_memory_two_gpus():
         (13, 512, 4160),           # Q5_K, N % 256 == 64
     ]
     mp.spawn(_rank_main, args=(2, _free_port(), cases), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("qt,K,N,world", [
+    (14, 256, 151936, 2),  # wide shards: 64 values per lane
+    (14, 2048, 37984, 2),  # shards straddle super-blocks
+    (12, 2048, 11008, 4),
+    (13, 512, 4160, 2),
+])
+def test_allgather_kernel_single_rank(qt, K, N, world):
+    """The all-gather kernel run as rank 0 of 1 for each shard of a
+    `world`-way split: the shard's columns land in the output at their
+    global offset and match the oracle; the other columns stay untouched."""
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from oracle import kq_oracle
+    from vibrant_b200 import synth, vkq
+    from vibrant_b200 import tensor as vt
+    wq = synth.weights(qt, K, N, seed=K + N + world)
+    w = vt.QuantWeight(qt, K, N, wq)
+    wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+    _, bounds = vt.shard_columns(N, world)
+    m_max = 4
+    out, _ = vkq.ipc_alloc(m_max * N * 4)
+    flags, _ = vkq.ipc_alloc(256)
+    sync, _ = vkq.ipc_alloc(256)
+    try:
+        peer_out = torch.tensor([out], dtype=torch.int64, device="cuda")
+        peer_flags = torch.tensor([flags], dtype=torch.int64, device="cuda")
+        Y = torch.as_tensor(vt._DeviceArray(out, (m_max, N)), device="cuda")
+        for M in (1, 3):
+            for lo, hi in bounds:
+                x = synth.activations(M, K, seed=M * 7 + lo)
+                xt = torch.from_numpy(x).cuda()
+                ws = vt.workspace(vt.workspace_bytes(qt, M, K, hi - lo, 0), 0)
+                Y.fill_(123.0)
+                vkq.gemv_allgather(qt, w.buf.data_ptr(), w.nbytes, K, N, lo, hi, xt.data_ptr(), M,
+                                   peer_out.data_ptr(), peer_flags.data_ptr(), sync, 1, 0, ws.data_ptr(),
+                                   ws.numel(), device=0)
+                torch.cuda.synchronize()
+                y = Y[:M].cpu().numpy()
+                err = helpers.matmul_error(y[:, lo:hi], x, wd[:, lo:hi])
+                assert err <= helpers.GEMV_TOL, (qt, K, N, M, lo, hi, err)
+                assert (y[:, :lo] == 123.0).all() and (y[:, hi:] == 123.0).all()
+        assert vkq.device_status(0) == vkq.OK
+    finally:
+        torch.cuda.synchronize()
+        for p in (out, flags, sync):
+            vkq.ipc_free(p)

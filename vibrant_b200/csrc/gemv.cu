@@ -13,23 +13,30 @@
 //    chunk (one k, TN columns) is a contiguous run of super-blocks.  The
 //    (tile, k) space is flattened and split evenly over a grid of 2 CTAs per
 //    SM ("stream-K" over rows), so every shape fills the machine.
-//  * One producer warp per CTA streams row chunks into a shared-memory ring
-//    with cp.async.bulk (no multicast), STAGES x 8 rows deep, tracked by
-//    mbarriers; the weight prefetch starts before griddepcontrol.wait, so it
-//    overlaps the tail of the previous kernel when launched with
-//    programmatic stream serialization.
-//  * 8 consumer warps take one row each per stage; lane l decodes VPT
-//    consecutive values (a 32-value sub-block for M == 1) straight from the
-//    packed bytes: nibbles are moved into byte lanes, turned into floats with
-//    a byte permute into a 2^23 magic exponent and one packed fp32x2 add, and
-//    accumulated with packed fp32x2 FMAs.  Q4_K/Q5_K values are formed as
-//    w = (d*sc)*q - dmin*m before the product with x (keeps the error
-//    relative to |x*w| where the two terms cancel); Q6_K applies
-//    a = x*(d*scale) to q - 32.
-//  * Partial sums of the 8 warps are added in shared memory in a fixed order;
-//    tiles split over several CTAs go through a small partials buffer and
-//    the last CTA to arrive (an atomic counter per tile, reset after use)
-//    adds the partials in CTA order, so results are deterministic.
+//  * Each of the 8 warps of a CTA takes every 8th row of the CTA's range and
+//    streams its own rows into a private shared-memory ring (STAGES slots,
+//    one mbarrier each): lane 0 issues one cp.async.bulk (no multicast) per
+//    row chunk, refilling a slot right after its row is decoded.  There is
+//    no producer warp and no cross-warp wait outside the tile flushes.  The
+//    first STAGES rows are requested before griddepcontrol.wait, so the
+//    weight stream overlaps the tail of the previous kernel when launched
+//    with programmatic stream serialization.  x for 32 rows at a time sits
+//    one value per lane and reaches each row through a shuffle.
+//  * Lane l decodes VPT consecutive values of the row (64 for M == 1 on wide
+//    matrices, else 32 / 32 / 16 / 8 for M = 1 / 2 / 4 / 8), in groups of at
+//    most 32 that never straddle a super-block, straight from the packed
+//    bytes: nibbles are merged into byte lanes, each value is moved into a
+//    word of its own by one byte permute and used as a float as it is (the
+//    integer q is the subnormal q * 2^-149; the multipliers carry a
+//    power-of-two scale that undoes it), and accumulated with packed fp32x2
+//    FMAs: a = x*(d*scale) times q per value (Q6_K; 32*a once per row and
+//    lane into a correction sum applied at the flush), or w = (d*sc)*q -
+//    dmin*m formed per value and then multiplied by x (Q4_K/Q5_K: keeps the
+//    error relative to |x*w| where the two terms cancel).
+//  * Partial sums of the 8 warps are added through shared memory in a fixed
+//    tree order; tiles split over several CTAs go through a small partials
+//    buffer and the last CTA to arrive (an atomic counter per tile, reset
+//    after use) adds the partials in CTA order, so results are deterministic.
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -41,12 +48,13 @@ namespace vkq {
 
 static __device__ int g_gemv_status;
 
-constexpr int kNW = 8;                       // consumer warps
-constexpr int kRPW = 1;                      // rows per consumer warp per stage
-constexpr int kRPS = kRPW * kNW;             // rows per ring stage
-constexpr int kThreads = (kNW + 1) * 32;     // + one producer warp
+constexpr int kNW = 8;                       // warps per CTA, each streaming its own rows
+constexpr int kThreads = kNW * 32;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
 constexpr int kSmemPerCta = 112 * 1024;      // two CTAs per SM
+constexpr int kRedSlots = 4;                 // [MR][TN] partial-sum slots of the warp reduction
+constexpr int kMaxStages = 12;               // ring slots per warp
+constexpr int kMinStages = 3;
 
 struct GemvParams {
     const uint8_t *w;
@@ -112,21 +120,55 @@ __device__ __forceinline__ bool wait_flags(const unsigned *f, int count, unsigne
 }
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
-// Q6_K: acc[m] += a[m] * (q - 32) with a = x * (d * scale).
+// Integer weights as subnormal floats.  A 6-bit quant q isolated in the low
+// bits of a 32-bit word is, read as a float, the subnormal q * 2^-149: one
+// byte permute per value makes an fma operand, with no conversion.
+//  * Q6_K: fma(a * 2^76, word, acc) adds a * q * 2^-73 with the single
+//    rounding of fma(a, float(q), acc * 2^73); the flush multiplies by 2^73.
+//    Exact while |a| < 2^52 (a * 2^76 finite) and |a * q| >= 2^-53 or 0.
+//  * Q4_K / Q5_K: fma(d*sc * 2^100, word, -dmin*m * 2^-49) is the weight
+//    w = d*sc*q - dmin*m times 2^-49 with one rounding (all three terms stay
+//    normal for f16 d, dmin and 6-bit sc, m), and x * 2^49 restores the scale
+//    in the product with x.
+constexpr float kQ6Scale = 0x1p76f;     // Q6_K per-row multipliers
+constexpr float kQ6Unscale = 0x1p73f;   // Q6_K accumulators at the flush
+constexpr float kQ45Scale = 0x1p100f;   // Q4_K / Q5_K d*sc
+constexpr float kQ45Down = 0x1p-49f;    // Q4_K / Q5_K -dmin*m (and 1 / the x scale)
+constexpr float kQ45XScale = 0x1p49f;   // Q4_K / Q5_K x
+// Q6_K takes the subnormal product with a correction sum for MR <= 2 and
+// the exact 2^23 form for MR >= 4 (accum_chunk_magic).
+template <int MR> constexpr bool kQ6Split = MR <= 2;
+constexpr float kQ6MagicScale = 0x1p-73f;  // Q6_K per-row multipliers of the 2^23 form
+
+// Q6_K: acc[m][pair0 + j] += a[m] * (value 2j, value 2j+1) of an 8-value
+// chunk; byte lane j of E / O holds value 2j / 2j+1.
 template <int MR, int NP>
-__device__ __forceinline__ void accum_chunk_scaled(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
-                                                   const float (&a)[MR], float magic) {
-    const uint64_t negm = pk2(-magic, -magic);
+__device__ __forceinline__ void accum_chunk_scaled(float2 (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
+                                                   const float (&a)[MR]) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        float fe, fo;
-        if (j == 0) { fe = byte_as_magic<0>(E); fo = byte_as_magic<0>(O); }
-        if (j == 1) { fe = byte_as_magic<1>(E); fo = byte_as_magic<1>(O); }
-        if (j == 2) { fe = byte_as_magic<2>(E); fo = byte_as_magic<2>(O); }
-        if (j == 3) { fe = byte_as_magic<3>(E); fo = byte_as_magic<3>(O); }
-        const uint64_t q2 = fadd2(pk2(fe, fo), negm);
+        const float2 q2 = make_float2(__uint_as_float(prmt(E, 0u, 0x4440u | j)),
+                                      __uint_as_float(prmt(O, 0u, 0x4440u | j)));
 #pragma unroll
-        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = ffma2(pk2(a[m], a[m]), q2, acc[m][pair0 + j]);
+        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = f2fma(make_float2(a[m], a[m]), q2, acc[m][pair0 + j]);
+    }
+}
+
+// Q6_K for MR >= 4, where the correction sums would cost registers the MR
+// accumulators need and one more packed add per pair is small beside the MR
+// FMAs: acc[m] += a'[m] * (q - 32) with the value q - 32 formed exactly by a
+// byte permute into the exponent of 2^23 and one packed add of -(2^23 + 32);
+// a' = a * 2^-73 (kQ6MagicScale) so that the flush treats both forms alike.
+template <int MR, int NP>
+__device__ __forceinline__ void accum_chunk_magic(float2 (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
+                                                  const float (&a)[MR]) {
+    const float2 neg = make_float2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const float2 q2 = f2add(make_float2(__uint_as_float(prmt(E, 0x4B000000u, 0x7440u | j)),
+                                            __uint_as_float(prmt(O, 0x4B000000u, 0x7440u | j))), neg);
+#pragma unroll
+        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = f2fma(make_float2(a[m], a[m]), q2, acc[m][pair0 + j]);
     }
 }
 
@@ -135,29 +177,26 @@ __device__ __forceinline__ void accum_chunk_scaled(uint64_t (&acc)[MR][NP], int 
 // Forming w first keeps the error relative to |x*w| even where scale*q and
 // min nearly cancel.
 template <int MR, int NP>
-__device__ __forceinline__ void accum_chunk_affine(uint64_t (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
-                                                   float scale, float mn, const float (&xv)[MR]) {
-    const uint64_t negm = pk2(-8388608.0f, -8388608.0f);
-    const uint64_t s2 = pk2(scale, scale), nm2 = pk2(-mn, -mn);
+__device__ __forceinline__ void accum_chunk_affine(float2 (&acc)[MR][NP], int pair0, uint32_t E, uint32_t O,
+                                                   float2 s2, float2 nm2, const float (&xs)[MR]) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        float fe, fo;
-        if (j == 0) { fe = byte_as_magic<0>(E); fo = byte_as_magic<0>(O); }
-        if (j == 1) { fe = byte_as_magic<1>(E); fo = byte_as_magic<1>(O); }
-        if (j == 2) { fe = byte_as_magic<2>(E); fo = byte_as_magic<2>(O); }
-        if (j == 3) { fe = byte_as_magic<3>(E); fo = byte_as_magic<3>(O); }
-        const uint64_t q2 = fadd2(pk2(fe, fo), negm);
-        const uint64_t w2 = ffma2(s2, q2, nm2);
+        const float2 q2 = make_float2(__uint_as_float(prmt(E, 0u, 0x4440u | j)),
+                                      __uint_as_float(prmt(O, 0u, 0x4440u | j)));
+        const float2 w2 = f2fma(s2, q2, nm2);
 #pragma unroll
-        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = ffma2(pk2(xv[m], xv[m]), w2, acc[m][pair0 + j]);
+        for (int m = 0; m < MR; m++) acc[m][pair0 + j] = f2fma(make_float2(xs[m], xs[m]), w2, acc[m][pair0 + j]);
     }
 }
 
 // Decode VPT values of one super-block (shared address blk, first value
-// `within`) and accumulate x[m] * W into acc.
+// `within`) and accumulate x[m] * W into acc.  Q6_K, w = (d*scale)*(q - 32):
+// acc gets a*q with a = x*d*scale (scaled by 2^76) and corr[m] (one
+// component per 16-value scale group) the sum of a, taken 32 times at the
+// flush.  Q4_K / Q5_K accumulate x*w directly (corr unused).
 template <int QT, int MR, int VPT>
 __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const float (&xv)[MR],
-                                             uint64_t (&acc)[MR][VPT / 2]) {
+                                             float2 (&acc)[MR][VPT / 2], float2 (&corr)[MR]) {
     constexpr int NCH = VPT / 8;  // chunks of 8 values
     if constexpr (QT == kQ4K || QT == kQ5K) {
         const uint4 hdr = lds128(blk);
@@ -166,8 +205,12 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
         const uint32_t sc24 = sb < 4 ? hdr.y : __funnelshift_r(hdr.y, hdr.z, 24);
         const uint32_t m24 = sb < 4 ? __funnelshift_r(hdr.z, hdr.w, 16) : (hdr.w >> 8);
         const uint32_t sh = 6u * (sb & 3);
-        const float ds = d * (float)((sc24 >> sh) & 63u);
-        const float dm = dmin * (float)((m24 >> sh) & 63u);
+        const float ds = (d * kQ45Scale) * (float)((sc24 >> sh) & 63u);
+        const float ndm = (dmin * -kQ45Down) * (float)((m24 >> sh) & 63u);
+        const float2 s2 = make_float2(ds, ds), nm2 = make_float2(ndm, ndm);
+        float xs[MR];
+#pragma unroll
+        for (int m = 0; m < MR; m++) xs[m] = xv[m] * kQ45XScale;
         const uint32_t qs = blk + (QT == kQ4K ? 16 : 48) + (within >> 1);
         uint32_t wq[NCH];
         if constexpr (NCH == 4) {
@@ -197,10 +240,10 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
                 E |= ((hb & 0x55u) * 0x410410u) & 0x10101010u;
                 O |= (((hb >> 1) & 0x55u) * 0x410410u) & 0x10101010u;
             }
-            accum_chunk_affine<MR, VPT / 2>(acc, 4 * c, E, O, ds, dm, xv);
+            accum_chunk_affine<MR, VPT / 2>(acc, 4 * c, E, O, s2, nm2, xs);
         }
     } else {  // Q6_K: blk is only 2-byte aligned in shared memory
-        const float d = hw_f16_to_f32(lds16(blk + 208));
+        const float d = hw_f16_to_f32(lds16(blk + 208)) * (kQ6Split<MR> ? kQ6Scale : kQ6MagicScale);
         const int g0 = within >> 4;  // first 16-value scale group
         const uint32_t sraw = lds16(blk + 192 + (g0 & ~1));
         const int s0 = (int)(int8_t)((g0 & 1) ? (sraw >> 8) : sraw);
@@ -211,6 +254,10 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
         for (int m = 0; m < MR; m++) {
             a0[m] = xv[m] * ds0;
             a1[m] = xv[m] * ds1;
+            if constexpr (kQ6Split<MR>) {
+                if constexpr (NCH == 4) corr[m] = f2add(corr[m], make_float2(a0[m], a1[m]));
+                else corr[m].x += a0[m];
+            }
         }
         const uint32_t ql = blk + (within >> 1);
         const uint32_t qha = blk + 128 + (within >> 2);
@@ -237,21 +284,28 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
         for (int i = 0; i < (NCH + 1) / 2; i++) qhs[i] = qh[i] >> 4;
 #pragma unroll
         for (int c = 0; c < NCH; c++) {
-            // byte lane j of X = nibble j of the chunk's 16 qh bits
-            //                  = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
-            const uint32_t X = prmt(qh[c >> 1], qhs[c >> 1], (c & 1) ? 0x7362u : 0x5140u) & 0x0F0F0F0Fu;
-            const uint32_t E = (wq[c] & 0x0F0F0F0Fu) | ((X & 0x03030303u) << 4);
+            // the low nibble of byte lane j of X is nibble j of the chunk's
+            // 16 qh bits = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
+            const uint32_t X = prmt(qh[c >> 1], qhs[c >> 1], (c & 1) ? 0x7362u : 0x5140u);
+            const uint32_t E = (wq[c] & 0x0F0F0F0Fu) | ((X << 4) & 0x30303030u);
             const uint32_t O = ((wq[c] >> 4) & 0x0F0F0F0Fu) | ((X << 2) & 0x30303030u);
-            if (NCH == 4 && c >= 2) accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a1, 8388640.0f);
-            else accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a0, 8388640.0f);  // 2^23 + 32
+            if constexpr (kQ6Split<MR>) {
+                if (NCH == 4 && c >= 2) accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a1);
+                else accum_chunk_scaled<MR, VPT / 2>(acc, 4 * c, E, O, a0);
+            } else {
+                accum_chunk_magic<MR, VPT / 2>(acc, 4 * c, E, O, a0);  // MR >= 4: VPT <= 16, one group
+            }
         }
     }
 }
 
+// XOR swizzle of a lane's float4 slots in the reduction buffer: the 8 lanes
+// of a quarter warp store to 8 different 16-byte bank groups.
 template <int VPT>
 __device__ __forceinline__ int red_swz(int lane) {
     constexpr int F = VPT / 4;  // float4 per lane
-    return (lane / (8 / F)) & (F - 1);
+    if constexpr (F >= 8) return lane & 7;
+    else return (lane / (8 / F)) & (F - 1);
 }
 
 // G: the all-gather variant (outputs stored into every rank's buffer, with
@@ -262,132 +316,124 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     constexpr int TN = 32 * VPT;
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = p.stages;
+    // [kNW][S] mbarriers | 2 flag words | ring [kNW][S][row_cap] | red [kRedSlots][MR][TN]
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + S;
-    int *flag = reinterpret_cast<int *>(empty + S);
-    const int hdr_bytes = ((16 * S + 16) + 127) & ~127;
+    int *flag = reinterpret_cast<int *>(full + kNW * S);
+    const int hdr_bytes = ((8 * kNW * S + 8) + 127) & ~127;
     uint8_t *ring = smem + hdr_bytes;
-    float *red = reinterpret_cast<float *>(ring + (size_t)S * kRPS * p.row_cap);
-    float *xbuf = red + kNW * MR * TN;  // [S][kRPS][MR]: x of each ring row
+    float *red = reinterpret_cast<float *>(ring + (size_t)kNW * S * p.row_cap);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x;  // 0..255
     const int64_t f0 = (int64_t)blockIdx.x * p.rpc;
     const int64_t f1 = imin64(f0 + p.rpc, p.rows_total);
-    const int64_t nrows = f1 - f0;
-    const int64_t nst = (nrows + kRPS - 1) / kRPS;
+    const int nrows = (int)(f1 - f0);
+    // this warp's rows: f0 + warp + kNW * j for j < nw
+    const int nw = nrows > warp ? (nrows - warp + kNW - 1) / kNW : 0;
     const int64_t K = p.K, N = p.N;
+    const uint32_t Ku = (uint32_t)K, Nu = (uint32_t)N;
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(smem_u32addr(&full[s]), 2);  // bytes posted + x stored
-            mbar_init(smem_u32addr(&empty[s]), kNW);
-        }
+    uint64_t *my_full = full + warp * S;
+    uint8_t *my_ring = ring + (size_t)warp * S * p.row_cap;
+    const uint32_t my_ring_u32 = smem_u32addr(my_ring);
+    if (lane == 0) {
+        for (int s = 0; s < S; s++) mbar_init(smem_u32addr(&my_full[s]), 1);
         mbar_init_fence();
     }
-    __syncthreads();
+    __syncwarp();
 
-    if (warp == kNW) {
-        // ------------------------------ producer ------------------------------
-        // The 32 lanes prepare 32 / kRPS stages of kRPS rows at once: lane l
-        // owns row (l % kRPS) of stage (batch + l / kRPS).  Each stage's byte
-        // count is summed over its lanes, the stage leader posts expect_tx,
-        // then every lane issues its own bulk copy.
-        constexpr int kSPB = 32 / kRPS;  // stages per producer batch
-        const uint32_t ring_base = smem_u32addr(ring);
-        const int r = lane % kRPS, sub = lane / kRPS;
-        const uint32_t Ku = (uint32_t)K;
-        uint32_t t, kk;  // (tile, k) of this lane's row in the current batch
-        {
-            const int64_t f = f0 + lane;
-            t = (uint32_t)(f / K);
-            kk = (uint32_t)(f - (int64_t)t * K);
+    // Per-row parameters are computed 32 rows at a time, one row per lane,
+    // and reach the lane that uses them through a shuffle.
+    //   issue side: byte offset of the row chunk's 16-byte aligned span of
+    //   super-blocks and its length (bulk copy), plus the < 16 bytes past the
+    //   last 16-byte boundary of w (copied by hand);
+    //   decode side: the low 32 bits of v0 = k*ld + n_base + n0 (in-block
+    //   offset of the row's first value and the 16-byte lead of its first
+    //   block), the first column n0 of the row's tile, and x of the row.
+    auto row_tk = [&](int r, uint32_t &t, uint32_t &k) {
+        const uint32_t f = (uint32_t)(f0 + warp) + (uint32_t)(kNW * r);  // rows_total < 2^31
+        t = f / Ku;
+        k = f - t * Ku;
+    };
+    uint32_t i_src = 0, i_len = 0;  // issue parameters of row ib + lane
+    auto issue_batch = [&](int ib) {
+        const int r = ib + lane;
+        i_src = 0;
+        i_len = 0;
+        if (r < nw) {
+            uint32_t t, k;
+            row_tk(r, t, k);
+            const int64_t n0 = (int64_t)t * TN, n1 = imin64(n0 + TN, N);
+            const int64_t base = G ? (int64_t)k * gq.ld + gq.n_base : (int64_t)k * N;
+            const int64_t a_lo = (((base + n0) >> 8) * B) & ~int64_t(15);
+            const int64_t byte_hi = ((base + n1 + 255) >> 8) * B;
+            int64_t c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
+            if (c_hi < a_lo) c_hi = a_lo;
+            i_src = (uint32_t)a_lo;  // weights are below 4 GiB on this path
+            const int64_t tail = byte_hi > c_hi ? byte_hi - c_hi : 0;  // < 16
+            i_len = (uint32_t)(c_hi - a_lo) | ((uint32_t)tail << 24);
         }
-        const int nst32 = (int)nst, nrows32 = (int)nrows;
-        int st = sub, slot = sub;  // this lane's stage and its ring slot (S >= kSPB)
-        uint32_t round = 0;        // st / S
-        float xr[MR];
-        for (int sb = 0; sb < nst32; sb += kSPB) {
-            const bool stage_ok = st < nst32;
-            if (stage_ok && round > 0) {
-                if (!mbar_wait_bounded(smem_u32addr(&empty[slot]), (round - 1) & 1u, kWaitNs))
-                    set_status(kStatusTimeout);
-            }
-            const bool row_ok = stage_ok && (st * kRPS + r) < nrows32;
-            int64_t a_lo = 0, c_hi = 0, byte_hi = 0;
-            if (row_ok) {
-                const int64_t n0 = (int64_t)t * TN, n1 = imin64(n0 + TN, N);
-                const int64_t base = G ? (int64_t)kk * gq.ld + gq.n_base : (int64_t)kk * N;
-                a_lo = (((base + n0) >> 8) * B) & ~int64_t(15);
-                byte_hi = ((base + n1 + 255) >> 8) * B;
-                c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
-                if (c_hi < a_lo) c_hi = a_lo;
-                for (int64_t bb = c_hi; bb < byte_hi; bb++)  // < 16 tail bytes at the very end of w
-                    ring[(slot * kRPS + r) * p.row_cap + (bb - a_lo)] = p.w[bb];
-            }
-            const uint32_t bytes = (uint32_t)(c_hi - a_lo);
-            uint32_t total = bytes;
-            total += __shfl_xor_sync(0xffffffffu, total, 1);
-            total += __shfl_xor_sync(0xffffffffu, total, 2);
-            total += __shfl_xor_sync(0xffffffffu, total, 4);
-            if (kRPS > 8) total += __shfl_xor_sync(0xffffffffu, total, 8);
-            __syncwarp();
-            if (stage_ok && r == 0) mbar_arrive_expect_tx(smem_u32addr(&full[slot]), total);
-            __syncwarp();
-            if (row_ok && bytes > 0)
-                bulk_g2s(ring_base + (uint32_t)((slot * kRPS + r) * p.row_cap), p.w + a_lo, bytes,
-                         smem_u32addr(&full[slot]));
-            if (sb == 0) {
-                pdl_launch_dependents();
-                pdl_wait();  // x comes from the preceding kernel; weights did not
-#pragma unroll
-                for (int m = 0; m < MR; m++)
-                    xr[m] = (row_ok && m < p.M) ? __ldg(p.x + (int64_t)m * K + kk) : 0.0f;
-            }
-            // x of this row for every m (loaded one batch ahead), then the
-            // stage's second arrival
-            if (stage_ok) {
-#pragma unroll
-                for (int m = 0; m < MR; m++) xbuf[(slot * kRPS + r) * MR + m] = xr[m];
-            }
-            __syncwarp();
-            if (stage_ok && r == 0) mbar_arrive(smem_u32addr(&full[slot]));
-            st += kSPB;
-            slot += kSPB;
-            if (slot >= S) {
-                slot -= S;
-                round++;
-            }
-            kk += kSPB * kRPS;
-            while (kk >= Ku) {
-                kk -= Ku;
-                t++;
-            }
-            {
-                const bool next_ok = st < nst32 && (st * kRPS + r) < nrows32;
-#pragma unroll
-                for (int m = 0; m < MR; m++)
-                    xr[m] = (next_ok && m < p.M) ? __ldg(p.x + (int64_t)m * K + kk) : 0.0f;
-            }
+    };
+    // Lane 0 streams this warp's row ji into ring slot sl.
+    int ji = 0;
+    auto issue_next = [&](int sl) {
+        if ((ji & 31) == 0) issue_batch(ji);
+        const uint32_t src = __shfl_sync(0xffffffffu, i_src, ji & 31);
+        const uint32_t len = __shfl_sync(0xffffffffu, i_len, ji & 31);
+        if (lane == 0) {
+            const uint32_t bytes = len & 0xFFFFFFu, tail = len >> 24;
+            uint8_t *dst = my_ring + (size_t)sl * p.row_cap;
+            for (uint32_t b = 0; b < tail; b++) dst[bytes + b] = p.w[(int64_t)src + bytes + b];
+            const uint32_t bar = smem_u32addr(&my_full[sl]);
+            mbar_arrive_expect_tx(bar, bytes);
+            if (bytes > 0) bulk_g2s(my_ring_u32 + (uint32_t)(sl * p.row_cap), p.w + src, bytes, bar);
         }
-        if (nst == 0) {
-            pdl_launch_dependents();
-            pdl_wait();
-        }
-        return;
-    }
+        ji++;
+    };
+    // the weights do not depend on the preceding kernel: fill the ring first
+    for (int s = 0; s < S && ji < nw; s++) issue_next(s);
+    pdl_launch_dependents();
+    pdl_wait();  // x, y and the workspace may belong to the preceding kernel
 
-    // ------------------------------ consumers ------------------------------
-    // Warp w handles rows w, w + 8, ... (kRPW of them) of every stage.
-    const uint32_t ring_base = smem_u32addr(ring);
+    uint32_t c_n0 = 0, c_v0 = 0;  // decode parameters of row jb + lane
+    auto decode_batch = [&](int jb) {
+        const int r = jb + lane;
+        if (r < nw) {
+            uint32_t t, k;
+            row_tk(r, t, k);
+            c_n0 = t * TN;
+            if constexpr (G) c_v0 = k * (uint32_t)gq.ld + (uint32_t)gq.n_base + c_n0;
+            else c_v0 = k * Nu + c_n0;
+        }
+    };
+    auto load_x = [&](int jb, float (&xr)[MR]) {
+        const int r = jb + lane;
+        uint32_t kx = 0;
+        if (r < nw) kx = ((uint32_t)(f0 + warp) + (uint32_t)(kNW * r)) % Ku;
+#pragma unroll
+        for (int m = 0; m < MR; m++) xr[m] = (r < nw && m < p.M) ? __ldg(p.x + (int64_t)m * K + kx) : 0.0f;
+    };
+    float xcur[MR], xnext[MR];
+    load_x(0, xcur);
+    load_x(32, xnext);
+    decode_batch(0);
+
     const uint32_t red_base = smem_u32addr(red);
-    const int tid = threadIdx.x;  // 0..255
-    uint64_t acc[MR][VPT / 2];
+    // H groups of VH <= 32 consecutive values per lane (two for VPT = 64);
+    // a group never straddles a super-block
+    constexpr int H = VPT > 32 ? VPT / 32 : 1;
+    constexpr int VH = VPT / H;
+    float2 acc[H][MR][VH / 2];
+    float2 corr[H][MR];
 #pragma unroll
-    for (int m = 0; m < MR; m++) {
+    for (int h = 0; h < H; h++) {
 #pragma unroll
-        for (int i = 0; i < VPT / 2; i++) acc[m][i] = 0ull;
+        for (int m = 0; m < MR; m++) {
+#pragma unroll
+            for (int i = 0; i < VH / 2; i++) acc[h][m][i] = make_float2(0.f, 0.f);
+            corr[h][m] = make_float2(0.f, 0.f);
+        }
     }
-    pdl_wait();  // y and the workspace may belong to the preceding kernel
 
     // All-gather: this call's number, and (CTA 0) the "started" flag on every
     // rank.  A CTA's first output store waits until every rank has started
@@ -410,21 +456,75 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     int64_t cur_tile = first_tile;
     int64_t next_boundary = (cur_tile + 1) * K - f0;
 
-    auto flush = [&](int64_t tile) {
-        // 1. per-warp partials into shared memory (swizzled float4 slots)
+    // this lane's float4 i (of VPT / 4) of row m in slot sl of the reduction buffer
+    auto red_addr = [&](int sl, int m, int i) {
+        return red_base + (uint32_t)(((sl * MR + m) * TN + lane * VPT + 4 * (i ^ red_swz<VPT>(lane))) * 4);
+    };
+    auto store_red = [&](int sl) {
 #pragma unroll
         for (int m = 0; m < MR; m++) {
 #pragma unroll
             for (int i = 0; i < VPT / 4; i++) {
-                float v0, v1, v2, v3;
-                upk2(acc[m][2 * i], v0, v1);
-                upk2(acc[m][2 * i + 1], v2, v3);
-                const int phys = lane * VPT + 4 * (i ^ red_swz<VPT>(lane));
-                const uint32_t addr = red_base + (uint32_t)(((warp * MR + m) * TN + phys) * 4);
-                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v0), "f"(v1), "f"(v2),
-                             "f"(v3));
-                acc[m][2 * i] = 0ull;
-                acc[m][2 * i + 1] = 0ull;
+                const float2 u = acc[i / (VH / 4)][m][2 * (i % (VH / 4))];
+                const float2 v = acc[i / (VH / 4)][m][2 * (i % (VH / 4)) + 1];
+                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(red_addr(sl, m, i)), "f"(u.x), "f"(u.y),
+                             "f"(v.x), "f"(v.y));
+            }
+        }
+    };
+    auto add_red = [&](int sl) {
+#pragma unroll
+        for (int m = 0; m < MR; m++) {
+#pragma unroll
+            for (int i = 0; i < VPT / 4; i++) {
+                float4 t4;
+                asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                             : "=f"(t4.x), "=f"(t4.y), "=f"(t4.z), "=f"(t4.w) : "r"(red_addr(sl, m, i)));
+                float2 &u = acc[i / (VH / 4)][m][2 * (i % (VH / 4))];
+                float2 &v = acc[i / (VH / 4)][m][2 * (i % (VH / 4)) + 1];
+                u = f2add(u, make_float2(t4.x, t4.y));
+                v = f2add(v, make_float2(t4.z, t4.w));
+            }
+        }
+    };
+
+    auto flush = [&](int64_t tile) {
+        // 1. Q6_K: value = acc * 2^73 - 32 * sum(a) (one rounding), in place
+        if constexpr (QT == kQ6K) {
+#pragma unroll
+            for (int h = 0; h < H; h++) {
+#pragma unroll
+                for (int m = 0; m < MR; m++) {
+                    const float c_lo = corr[h][m].x * -0x1p-71f;  // -32 * sum(a) / 2^76, values [0, 16)
+                    const float c_hi = corr[h][m].y * -0x1p-71f;  // values [16, 32) of the group
+#pragma unroll
+                    for (int i = 0; i < VH / 2; i++) {
+                        const float c = (VH == 32 && i >= 8) ? c_hi : c_lo;
+                        acc[h][m][i] = make_float2(fmaf(acc[h][m][i].x, kQ6Unscale, c),
+                                                   fmaf(acc[h][m][i].y, kQ6Unscale, c));
+                    }
+                    corr[h][m] = make_float2(0.f, 0.f);
+                }
+            }
+        }
+        // 2. sum over the 8 warps in a fixed order through kRedSlots slots:
+        //    w += w + 4, then w += w + 2; warps 0 and 1 leave the two halves
+        //    in slots 0 and 1
+        if (warp >= 4) store_red(warp - 4);
+        named_bar_sync(1, kNW * 32);
+        if (warp < 4) add_red(warp);
+        named_bar_sync(1, kNW * 32);
+        if (warp >= 2 && warp < 4) store_red(warp - 2);
+        named_bar_sync(1, kNW * 32);
+        if (warp < 2) add_red(warp);
+        named_bar_sync(1, kNW * 32);
+        if (warp < 2) store_red(warp);
+#pragma unroll
+        for (int h = 0; h < H; h++) {
+#pragma unroll
+            for (int m = 0; m < MR; m++) {
+#pragma unroll
+                for (int i = 0; i < VH / 2; i++) acc[h][m][i] = make_float2(0.f, 0.f);
             }
         }
         if constexpr (G) {
@@ -434,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             }
         }
         named_bar_sync(1, kNW * 32);
-        // 2. fixed-order sum over the warps
+        // 3. slot 0 + slot 1, stored coalesced
         const int64_t n0 = tile * TN;
         const int ncols = (int)imin64(TN, N - n0);
         const bool whole = (tile * K >= f0) && ((tile + 1) * K <= f1);
@@ -444,9 +544,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             if (m >= p.M || c >= ncols) continue;
             const int L = c / VPT, i = (c % VPT) / 4;
             const int phys = L * VPT + 4 * (i ^ red_swz<VPT>(L)) + (c & 3);
-            float sum = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
+            const float sum = red[m * TN + phys] + red[(MR + m) * TN + phys];
             if (whole) {
                 if constexpr (G) store_peers(gq, m, n0 + c, sum);
                 else p.y[(int64_t)m * N + n0 + c] = sum;
@@ -507,56 +605,50 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         }
     };
 
-    // this warp's row: local index pl, (tile, k) = (t, kk); slot/phase of the ring
-    static_assert(kRPW == 1, "one row per consumer warp per stage");
-    const uint32_t Ku = (uint32_t)K;
-    const int nst32 = (int)nst, nrows32 = (int)nrows;
-    uint32_t t, kk;
-    {
-        const int64_t f = f0 + warp;
-        t = (uint32_t)(f / K);
-        kk = (uint32_t)(f - (int64_t)t * K);
-    }
+    // this warp's row j: CTA-local index pl; its ring slot / phase
     int pl = warp;
     int nb32 = (int)next_boundary;
-    uint32_t slot = 0, phase = 0;
-    const uint32_t warp_row0 = ring_base + (uint32_t)(warp * p.row_cap);
-    const uint32_t stage_bytes = (uint32_t)(kRPS * p.row_cap);
-    const uint32_t Nu = (uint32_t)N;
+    int slot = 0, prev_slot = S - 1;
+    uint32_t phase = 0;
 
-    for (int s = 0; s < nst32; s++) {
-        if (!mbar_wait_bounded(smem_u32addr(&full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
-        if (pl < nrows32) {
-            while (pl >= nb32) {
-                flush(cur_tile);
-                cur_tile++;
-                nb32 += (int)K;
-            }
-            const uint32_t n0 = t * TN;
-            if ((int64_t)n0 + lane * VPT < N) {
-                // low 32 bits of v0 = k*ld + n_base + n0 give the in-block offset
-                // of the row's first value and the 16-byte lead of its first block
-                uint32_t v0;
-                if constexpr (G) v0 = kk * (uint32_t)gq.ld + (uint32_t)gq.n_base + n0;
-                else v0 = kk * Nu + n0;
-                const uint32_t lead = (((v0 >> 8) & 15u) * (uint32_t)B) & 15u;
-                const uint32_t wl = (v0 & 255u) + lane * VPT;
-                const uint32_t blk = warp_row0 + slot * stage_bytes + (wl >> 8) * B + lead;
-                float xv[MR];
+    for (int j = 0; j < nw; j++) {
+        if (!mbar_wait_bounded(smem_u32addr(&my_full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
+        while (pl >= nb32) {
+            flush(cur_tile);
+            cur_tile++;
+            nb32 += (int)K;
+        }
+        const int jj = j & 31;
+        float xv[MR];
 #pragma unroll
-                for (int m = 0; m < MR; m++) xv[m] = xbuf[(slot * kRPS + warp) * MR + m];
-                decode_accum<QT, MR, VPT>(blk, (int)(wl & 255u), xv, acc);
+        for (int m = 0; m < MR; m++) xv[m] = __shfl_sync(0xffffffffu, xcur[m], jj);
+        const uint32_t n0 = __shfl_sync(0xffffffffu, c_n0, jj);
+        const uint32_t v0 = __shfl_sync(0xffffffffu, c_v0, jj);
+        if (jj == 31) {
+#pragma unroll
+            for (int m = 0; m < MR; m++) xcur[m] = xnext[m];
+            load_x(j + 33, xnext);
+            decode_batch(j + 1);
+        }
+        if (n0 + lane * VPT < Nu) {
+            const uint32_t lead = (((v0 >> 8) & 15u) * (uint32_t)B) & 15u;
+            const uint32_t wl = (v0 & 255u) + lane * VPT;
+            const uint32_t row = my_ring_u32 + (uint32_t)(slot * p.row_cap) + lead;
+#pragma unroll
+            for (int h = 0; h < H; h++) {
+                const uint32_t wh = wl + h * VH;
+                // (N is a multiple of 32: a lane's second group may lie past N)
+                if (h == 0 || n0 + lane * VPT + h * VH < Nu)
+                    decode_accum<QT, MR, VH>(row + (wh >> 8) * B, (int)(wh & 255u), xv, acc[h], corr[h]);
             }
         }
+        // Refill the previous row's slot (every lane has long finished
+        // reading it) with the row S - 1 ahead of this one.
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32addr(&empty[slot]));
-        kk += kRPS;
-        while (kk >= Ku) {
-            kk -= Ku;
-            t++;
-        }
-        pl += kRPS;
-        if (++slot == (uint32_t)S) {
+        if (j >= 1 && ji < nw) issue_next(prev_slot);
+        pl += kNW;
+        prev_slot = slot;
+        if (++slot == S) {
             slot = 0;
             phase ^= 1u;
         }
@@ -644,9 +736,16 @@ static Plan make_plan(const GemvShape &s, int device) {
     const int64_t wbytes = ((s.K * s.N + 255) / 256) * block_bytes(s.qtype);
     pl.generic = (s.N % 32) != 0 || wbytes >= (int64_t(1) << 32) - 4096;
     if (pl.generic) return pl;
-    if (s.M <= 1) { pl.mr = 1; pl.vpt = 32; }
-    else if (s.M <= 2) { pl.mr = 2; pl.vpt = 16; }
-    else if (s.M <= 4) { pl.mr = 4; pl.vpt = 8; }
+    if (s.M <= 1) {
+        // 64 values per lane (2048-column tiles) halve the per-row work and
+        // the bulk copies per value; taken when the ragged last tile wastes
+        // little and there are enough tiles to keep the split-K fan-in low
+        const int64_t nt64 = (s.N + 2047) / 2048;
+        const bool wide = nt64 >= 16 && (nt64 * 2048 - s.N) * 32 <= s.N;
+        pl.mr = 1;
+        pl.vpt = wide ? 64 : 32;
+    } else if (s.M <= 2) { pl.mr = 2; pl.vpt = 32; }
+    else if (s.M <= 4) { pl.mr = 4; pl.vpt = 16; }
     else { pl.mr = 8; pl.vpt = 8; }
     pl.tn = 32 * pl.vpt;
     if ((s.N + pl.tn - 1) / pl.tn > (int64_t)(kWorkspaceCounterHead / 4)) {
@@ -655,6 +754,10 @@ static Plan make_plan(const GemvShape &s, int device) {
     }
     pl.ntiles = (int)((s.N + pl.tn - 1) / pl.tn);
     const int64_t rows_total = (int64_t)pl.ntiles * s.K;
+    if (rows_total >= (int64_t(1) << 31) || s.N >= (int64_t(1) << 31)) {
+        pl.generic = true;  // row indices and columns are kept in 32 bits
+        return pl;
+    }
     const int sms = device_sm_count(device);
     int64_t grid = (int64_t)sms * 2;
     if (grid > rows_total) grid = rows_total;
@@ -662,13 +765,12 @@ static Plan make_plan(const GemvShape &s, int device) {
     pl.grid = (int)((rows_total + pl.rpc - 1) / pl.rpc);
     const int B = block_bytes(s.qtype);
     pl.row_cap = (((pl.tn / 256 + 1) * B + 16 + 16) + 15) & ~15;
-    const size_t red = (size_t)kNW * pl.mr * pl.tn * 4;
-    int stages = 8;
+    const size_t red = (size_t)kRedSlots * pl.mr * pl.tn * 4;
     auto smem_for = [&](int st) {
-        return (size_t)(((16 * st + 16) + 127) & ~127) + (size_t)st * kRPS * pl.row_cap + red +
-               (size_t)st * kRPS * pl.mr * 4;
+        return (size_t)(((8 * kNW * st + 8) + 127) & ~127) + (size_t)kNW * st * pl.row_cap + red;
     };
-    while (stages > 4 && smem_for(stages) > (size_t)kSmemPerCta) stages--;
+    int stages = kMaxStages;
+    while (stages > kMinStages && smem_for(stages) > (size_t)kSmemPerCta) stages--;
     pl.stages = stages;
     pl.smem = smem_for(stages);
     pl.partial_bytes = ((size_t)pl.grid * 2 * pl.mr * pl.tn * 4 + 255) & ~size_t(255);
@@ -706,9 +808,12 @@ static cudaError_t launch_fast(const GemvParams &gp, const GatherParams &gq, con
 template <int QT>
 static cudaError_t dispatch_mr(const GemvParams &gp, const GatherParams &gq, const Plan &pl, cudaStream_t st) {
     switch (pl.mr) {
-    case 1: return gq.peer_y ? launch_fast<QT, 1, 32, true>(gp, gq, pl, st) : launch_fast<QT, 1, 32, false>(gp, gq, pl, st);
-    case 2: return gq.peer_y ? launch_fast<QT, 2, 16, true>(gp, gq, pl, st) : launch_fast<QT, 2, 16, false>(gp, gq, pl, st);
-    case 4: return gq.peer_y ? launch_fast<QT, 4, 8, true>(gp, gq, pl, st) : launch_fast<QT, 4, 8, false>(gp, gq, pl, st);
+    case 1:
+        if (pl.vpt == 64)
+            return gq.peer_y ? launch_fast<QT, 1, 64, true>(gp, gq, pl, st) : launch_fast<QT, 1, 64, false>(gp, gq, pl, st);
+        return gq.peer_y ? launch_fast<QT, 1, 32, true>(gp, gq, pl, st) : launch_fast<QT, 1, 32, false>(gp, gq, pl, st);
+    case 2: return gq.peer_y ? launch_fast<QT, 2, 32, true>(gp, gq, pl, st) : launch_fast<QT, 2, 32, false>(gp, gq, pl, st);
+    case 4: return gq.peer_y ? launch_fast<QT, 4, 16, true>(gp, gq, pl, st) : launch_fast<QT, 4, 16, false>(gp, gq, pl, st);
     default: return gq.peer_y ? launch_fast<QT, 8, 8, true>(gp, gq, pl, st) : launch_fast<QT, 8, 8, false>(gp, gq, pl, st);
     }
 }
