@@ -55,6 +55,9 @@ constexpr int kSmemPerCta = 112 * 1024;      // two CTAs per SM
 constexpr int kRedSlots = 4;                 // [MR][TN] partial-sum slots of the warp reduction
 constexpr int kMaxStages = 12;               // ring slots per warp
 constexpr int kMinStages = 3;
+constexpr int kCombineLoads = 8;             // partial loads in flight per thread in the split-K sum
+constexpr int kMaxFanIn = 32;                // CTAs per tile summed in one level
+constexpr int kGroup = 16;                   // CTAs per first-level group above that
 
 struct GemvParams {
     const uint8_t *w;
@@ -68,8 +71,10 @@ struct GemvParams {
     int grid;
     int64_t rows_total;  // ntiles * K
     int64_t rpc;         // rows (tile, k) per CTA
-    float *partials;     // [grid][2][MR][TN]
-    int *counters;       // [ntiles]
+    float *partials;     // [grid][2][MR][TN]: per-CTA sums of shared tiles
+    float *gpartials;    // [ntiles + ngroups][MR][TN]: per-group sums (two-level split-K)
+    int *counters;       // [ntiles] per tile, then [ntiles + ngroups] per (tile + group)
+    int group;           // CTAs per first-level group of the split-K sum
     int row_cap;         // bytes per ring row slot (multiple of 16)
     int stages;
 };
@@ -454,6 +459,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     const int64_t first_tile = f0 / K;
     const int64_t last_tile = (f1 - 1) / K;
     int64_t cur_tile = first_tile;
+    bool pend_first = false, pend_last = false;  // shared tiles written as partials
+    int old_first = 0, old_last = 0;             // their first-level counts (thread 0)
     int64_t next_boundary = (cur_tile + 1) * K - f0;
 
     // this lane's float4 i (of VPT / 4) of row m in slot sl of the reduction buffer
@@ -552,57 +559,108 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = sum;
         }
         named_bar_sync(1, kNW * 32);
+        // A tile shared with other CTAs (only the first and the last tile of
+        // this CTA's rows): count this CTA in at once (thread 0 keeps the
+        // counter's old value; the atomic's latency overlaps the rows that
+        // follow), and sum after this CTA's last row, when the accumulators
+        // are free.
         if (!whole) {
             __threadfence();
             named_bar_sync(1, kNW * 32);
-            const int64_t cf = (tile * K) / p.rpc;
-            const int64_t cl = imin64(((tile + 1) * K - 1) / p.rpc, p.grid - 1);
             if (tid == 0) {
-                const int old = atomicAdd(&p.counters[tile], 1);
-                flag[0] = (old == (int)(cl - cf));
+                const int64_t g = blockIdx.x / p.group;
+                const int old = atomicAdd(p.counters + p.ntiles + tile + g, 1);
+                if (tile == first_tile) old_first = old;
+                else old_last = old;
             }
-            named_bar_sync(1, kNW * 32);
-            if (flag[0]) {
-                __threadfence();
-                // contributor cf starts before the tile (slot 1) unless it
-                // starts exactly on it; every later contributor starts inside
-                // the tile (slot 0).  Sum in CTA order, 4 loads in flight.
-                const int ncon = (int)(cl - cf + 1);
-                const bool cf_slot1 = cf * p.rpc < tile * K;
-                for (int idx4 = tid; idx4 < MR * TN / 4; idx4 += kNW * 32) {
-                    const int m = (idx4 * 4) / TN, c = (idx4 * 4) % TN;
-                    if (m >= p.M || c >= ncols) continue;
-                    const float *base = p.partials + (size_t)m * TN + c;
-                    float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int j0 = 0; j0 < ncon; j0 += 4) {
-                        float4 v[4];
+            if (tile == first_tile) pend_first = true;
+            else pend_last = true;
+        }
+    };
+
+    // Split-K sum of a shared tile, in two levels so that no CTA reads more
+    // than about `group` partial rows: the CTAs of the tile are cut into
+    // groups of p.group consecutive CTAs; the last CTA of a group to get here
+    // adds the group's partials in CTA order, and the last group to finish
+    // adds the group sums in group order (deterministic).  A tile whose CTAs
+    // all lie in one group is finished by the first level.
+    auto sum_rows = [&](int64_t tile, auto src, int count, auto sink) {
+        const int64_t n0 = tile * TN;
+        const int ncols = (int)imin64(TN, N - n0);
+        for (int idx4 = tid; idx4 < MR * TN / 4; idx4 += kNW * 32) {
+            const int m = (idx4 * 4) / TN, c = (idx4 * 4) % TN;
+            if (m >= p.M || c >= ncols) continue;
+            float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int j0 = 0; j0 < count; j0 += kCombineLoads) {
+                float4 v[kCombineLoads];
 #pragma unroll
-                        for (int u = 0; u < 4; u++) {
-                            const int j = j0 + u;
-                            if (j < ncon) {
-                                const int64_t cta = cf + j;
-                                const int sl = (j == 0 && cf_slot1) ? 1 : 0;
-                                v[u] = __ldcg(reinterpret_cast<const float4 *>(base + (size_t)(cta * 2 + sl) * MR * TN));
-                            }
-                        }
+                for (int u = 0; u < kCombineLoads; u++)
+                    if (j0 + u < count) v[u] = __ldcg(reinterpret_cast<const float4 *>(src(j0 + u) + (size_t)m * TN + c));
 #pragma unroll
-                        for (int u = 0; u < 4; u++) {
-                            if (j0 + u < ncon) {
-                                acc4.x += v[u].x; acc4.y += v[u].y; acc4.z += v[u].z; acc4.w += v[u].w;
-                            }
-                        }
-                    }
-                    if constexpr (G) {
-                        store_peers4(gq, m, n0 + c, acc4);
-                    } else {
-                        float *yo = p.y + (int64_t)m * N + n0 + c;
-                        yo[0] = acc4.x; yo[1] = acc4.y; yo[2] = acc4.z; yo[3] = acc4.w;
+                for (int u = 0; u < kCombineLoads; u++) {
+                    if (j0 + u < count) {
+                        acc4.x += v[u].x; acc4.y += v[u].y; acc4.z += v[u].z; acc4.w += v[u].w;
                     }
                 }
-                if (tid == 0) atomicExch(&p.counters[tile], 0);
             }
-            named_bar_sync(1, kNW * 32);
+            sink(m, c, acc4);
         }
+    };
+    auto to_output = [&](int64_t tile) {
+        const int64_t n0 = tile * TN;
+        return [=, &gq, &p](int m, int c, float4 v) {
+            if constexpr (G) {
+                store_peers4(gq, m, n0 + c, v);
+            } else {
+                float *yo = p.y + (int64_t)m * N + n0 + c;
+                yo[0] = v.x; yo[1] = v.y; yo[2] = v.z; yo[3] = v.w;
+            }
+        };
+    };
+    auto combine = [&](int64_t tile, int old1) {  // old1: thread 0's first-level count
+        const int64_t cf = (tile * K) / p.rpc;
+        const int64_t cl = imin64(((tile + 1) * K - 1) / p.rpc, p.grid - 1);
+        const int64_t gl = cf / p.group, gh = cl / p.group, g = blockIdx.x / p.group;
+        const int64_t c_lo = cf > g * p.group ? cf : g * p.group;
+        const int64_t c_hi = imin64(cl, g * p.group + p.group - 1);
+        int *cnt1 = p.counters + p.ntiles + tile + g;
+        named_bar_sync(1, kNW * 32);
+        if (tid == 0) flag[0] = (old1 == (int)(c_hi - c_lo));
+        named_bar_sync(1, kNW * 32);
+        if (!flag[0]) return;
+        __threadfence();
+        // a CTA holds this tile in slot 0 if the tile is its first, else in
+        // slot 1: only CTA cf can start before the tile
+        const bool cf_slot1 = cf * p.rpc < tile * K;
+        auto part = [&](int j) {
+            const int64_t cta = c_lo + j;
+            const int sl = (cta == cf && cf_slot1) ? 1 : 0;
+            return p.partials + (size_t)(cta * 2 + sl) * MR * TN;
+        };
+        const int n1 = (int)(c_hi - c_lo + 1);
+        if (gl == gh) {
+            sum_rows(tile, part, n1, to_output(tile));
+            named_bar_sync(1, kNW * 32);
+            if (tid == 0) atomicExch(cnt1, 0);
+            return;
+        }
+        float *gdst = p.gpartials + (size_t)(tile + g) * MR * TN;
+        sum_rows(tile, part, n1, [&](int m, int c, float4 v) {
+            *reinterpret_cast<float4 *>(gdst + (size_t)m * TN + c) = v;
+        });
+        __threadfence();
+        named_bar_sync(1, kNW * 32);
+        if (tid == 0) {
+            atomicExch(cnt1, 0);
+            flag[0] = (atomicAdd(&p.counters[tile], 1) == (int)(gh - gl));
+        }
+        named_bar_sync(1, kNW * 32);
+        if (!flag[0]) return;
+        __threadfence();
+        auto gpart = [&](int j) { return p.gpartials + (size_t)(tile + gl + j) * MR * TN; };
+        sum_rows(tile, gpart, (int)(gh - gl + 1), to_output(tile));
+        named_bar_sync(1, kNW * 32);
+        if (tid == 0) atomicExch(&p.counters[tile], 0);
     };
 
     // this warp's row j: CTA-local index pl; its ring slot / phase
@@ -657,6 +715,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         flush(cur_tile);
         cur_tile++;
     }
+    if (pend_first) combine(first_tile, old_first);
+    if (pend_last) combine(last_tile, old_last);
     // All-gather: the last CTA to finish tells every rank this rank's shard
     // is in place, then waits until every rank's shard is in its own buffer.
     if (G && gq.world > 1) {
@@ -724,7 +784,8 @@ struct Plan {
     int ntiles, grid, stages, row_cap;
     int64_t rpc;
     size_t smem;
-    size_t partial_bytes, counter_bytes;
+    int group, ngroups;  // CTAs per first-level split-K group, and the group count
+    size_t part1_bytes, partial_bytes, counter_bytes;
     bool generic;
 };
 
@@ -773,8 +834,19 @@ static Plan make_plan(const GemvShape &s, int device) {
     while (stages > kMinStages && smem_for(stages) > (size_t)kSmemPerCta) stages--;
     pl.stages = stages;
     pl.smem = smem_for(stages);
-    pl.partial_bytes = ((size_t)pl.grid * 2 * pl.mr * pl.tn * 4 + 255) & ~size_t(255);
-    pl.counter_bytes = ((size_t)pl.ntiles * 4 + 255) & ~size_t(255);
+    // split-K: a tile is shared by up to ceil(K / rpc) + 1 CTAs; above
+    // kMaxFanIn the sum goes through groups of kGroup CTAs
+    const int64_t fan_in = (s.K + pl.rpc - 1) / pl.rpc + 1;
+    pl.group = fan_in > kMaxFanIn ? kGroup : pl.grid;
+    pl.ngroups = (pl.grid + pl.group - 1) / pl.group;
+    if (2 * (int64_t)pl.ntiles + pl.ngroups > (int64_t)(kWorkspaceCounterHead / 4)) {
+        pl.generic = true;  // more split-K counters than the workspace head holds
+        return pl;
+    }
+    pl.part1_bytes = ((size_t)pl.grid * 2 * pl.mr * pl.tn * 4 + 255) & ~size_t(255);
+    const size_t gpart = pl.group < pl.grid ? (size_t)(pl.ntiles + pl.ngroups) * pl.mr * pl.tn * 4 : 0;
+    pl.partial_bytes = pl.part1_bytes + ((gpart + 255) & ~size_t(255));
+    pl.counter_bytes = ((size_t)(2 * pl.ntiles + pl.ngroups) * 4 + 255) & ~size_t(255);
     return pl;
 }
 
@@ -863,6 +935,8 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
     // partials after the fixed counter head: a later call with more tiles
     // must find its counters at zero, never overwritten by these partials
     gp.partials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kWorkspaceCounterHead);
+    gp.gpartials = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + kWorkspaceCounterHead + pl.part1_bytes);
+    gp.group = pl.group;
     gp.row_cap = pl.row_cap;
     gp.stages = pl.stages;
     GatherParams gq{};
