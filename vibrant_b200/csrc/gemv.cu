@@ -663,35 +663,25 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         if (tid == 0) atomicExch(&p.counters[tile], 0);
     };
 
-    // this warp's row j: CTA-local index pl; its ring slot / phase
+    // this warp's next row j: CTA-local index pl, its ring slot / phase
     int pl = warp;
     int nb32 = (int)next_boundary;
-    int slot = 0, prev_slot = S - 1;
+    int slot = 0;
     uint32_t phase = 0;
+    int islot = ji % S;  // ring slot of the next row to stream
 
-    for (int j = 0; j < nw; j++) {
-        if (!mbar_wait_bounded(smem_u32addr(&my_full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
-        while (pl >= nb32) {
-            flush(cur_tile);
-            cur_tile++;
-            nb32 += (int)K;
-        }
-        const int jj = j & 31;
+    // Decode row j (its parameters sit in lane j % 32 of the current batch)
+    // from ring slot sl.
+    auto decode_row = [&](int jj, int sl) {
         float xv[MR];
 #pragma unroll
         for (int m = 0; m < MR; m++) xv[m] = __shfl_sync(0xffffffffu, xcur[m], jj);
         const uint32_t n0 = __shfl_sync(0xffffffffu, c_n0, jj);
         const uint32_t v0 = __shfl_sync(0xffffffffu, c_v0, jj);
-        if (jj == 31) {
-#pragma unroll
-            for (int m = 0; m < MR; m++) xcur[m] = xnext[m];
-            load_x(j + 33, xnext);
-            decode_batch(j + 1);
-        }
         if (n0 + lane * VPT < Nu) {
             const uint32_t lead = (((v0 >> 8) & 15u) * (uint32_t)B) & 15u;
             const uint32_t wl = (v0 & 255u) + lane * VPT;
-            const uint32_t row = my_ring_u32 + (uint32_t)(slot * p.row_cap) + lead;
+            const uint32_t row = my_ring_u32 + (uint32_t)(sl * p.row_cap) + lead;
 #pragma unroll
             for (int h = 0; h < H; h++) {
                 const uint32_t wh = wl + h * VH;
@@ -700,15 +690,50 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
                     decode_accum<QT, MR, VH>(row + (wh >> 8) * B, (int)(wh & 255u), xv, acc[h], corr[h]);
             }
         }
-        // Refill the previous row's slot (every lane has long finished
-        // reading it) with the row S - 1 ahead of this one.
-        __syncwarp();
-        if (j >= 1 && ji < nw) issue_next(prev_slot);
-        pl += kNW;
-        prev_slot = slot;
-        if (++slot == S) {
-            slot = 0;
+    };
+
+    for (int j = 0; j < nw;) {
+        while (pl >= nb32) {
+            flush(cur_tile);
+            cur_tile++;
+            nb32 += (int)K;
+        }
+        // Two rows at a time when both lie in the current tile and in the
+        // current parameter batch: one straight run of decode code for both
+        // (more independent work in flight, loop costs shared).
+        const int jj = j & 31;
+        const bool pair = (j + 1 < nw) && (pl + kNW < nb32) && (jj != 31);
+        if (!mbar_wait_bounded(smem_u32addr(&my_full[slot]), phase, kWaitNs)) set_status(kStatusTimeout);
+        int used = 1;
+        if (pair) {
+            const int slot1 = slot + 1 == S ? 0 : slot + 1;
+            const uint32_t phase1 = slot + 1 == S ? phase ^ 1u : phase;
+            if (!mbar_wait_bounded(smem_u32addr(&my_full[slot1]), phase1, kWaitNs)) set_status(kStatusTimeout);
+            decode_row(jj, slot);
+            decode_row(jj + 1, slot1);
+            used = 2;
+        } else {
+            decode_row(jj, slot);
+        }
+        j += used;
+        pl += used * kNW;
+        slot += used;
+        if (slot >= S) {
+            slot -= S;
             phase ^= 1u;
+        }
+        if ((j & 31) == 0 && j < nw) {  // next batch of 32 rows
+#pragma unroll
+            for (int m = 0; m < MR; m++) xcur[m] = xnext[m];
+            load_x(j + 32, xnext);
+            decode_batch(j);
+        }
+        // Refill the slots of all but the last decoded row (every lane has
+        // long finished reading them): up to S - 1 rows ahead.
+        __syncwarp();
+        while (ji < nw && ji < j - 1 + S) {
+            issue_next(islot);
+            if (++islot == S) islot = 0;
         }
     }
     while (cur_tile <= last_tile) {
