@@ -65,14 +65,16 @@ def peaks():
 
 
 def committed_traffic(workload: str):
-    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    """(dram bytes per launch, kernel name) of the dominant kernel from the
+    committed ncu summary."""
     p = os.path.join(ROOT, "profiles", f"{workload}.traffic.json")
     if os.path.exists(p):
         try:
-            return json.load(open(p)).get("dram_bytes_per_launch")
+            d = json.load(open(p))
+            return d.get("dram_bytes_per_launch"), d.get("kernel")
         except Exception:
-            return None
-    return None
+            return None, None
+    return None, None
 
 
 class ClockSampler:
@@ -401,7 +403,7 @@ def run_ours(args):
     value = total_bytes / step_s / 1e9
     shard_bytes = algorithmic_bytes(qt, K, n_local, 1)
     achieved = shard_bytes / k_dt / 1e9
-    traffic = committed_traffic(WORKLOAD) if world == 1 else None
+    traffic, kernel_name = committed_traffic(WORKLOAD) if world == 1 else (None, None)
     launches_per_step = 1    # the GEMV (with the all-gather fused in when N > 1)
     line = None
     if rank == 0:
@@ -438,7 +440,7 @@ def run_ours(args):
                              f"({2 * w0.nbytes / 1e6:.0f} MB per GPU)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                         "peak_kind": peak_kind, "kernel": "vkq::gemv_kernel<Q6_K,1,32>",
+                         "peak_kind": peak_kind, "kernel": kernel_name or "vkq::gemv_kernel<Q6_K,1,64>",
                          "algorithmic_bytes_per_launch": shard_bytes,
                          "us_per_launch": round(k_dt * 1e6, 3)},
             "cpu_baseline": cpu,

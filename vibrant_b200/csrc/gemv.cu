@@ -52,7 +52,11 @@ constexpr int kNW = 8;                       // warps per CTA, each streaming it
 constexpr int kThreads = kNW * 32;
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
 constexpr int kSmemPerCta = 112 * 1024;      // two CTAs per SM
-constexpr int kRedSlots = 4;                 // [MR][TN] partial-sum slots of the warp reduction
+constexpr int kRedSlots = 4;                 // [MR][TN] partial-sum slots of the tree warp reduction
+// Tiles of at most 1024 values (all rows m) reduce across the 8 warps in one
+// step through 8 slots (fewer barriers); larger ones through a tree over
+// kRedSlots slots (less shared memory).
+__host__ __device__ constexpr bool flat_reduction(int mr, int vpt) { return mr * 32 * vpt <= 1024; }
 constexpr int kMaxStages = 12;               // ring slots per warp
 constexpr int kMinStages = 3;
 constexpr int kCombineLoads = 8;             // partial loads in flight per thread in the split-K sum
@@ -319,9 +323,10 @@ template <int QT, int MR, int VPT, bool G>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, const GatherParams gq) {
     constexpr int B = QT_<QT>::BYTES;
     constexpr int TN = 32 * VPT;
+    constexpr bool kFlatRed = flat_reduction(MR, VPT);
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = p.stages;
-    // [kNW][S] mbarriers | 2 flag words | ring [kNW][S][row_cap] | red [kRedSlots][MR][TN]
+    // [kNW][S] mbarriers | 2 flag words | ring [kNW][S][row_cap] | red [8 or kRedSlots][MR][TN]
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     int *flag = reinterpret_cast<int *>(full + kNW * S);
     const int hdr_bytes = ((8 * kNW * S + 8) + 127) & ~127;
@@ -514,18 +519,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
                 }
             }
         }
-        // 2. sum over the 8 warps in a fixed order through kRedSlots slots:
-        //    w += w + 4, then w += w + 2; warps 0 and 1 leave the two halves
-        //    in slots 0 and 1
-        if (warp >= 4) store_red(warp - 4);
-        named_bar_sync(1, kNW * 32);
-        if (warp < 4) add_red(warp);
-        named_bar_sync(1, kNW * 32);
-        if (warp >= 2 && warp < 4) store_red(warp - 2);
-        named_bar_sync(1, kNW * 32);
-        if (warp < 2) add_red(warp);
-        named_bar_sync(1, kNW * 32);
-        if (warp < 2) store_red(warp);
+        // 2. sum over the 8 warps in a fixed order.  Small tiles: every warp
+        //    stores its slot and step 3 adds the 8 slots.  Large tiles
+        //    (kRedSlots slots only): w += w + 4, then w += w + 2, and warps
+        //    0 and 1 leave the two halves in slots 0 and 1.
+        if constexpr (kFlatRed) {
+            store_red(warp);
+        } else {
+            if (warp >= 4) store_red(warp - 4);
+            named_bar_sync(1, kNW * 32);
+            if (warp < 4) add_red(warp);
+            named_bar_sync(1, kNW * 32);
+            if (warp >= 2 && warp < 4) store_red(warp - 2);
+            named_bar_sync(1, kNW * 32);
+            if (warp < 2) add_red(warp);
+            named_bar_sync(1, kNW * 32);
+            if (warp < 2) store_red(warp);
+        }
 #pragma unroll
         for (int h = 0; h < H; h++) {
 #pragma unroll
@@ -541,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             }
         }
         named_bar_sync(1, kNW * 32);
-        // 3. slot 0 + slot 1, stored coalesced
+        // 3. the slots added in order, stored coalesced
         const int64_t n0 = tile * TN;
         const int ncols = (int)imin64(TN, N - n0);
         const bool whole = (tile * K >= f0) && ((tile + 1) * K <= f1);
@@ -551,7 +561,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             if (m >= p.M || c >= ncols) continue;
             const int L = c / VPT, i = (c % VPT) / 4;
             const int phys = L * VPT + 4 * (i ^ red_swz<VPT>(L)) + (c & 3);
-            const float sum = red[m * TN + phys] + red[(MR + m) * TN + phys];
+            float sum = red[m * TN + phys] + red[(MR + m) * TN + phys];
+            if constexpr (kFlatRed) {
+#pragma unroll
+                for (int w = 2; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
+            }
             if (whole) {
                 if constexpr (G) store_peers(gq, m, n0 + c, sum);
                 else p.y[(int64_t)m * N + n0 + c] = sum;
@@ -827,7 +841,7 @@ static Plan make_plan(const GemvShape &s, int device) {
         // the bulk copies per value; taken when the ragged last tile wastes
         // little and there are enough tiles to keep the split-K fan-in low
         const int64_t nt64 = (s.N + 2047) / 2048;
-        const bool wide = nt64 >= 16 && (nt64 * 2048 - s.N) * 32 <= s.N;
+        const bool wide = nt64 >= 12 && (nt64 * 2048 - s.N) * 25 <= s.N;
         pl.mr = 1;
         pl.vpt = wide ? 64 : 32;
     } else if (s.M <= 2) { pl.mr = 2; pl.vpt = 32; }
@@ -851,7 +865,7 @@ static Plan make_plan(const GemvShape &s, int device) {
     pl.grid = (int)((rows_total + pl.rpc - 1) / pl.rpc);
     const int B = block_bytes(s.qtype);
     pl.row_cap = (((pl.tn / 256 + 1) * B + 16 + 16) + 15) & ~15;
-    const size_t red = (size_t)kRedSlots * pl.mr * pl.tn * 4;
+    const size_t red = (size_t)(flat_reduction(pl.mr, pl.vpt) ? kNW : kRedSlots) * pl.mr * pl.tn * 4;
     auto smem_for = [&](int st) {
         return (size_t)(((8 * kNW * st + 8) + 127) & ~127) + (size_t)kNW * st * pl.row_cap + red;
     };
