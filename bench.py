@@ -184,7 +184,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded, BASELINE distributions)",
+            "data": "synthetic (seeded; d, dmin, scale and quant distributions of the workload description)",
             "config": {"workload": WORKLOAD, "qtype": "Q6_K", "K": wl["K"], "N": wl["N"], "M": 1,
                        "parallelism": "single host thread (matmul_simd.go:189-199 has no fan-out)"},
             "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
@@ -429,7 +429,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": warm, "ms_per_step": round(step_s * 1e3, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded, BASELINE distributions)",
+            "data": "synthetic (seeded; d, dmin, scale and quant distributions of the workload description)",
             "config": {"workload": WORKLOAD, "qtype": "Q6_K", "K": K, "N": N, "M": 1,
                        "columns_per_rank": n_local,
                        "parallelism": "single GPU" if world == 1 else
