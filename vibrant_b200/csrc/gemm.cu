@@ -165,17 +165,27 @@ __device__ __forceinline__ void load_unit(uint32_t blk, uint32_t within, bool va
 
 // A pair of fp32 values rounded to a bf16 pair.
 __device__ __forceinline__ uint32_t pair_bf16(float2 w2) { return bf16x2(w2.x, w2.y); }
-template <int J>
-__device__ __forceinline__ float2 magic_pair(uint32_t E, uint32_t O) {
-    return make_float2(byte_as_magic<J>(E), byte_as_magic<J>(O));
-}
 
 // Decode one unit into 32 values, rounded to bf16 pairs (16 words).  The
 // values come out of the packed bytes as in the fp32 GEMV: nibbles of even
-// and odd values are moved into byte lanes E and O, a byte permute into the
-// exponent of 2^23 turns each into a float, one packed add removes 2^23.
+// and odd values are merged into byte lanes E and O, and a byte permute moves
+// each quant q into a word of its own, which is used as it is as an fma
+// operand: read as a float it is the subnormal q * 2^-149, so with the scale
+// pre-multiplied by 2^100 one packed fma gives w * 2^-49 with the single
+// rounding of the unscaled fma (every term stays normal: |d*sc| < 2^24).
 // Q4_K/Q5_K: w = fma(d*sc, q, -dmin*m), equal to the reference's
-// (d*sc)*q - dmin*m because (d*sc)*q is exact; Q6_K: w = (d*s) * (q - 32).
+// (d*sc)*q - dmin*m because (d*sc)*q is exact; Q6_K: w = (d*s) * (q - 32)
+// as fma(d*s, q, -32*d*s).  The 2^-49 is undone by X, which is converted to
+// bf16 times 2^49 (x_to_bf16_kernel): every product, and so Y, is unchanged.
+constexpr float kWScale = 0x1p100f;  // on d*sc, d*s
+constexpr float kWDown = 0x1p-49f;   // w comes out times this
+constexpr float kXScale = 0x1p49f;   // X goes into bf16 times this
+
+template <int J>
+__device__ __forceinline__ float2 int_pair(uint32_t E, uint32_t O) {
+    return make_float2(__uint_as_float(prmt(E, 0u, 0x4440u | J)), __uint_as_float(prmt(O, 0u, 0x4440u | J)));
+}
+
 template <int QT>
 __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&out)[16]) {
     if (!u.valid) {
@@ -189,9 +199,9 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
         const uint32_t sc24 = sb < 4 ? u.v[1] : __funnelshift_r(u.v[1], u.v[2], 24);
         const uint32_t m24 = sb < 4 ? __funnelshift_r(u.v[2], u.v[3], 16) : (u.v[3] >> 8);
         const uint32_t sh = 6u * (sb & 3);
-        const float ds = d * (float)((sc24 >> sh) & 63u);
-        const float dm = dmin * (float)((m24 >> sh) & 63u);
-        const float2 negmag = make_float2(-8388608.0f, -8388608.0f), s2 = make_float2(ds, ds), nm2 = make_float2(-dm, -dm);
+        const float ds = (d * kWScale) * (float)((sc24 >> sh) & 63u);
+        const float ndm = (dmin * -kWDown) * (float)((m24 >> sh) & 63u);
+        const float2 s2 = make_float2(ds, ds), nm2 = make_float2(ndm, ndm);
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             uint32_t E = u.v[4 + c] & 0x0F0F0F0Fu;
@@ -203,10 +213,10 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
                 E |= ((hb & 0x55u) * 0x410410u) & 0x10101010u;
                 O |= (((hb >> 1) & 0x55u) * 0x410410u) & 0x10101010u;
             }
-            out[4 * c + 0] = pair_bf16(f2fma(s2, f2add(magic_pair<0>(E, O), negmag), nm2));
-            out[4 * c + 1] = pair_bf16(f2fma(s2, f2add(magic_pair<1>(E, O), negmag), nm2));
-            out[4 * c + 2] = pair_bf16(f2fma(s2, f2add(magic_pair<2>(E, O), negmag), nm2));
-            out[4 * c + 3] = pair_bf16(f2fma(s2, f2add(magic_pair<3>(E, O), negmag), nm2));
+            out[4 * c + 0] = pair_bf16(f2fma(s2, int_pair<0>(E, O), nm2));
+            out[4 * c + 1] = pair_bf16(f2fma(s2, int_pair<1>(E, O), nm2));
+            out[4 * c + 2] = pair_bf16(f2fma(s2, int_pair<2>(E, O), nm2));
+            out[4 * c + 3] = pair_bf16(f2fma(s2, int_pair<3>(E, O), nm2));
         }
     } else {
         uint32_t ql[4], qh[2], qhs[2];
@@ -217,10 +227,11 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
             qh[i] = __funnelshift_r(u.v[5 + i], u.v[6 + i], u.shf);
             qhs[i] = qh[i] >> 4;
         }
-        const float d = hw_f16_to_f32(u.v[8] >> 16);
+        const float d = hw_f16_to_f32(u.v[8] >> 16) * kWScale;
         const float ds0 = d * (float)(int)(int8_t)(u.v[8] & 0xFFu);
         const float ds1 = d * (float)(int)(int8_t)((u.v[8] >> 8) & 0xFFu);
-        const float2 neg = make_float2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+        // -32 * d*s * 2^-49 = (d*s * 2^100) * -2^-144, exact
+        const float o0 = ds0 * -0x1p-144f, o1 = ds1 * -0x1p-144f;
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             // byte lane j of X = nibble j of the chunk's 16 qh bits
@@ -229,10 +240,11 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
             const uint32_t E = (ql[c] & 0x0F0F0F0Fu) | ((X & 0x03030303u) << 4);
             const uint32_t O = ((ql[c] >> 4) & 0x0F0F0F0Fu) | ((X << 2) & 0x30303030u);
             const float2 s2 = c < 2 ? make_float2(ds0, ds0) : make_float2(ds1, ds1);
-            out[4 * c + 0] = pair_bf16(f2mul(s2, f2add(magic_pair<0>(E, O), neg)));
-            out[4 * c + 1] = pair_bf16(f2mul(s2, f2add(magic_pair<1>(E, O), neg)));
-            out[4 * c + 2] = pair_bf16(f2mul(s2, f2add(magic_pair<2>(E, O), neg)));
-            out[4 * c + 3] = pair_bf16(f2mul(s2, f2add(magic_pair<3>(E, O), neg)));
+            const float2 o2 = c < 2 ? make_float2(o0, o0) : make_float2(o1, o1);
+            out[4 * c + 0] = pair_bf16(f2fma(s2, int_pair<0>(E, O), o2));
+            out[4 * c + 1] = pair_bf16(f2fma(s2, int_pair<1>(E, O), o2));
+            out[4 * c + 2] = pair_bf16(f2fma(s2, int_pair<2>(E, O), o2));
+            out[4 * c + 3] = pair_bf16(f2fma(s2, int_pair<3>(E, O), o2));
         }
     }
 }
@@ -640,7 +652,7 @@ __global__ void __launch_bounds__(256) x_to_bf16_kernel(const float *__restrict_
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < npairs;
          i += (int64_t)gridDim.x * blockDim.x) {
         const float2 v = reinterpret_cast<const float2 *>(x)[i];
-        xb[i] = bf16x2(v.x, v.y);
+        xb[i] = bf16x2(v.x * kXScale, v.y * kXScale);  // exact scaling: see decode_unit_bf16
     }
     pdl_launch_dependents();
 }
