@@ -271,8 +271,11 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
         const uint32_t ql = blk + (within >> 1);
         const uint32_t qha = blk + 128 + (within >> 2);
         uint32_t wq[NCH];
+        // ql and (for groups of >= 16 values) qh lie at the same offset
+        // modulo 4: one shift serves both
+        const uint32_t shf = (ql & 3u) * 8u;
         {
-            const uint32_t base = ql & ~3u, shf = (ql & 3u) * 8u;
+            const uint32_t base = ql & ~3u;
             uint32_t wv[NCH + 1];
 #pragma unroll
             for (int i = 0; i <= NCH; i++) wv[i] = lds32(base + 4 * i);
@@ -280,11 +283,13 @@ __device__ __forceinline__ void decode_accum(uint32_t blk, int within, const flo
             for (int i = 0; i < NCH; i++) wq[i] = __funnelshift_r(wv[i], wv[i + 1], shf);
         }
         uint32_t qh[(NCH + 1) / 2];
-        if constexpr (NCH == 4) {
-            qh[0] = lds32_a2(qha);
-            qh[1] = lds32_a2(qha + 4);
-        } else if constexpr (NCH == 2) {
-            qh[0] = lds32_a2(qha);
+        if constexpr (NCH >= 2) {
+            const uint32_t base = qha & ~3u;
+            uint32_t hv[NCH / 2 + 1];
+#pragma unroll
+            for (int i = 0; i <= NCH / 2; i++) hv[i] = lds32(base + 4 * i);
+#pragma unroll
+            for (int i = 0; i < NCH / 2; i++) qh[i] = __funnelshift_r(hv[i], hv[i + 1], shf);
         } else {
             qh[0] = lds16(qha);
         }
