@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define VKQ_ABI_VERSION 1
+#define VKQ_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define VKQ_API __attribute__((visibility("default")))
@@ -55,7 +55,8 @@ enum vkq_status {
     VKQ_ERR_WORKSPACE = 4,        /* workspace missing or smaller than required */
     VKQ_ERR_CUDA = 5,             /* CUDA runtime error (message in vkq_last_error) */
     VKQ_ERR_DEVICE_TIMEOUT = 6,   /* a bounded device-side wait gave up */
-    VKQ_ERR_NCCL = 7              /* collective failure in the sharded path */
+    VKQ_ERR_NCCL = 7,             /* collective failure in the sharded path */
+    VKQ_ERR_PEER = 8              /* a peer rank is out of step, or its channel failed earlier */
 };
 
 /* Version of this ABI (VKQ_ABI_VERSION of the built library). */
@@ -129,52 +130,108 @@ VKQ_API int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int6
 
 /* The fp32 GEMV of vkq_gemv without a workspace argument, for callers that
  * cannot allocate device memory: a host whose allocator owns every byte of
- * the device (a pool sized to a fixed budget, as vibrant's gpu.BufferPool
- * is), a plugin whose memory plan is fixed before it runs, or a caller that
- * must avoid cudaMalloc's device-wide synchronisation.  No counterpart in the
- * reference.  The split-K scratch lives in a fixed 8 MiB device array inside
- * the library, which every GPU that loads the library holds until the
- * process exits; a problem needing more scratch is rejected with
- * VKQ_ERR_WORKSPACE.  The call allocates nothing.  Its first call on a device
- * looks the array up (cudaGetSymbolAddress) -- make that first call before
- * any stream capture.  All calls share the one array: calls that overlap on
- * the GPU (different streams, or different host threads on one device) race
- * and must be serialised by the caller.  1 <= M <= 8. */
+ * the device budget, a plugin whose memory plan is fixed before it runs, or a
+ * caller that must avoid cudaMalloc's device-wide synchronisation.  No
+ * counterpart in the reference.  The split-K scratch lives in a fixed 8 MiB
+ * device array inside the library, which every GPU that loads the library
+ * holds until the process exits; a problem needing more scratch is rejected
+ * with VKQ_ERR_WORKSPACE.  The call allocates nothing.  Its first call on a
+ * device looks the array up (cudaGetSymbolAddress) -- make that first call
+ * before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (different streams, or different host threads on one
+ * device) race and must be serialised by the caller.  1 <= M <= 8. */
 VKQ_API int vkq_gemv_noalloc(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                              const float *x, int64_t M, float *y, void *stream);
 
-/* ---- Row-sharded matmul across the GPUs of one node (one process per GPU) ----
+/* The steps between the linear layers of a decode step (float32, device
+ * buffers).  out = SiLU(gate) * up elementwise, SiLU(g) = g / (1 + exp(-g)):
+ * replaces silu_f32 followed by mul_f32 (internal/gpu/cuda/kernels.cu:306-341)
+ * as FeedForward.Forward applies them (internal/transformer/feedforward.go:92-94);
+ * buffers 16-byte aligned.  vkq_rms_norm: out[r] = (x[r] / sqrt(mean(x[r]^2)
+ * + eps)) * weight for each of `rows` rows of n values: replaces
+ * rms_norm_f32 / rms_norm_batched_f32 (kernels.cu:209-288). */
+VKQ_API int vkq_silu_mul(int device, const float *gate, const float *up, float *out, int64_t n, void *stream);
+VKQ_API int vkq_rms_norm(int device, const float *x, const float *weight, float *out, int64_t rows, int64_t n,
+                         float eps, void *stream);
+
+/* ---- Row-sharded matmul across the GPUs of one node ----
  * The reference runs on a single device (internal/gpu/cuda/cuda.go:33-46);
- * these entry points implement the multi-GPU layout of the same MatMul:
- * each rank holds the weight columns [rank * N_shard, (rank + 1) * N_shard)
- * and the result is all-gathered through peer memory over NVLink.
+ * these entry points implement the multi-GPU layout of the same MatMul.  The
+ * output columns of a [K, N] weight are split over `world` ranks (at most 8)
+ * in equal ranges rounded up to multiples of 32 (vkq_shard_columns); each
+ * rank holds only its row-block shard of the weight (vkq_shard_weight) and
+ * the result is all-gathered inside the GEMV kernel through peer memory over
+ * NVLink (plain stores into every rank's output, no collective library).
  *
- * Device buffers shared between processes: vkq_ipc_alloc allocates `bytes`
- * of zero-filled device memory and returns a 64-byte handle another process
- * passes to vkq_ipc_open to map the same buffer (peer access is enabled on
- * the mapping).  vkq_ipc_close unmaps, vkq_ipc_free releases the owner's
- * buffer (after every mapping of it has been closed). */
+ * Channel protocol, shared by both forms below: every rank makes the same
+ * sequence of calls on a channel, each rank on one stream.  A call stores
+ * into another rank's output only after that rank has started the same call
+ * (so it has finished with the previous contents); when it completes on the
+ * stream every rank's columns are in this rank's output.  Every wait is
+ * bounded (VKQ_PEER_WAIT_MS in the environment, default 2000): a rank that
+ * never arrives makes the others give up with VKQ_ERR_DEVICE_TIMEOUT, a rank
+ * whose call number differs makes them give up at once with VKQ_ERR_PEER
+ * (both read with vkq_device_status).  A failed call stores nothing into
+ * other ranks' outputs, and every later call on that channel fails at once
+ * (VKQ_ERR_PEER, no waits) until the channel is reset. */
+
+/* Output columns [*lo, *hi) of rank `rank`; N a multiple of 32. */
+VKQ_API int vkq_shard_columns(int64_t N, int world, int rank, int64_t *lo, int64_t *hi);
+/* Size of the row-block shard of columns [col_lo, col_hi) of a [K, N] weight:
+ * K rows of *row_blocks super-block slots (*bytes = K * row_blocks * block
+ * bytes).  Host-only. */
+VKQ_API int vkq_shard_bytes(int qtype, int64_t K, int64_t N, int64_t col_lo, int64_t col_hi, int64_t *row_blocks,
+                            int64_t *bytes);
+/* Builds the row-block shard of columns [col_lo, col_hi) from the full raw
+ * weight (HOST memory, e.g. the mmapped GGUF bytes of
+ * internal/gguf/loader.go:11-73): row k holds the super-blocks covering
+ * values k*N + col_lo .. k*N + col_hi - 1, copied byte for byte (blocks that
+ * straddle rows or shards are duplicated), zero-padded to row_blocks slots.
+ * The caller uploads the result (raw blocks, no float32 expansion). */
+VKQ_API int vkq_shard_weight(int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, int64_t col_lo,
+                             int64_t col_hi, void *out, int64_t out_bytes);
+
+/* In-process form: one process drives every GPU (vibrant's host is one Go
+ * process).  vkq_comm_init enables peer access between the listed devices
+ * and allocates each device's channel flags; one communicator is one channel. */
+typedef struct vkq_comm vkq_comm;
+VKQ_API int vkq_comm_init(int world, const int *devices, vkq_comm **comm);
+/* Zeroes every device's channel (after synchronising them): the recovery
+ * from a failed call; no call may be in flight. */
+VKQ_API int vkq_comm_reset(vkq_comm *comm);
+VKQ_API int vkq_comm_destroy(vkq_comm *comm);
+VKQ_API int vkq_comm_size(const vkq_comm *comm);
+/* y[r] = x[r] . W on every device r, computed as rank r's columns of the
+ * shards w_shards[r] (each on device r, built for the columns of
+ * vkq_shard_columns(N, world, r)) and all-gathered into every y[r] (device r,
+ * float32 [M, N], 16-byte aligned).  Arrays are HOST arrays of `world`
+ * entries; workspaces[r] holds vkq_matmul_workspace_bytes(M, K, hi - lo) on
+ * device r; streams[r] is a stream of device r.  Launches on every device
+ * and returns; 1 <= M <= 8. */
+VKQ_API int vkq_gemv_sharded(vkq_comm *comm, int qtype, const void *const *w_shards, const int64_t *w_bytes,
+                             int64_t K, int64_t N, const float *const *x, int64_t M, float *const *y,
+                             void *const *workspaces, const size_t *workspace_bytes, void *const *streams);
+
+/* Multi-process form (one process per GPU): device buffers shared between
+ * processes.  vkq_ipc_alloc allocates `bytes` of zero-filled device memory and
+ * returns a 64-byte handle another process passes to vkq_ipc_open to map the
+ * same buffer (peer access is enabled on the mapping).  vkq_ipc_close unmaps,
+ * vkq_ipc_free releases the owner's buffer (after every mapping of it has
+ * been closed). */
 VKQ_API int vkq_ipc_alloc(int device, size_t bytes, void **ptr, unsigned char handle[64]);
 VKQ_API int vkq_ipc_open(int device, const unsigned char handle[64], void **ptr);
 VKQ_API int vkq_ipc_close(int device, void *ptr);
 VKQ_API int vkq_ipc_free(int device, void *ptr);
 
-/* y[M, N] = x[M, K] . W[K, N] computed across `world` ranks, rank `rank`
- * computing output columns [col_lo, col_hi) (multiples of 32) with the fp32
- * GEMV of vkq_gemv, fused with the all-gather: each value is stored into
- * every rank's output buffer y[M][N] through peer memory, with no collective
- * library call.  Every rank passes the same full weight W (the raw
- * super-blocks, resident on every GPU; a rank reads only the blocks under its
- * columns, so shards need no re-encoding when N % 256 != 0).  peer_out and
- * peer_flags are DEVICE arrays of `world` pointers: this process's mappings
- * of every rank's output buffer and flag array (own entry included); a flag
- * array holds 2 * world uint32 and starts at zero; sync points to this rank's
- * 2 uint32 (zero at first) that count its calls.  Every rank makes the same
- * sequence of calls.  A call stores into another rank's buffer only after
- * that rank has started the same call, and when it completes on the stream
- * every rank's columns are in this rank's output.  The waits inside are
- * bounded: a rank that never arrives makes the others give up after about
- * 2 s with VKQ_ERR_DEVICE_TIMEOUT (read with vkq_device_status).
+/* This rank's part of a sharded y[M, N] = x[M, K] . W[K, N]: columns
+ * [col_lo, col_hi) (multiples of 32) computed with the fp32 GEMV of vkq_gemv
+ * from the rank's row-block shard w (vkq_shard_weight for the same columns,
+ * w_bytes >= vkq_shard_bytes) and stored into every rank's output y[M][N].
+ * peer_out and peer_flags are HOST arrays of `world` device pointers usable
+ * on this device: every rank's output buffer and channel flag array (own
+ * entry included); a flag array holds 2 * world uint32 and starts at zero;
+ * sync points to this rank's 4 uint32 channel words (zero at first; zero them
+ * on every rank, with the flags, to reset a failed channel).
  * 1 <= M <= 8; the workspace is vkq_matmul_workspace_bytes(M, K, col_hi - col_lo). */
 VKQ_API int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                                int64_t col_lo, int64_t col_hi, const float *x, int64_t M, void *const *peer_out,
@@ -182,8 +239,9 @@ VKQ_API int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_b
                                size_t workspace_bytes, void *stream);
 
 /* Reads and clears the device-side status word of this library on a device
- * (set when a bounded wait inside a kernel gave up).  Synchronizes with the
- * device.  *code receives VKQ_OK or VKQ_ERR_DEVICE_TIMEOUT. */
+ * (set when a bounded wait inside a kernel gave up, or a peer was out of
+ * step).  Synchronizes with the device.  *code receives VKQ_OK,
+ * VKQ_ERR_DEVICE_TIMEOUT or VKQ_ERR_PEER. */
 VKQ_API int vkq_device_status(int device, int *code);
 
 #ifdef __cplusplus

@@ -1,15 +1,27 @@
 """Row-sharded GEMV with the all-gather fused into the kernel through peer
-memory (vkq_gemv_allgather, vibrant_b200.tensor.PeerGather) on 2 GPUs.
+memory (vkq_gemv_allgather / vkq_gemv_sharded).
 
-Every rank keeps the full quantized weight, computes its columns and stores
-them into every rank's output over NVLink.  After each call every rank's
-output must equal the full product within the GEMV tolerance (1e-5 of
-sum_k |x w|), for consecutive calls of different M and for a weight whose N
-is not a multiple of 256 (super-blocks straddle the rows and the shards).
-The ranks run as child processes; the test needs 2 GPUs and is skipped
-otherwise."""
+Each rank holds only its row-block shard of the weight (vkq_shard_weight),
+computes its columns and stores them into every rank's output over NVLink.
+After each call every rank's output must equal the full product within the
+GEMV tolerance (1e-5 of sum_k |x w|), for consecutive calls of different M
+and for weights whose N is not a multiple of 256 (super-blocks straddle the
+rows and the shards).
+
+* one GPU: the kernel as rank 0 of 1 for every shard of a world-way split;
+  the channel protocol with a second rank that never arrives (a flag that
+  nothing sets): the waits run out after VKQ_PEER_WAIT_MS, the status is
+  VKQ_ERR_DEVICE_TIMEOUT, nothing is stored into the absent rank's buffer,
+  the next call fails at once with VKQ_ERR_PEER, a flag beyond the call
+  number is refused at once, and a reset channel works again;
+* two GPUs: one process per GPU over CUDA IPC, and one process driving both
+  GPUs (vkq_comm_init); skipped on a box with fewer GPUs.
+"""
 import os
 import socket
+import subprocess
+import sys
+import textwrap
 
 import numpy as np
 import pytest
@@ -27,9 +39,121 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("qt,K,N,world", [
+    (14, 256, 151936, 2),  # wide shards: 64 values per lane; rows straddle blocks
+    (14, 2048, 37984, 3),  # shards straddle super-blocks
+    (12, 2048, 11008, 4),
+    (13, 512, 4160, 2),
+    (14, 2048, 151936, 8),
+])
+def test_allgather_kernel_single_rank(qt, K, N, world):
+    """The all-gather kernel run as rank 0 of 1 on each rank's shard of a
+    `world`-way split: the shard's columns land in the output at their
+    global offset and match the oracle; the other columns stay untouched."""
+    import torch
+    from oracle import kq_oracle
+    from vibrant_b200 import synth, vkq
+    from vibrant_b200 import tensor as vt
+    wq = synth.weights(qt, K, N, seed=K + N + world)
+    wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+    m_max = 4
+    out, _ = vkq.ipc_alloc(m_max * N * 4)
+    flags, _ = vkq.ipc_alloc(256)
+    sync, _ = vkq.ipc_alloc(256)
+    try:
+        Y = torch.as_tensor(vt._DeviceArray(out, (m_max, N)), device="cuda")
+        for M in (1, 3):
+            for r in range(world):
+                sh = vt.ShardedWeight(qt, K, N, world, r, wq)
+                lo, hi = sh.lo, sh.hi
+                x = synth.activations(M, K, seed=M * 7 + lo)
+                xt = torch.from_numpy(x).cuda()
+                ws = vt.workspace(vt.workspace_bytes(qt, M, K, hi - lo, 0), 0)
+                Y.fill_(123.0)
+                vkq.gemv_allgather(qt, sh.buf.data_ptr(), sh.nbytes, K, N, lo, hi, xt.data_ptr(), M, [out], [flags],
+                                   sync, 1, 0, ws.data_ptr() if ws is not None else None,
+                                   ws.numel() if ws is not None else 0, device=0)
+                torch.cuda.synchronize()
+                y = Y[:M].cpu().numpy()
+                err = helpers.matmul_error(y[:, lo:hi], x, wd[:, lo:hi])
+                assert err <= helpers.GEMV_TOL, (qt, K, N, M, lo, hi, err)
+                assert (y[:, :lo] == 123.0).all() and (y[:, hi:] == 123.0).all()
+        assert vkq.device_status(0) == vkq.OK
+    finally:
+        torch.cuda.synchronize()
+        for p in (out, flags, sync):
+            vkq.ipc_free(p)
+
+
+_PROTOCOL_SCRIPT = textwrap.dedent("""
+    import sys, time
+    sys.path.insert(0, sys.argv[1])
+    import numpy as np, torch
+    from vibrant_b200 import synth, vkq
+    from vibrant_b200 import tensor as vt
+    torch.cuda.set_device(0)
+    qt, K, N, M = 12, 1024, 4096, 1
+    wq = synth.weights(qt, K, N, seed=9)
+    world = 2
+    sh = vt.ShardedWeight(qt, K, N, world, 0, wq)
+    x = torch.from_numpy(synth.activations(M, K, seed=1)).cuda()
+    bufs = [vkq.ipc_alloc(M * N * 4)[0] for _ in range(world)]   # rank 1's buffer: nobody behind it
+    flags = [vkq.ipc_alloc(256)[0] for _ in range(world)]
+    sync = vkq.ipc_alloc(256)[0]
+    Y = [torch.as_tensor(vt._DeviceArray(b, (M, N)), device="cuda") for b in bufs]
+    F0 = torch.as_tensor(vt._DeviceArray(flags[0], (2 * world,), "<u4"), device="cuda")
+    S0 = torch.as_tensor(vt._DeviceArray(sync, (4,), "<u4"), device="cuda")
+    ws = vt.workspace(vt.workspace_bytes(qt, M, K, sh.width, 0), 0)
+    def call():
+        vkq.gemv_allgather(qt, sh.buf.data_ptr(), sh.nbytes, K, N, sh.lo, sh.hi, x.data_ptr(), M, bufs, flags,
+                           sync, world, 0, ws.data_ptr(), ws.numel(), device=0)
+    Y[1].fill_(7.0)
+    t0 = time.time(); call(); st = vkq.device_status(0); t1 = time.time()
+    assert st == vkq.ERR_DEVICE_TIMEOUT, st
+    assert 0.25 < t1 - t0 < 10.0, t1 - t0
+    assert (Y[1] == 7.0).all().item(), "stored into the absent rank's buffer"
+    assert torch.isfinite(Y[0][:, :sh.hi]).all().item()
+    # the channel is marked failed: the next call fails at once, with no wait
+    t0 = time.time(); call(); st = vkq.device_status(0); t1 = time.time()
+    assert st == vkq.ERR_PEER, st
+    assert t1 - t0 < 0.25, t1 - t0
+    assert (Y[1] == 7.0).all().item()
+    # reset; a flag beyond the call number (a rank ahead) is refused at once
+    torch.cuda.synchronize(); F0.zero_(); S0.zero_(); torch.cuda.synchronize()
+    F0[1] = 5
+    t0 = time.time(); call(); st = vkq.device_status(0); t1 = time.time()
+    assert st == vkq.ERR_PEER, st
+    assert t1 - t0 < 0.25, t1 - t0
+    assert (Y[1] == 7.0).all().item()
+    # reset; as rank 0 of 1 the same buffers work again
+    torch.cuda.synchronize(); F0.zero_(); S0.zero_(); torch.cuda.synchronize()
+    sh1 = vt.ShardedWeight(qt, K, N, 1, 0, wq)
+    vkq.gemv_allgather(qt, sh1.buf.data_ptr(), sh1.nbytes, K, N, 0, N, x.data_ptr(), M, bufs[:1], flags[:1], sync,
+                       1, 0, ws.data_ptr(), ws.numel(), device=0)
+    assert vkq.device_status(0) == vkq.OK
+    ref = torch.empty(M, N, device="cuda")
+    w = vt.QuantWeight(qt, K, N, wq)
+    vt.matmul(x, w, out=ref)
+    torch.cuda.synchronize()
+    assert torch.equal(ref, Y[0]), "reset channel gives a different result"
+    for p in bufs + flags + [sync]:
+        vkq.ipc_free(p)
+    print("protocol ok")
+""")
+
+
+def test_absent_peer_times_out_and_the_channel_fails_closed():
+    """A second rank that never arrives (one GPU, a flag nothing sets)."""
+    import torch
+    assert torch.cuda.is_available()
+    env = dict(os.environ, VKQ_PEER_WAIT_MS="300")
+    r = subprocess.run([sys.executable, "-c", _PROTOCOL_SCRIPT, ROOT], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "protocol ok" in r.stdout, r.stdout + r.stderr
+
+
 def _rank_main(rank, world, port, cases):
     import datetime
-    import sys
     sys.path.insert(0, ROOT)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -42,7 +166,7 @@ def _rank_main(rank, world, port, cases):
     from vibrant_b200 import tensor as vt
     for qt, K, N in cases:
         wq = synth.weights(qt, K, N, seed=K + N)
-        w = vt.QuantWeight(qt, K, N, wq, device=f"cuda:{rank}")
+        w = vt.ShardedWeight(qt, K, N, world, rank, wq, device=f"cuda:{rank}")
         wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
         g = vt.PeerGather(dist.group.WORLD, rank, world, rank, N, m_max=4)
         for call, M in enumerate([1, 3, 1, 4, 2]):
@@ -62,57 +186,39 @@ def test_allgather_through_peer_memory_two_gpus():
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     cases = [
-        (14, 2048, 151936 // 4),   # Q6_K, N % 256 == 0 only per 4 rows: shards straddle blocks
+        (14, 2048, 151936),        # Q6_K vocabulary projection: rows and shards straddle blocks
         (12, 2048, 11008),         # Q4_K FFN gate/up
         (13, 512, 4160),           # Q5_K, N % 256 == 64
     ]
     mp.spawn(_rank_main, args=(2, _free_port(), cases), nprocs=2, join=True)
 
 
-@pytest.mark.parametrize("qt,K,N,world", [
-    (14, 256, 151936, 2),  # wide shards: 64 values per lane
-    (14, 2048, 37984, 2),  # shards straddle super-blocks
-    (12, 2048, 11008, 4),
-    (13, 512, 4160, 2),
-])
-def test_allgather_kernel_single_rank(qt, K, N, world):
-    """The all-gather kernel run as rank 0 of 1 for each shard of a
-    `world`-way split: the shard's columns land in the output at their
-    global offset and match the oracle; the other columns stay untouched."""
+def test_in_process_communicator_two_gpus():
+    """One process drives both GPUs (vkq_comm_init / vkq_gemv_sharded)."""
     import torch
-    if not torch.cuda.is_available():
-        pytest.skip("needs a GPU")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
     from oracle import kq_oracle
     from vibrant_b200 import synth, vkq
     from vibrant_b200 import tensor as vt
-    wq = synth.weights(qt, K, N, seed=K + N + world)
-    w = vt.QuantWeight(qt, K, N, wq)
-    wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
-    _, bounds = vt.shard_columns(N, world)
-    m_max = 4
-    out, _ = vkq.ipc_alloc(m_max * N * 4)
-    flags, _ = vkq.ipc_alloc(256)
-    sync, _ = vkq.ipc_alloc(256)
+    comm = vt.Comm([0, 1])
     try:
-        peer_out = torch.tensor([out], dtype=torch.int64, device="cuda")
-        peer_flags = torch.tensor([flags], dtype=torch.int64, device="cuda")
-        Y = torch.as_tensor(vt._DeviceArray(out, (m_max, N)), device="cuda")
-        for M in (1, 3):
-            for lo, hi in bounds:
-                x = synth.activations(M, K, seed=M * 7 + lo)
-                xt = torch.from_numpy(x).cuda()
-                ws = vt.workspace(vt.workspace_bytes(qt, M, K, hi - lo, 0), 0)
-                Y.fill_(123.0)
-                vkq.gemv_allgather(qt, w.buf.data_ptr(), w.nbytes, K, N, lo, hi, xt.data_ptr(), M,
-                                   peer_out.data_ptr(), peer_flags.data_ptr(), sync, 1, 0, ws.data_ptr(),
-                                   ws.numel(), device=0)
-                torch.cuda.synchronize()
-                y = Y[:M].cpu().numpy()
-                err = helpers.matmul_error(y[:, lo:hi], x, wd[:, lo:hi])
-                assert err <= helpers.GEMV_TOL, (qt, K, N, M, lo, hi, err)
-                assert (y[:, :lo] == 123.0).all() and (y[:, hi:] == 123.0).all()
-        assert vkq.device_status(0) == vkq.OK
+        for qt, K, N in [(14, 2048, 151936), (12, 2048, 11008), (13, 512, 4160)]:
+            wq = synth.weights(qt, K, N, seed=K + N + 1)
+            wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+            shards = comm.shards(qt, K, N, wq)
+            for call, M in enumerate([1, 2, 1, 4]):
+                x = synth.activations(M, K, seed=call + qt)
+                xs = [torch.from_numpy(x).to(f"cuda:{d}") for d in comm.devices]
+                ys = [torch.full((M, N), float("nan"), device=f"cuda:{d}") for d in comm.devices]
+                for d in comm.devices:
+                    torch.cuda.synchronize(d)
+                comm.gemv(xs, shards, ys)
+                for r, d in enumerate(comm.devices):
+                    torch.cuda.synchronize(d)
+                    err = helpers.matmul_error(ys[r].cpu().numpy(), x, wd)
+                    assert err <= helpers.GEMV_TOL, (qt, K, N, call, M, r, err)
+        for d in comm.devices:
+            assert vkq.device_status(d) == vkq.OK
     finally:
-        torch.cuda.synchronize()
-        for p in (out, flags, sync):
-            vkq.ipc_free(p)
+        comm.close()

@@ -146,6 +146,7 @@ const char *vkq_status_string(int status) {
     case VKQ_ERR_CUDA: return "CUDA error";
     case VKQ_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
     case VKQ_ERR_NCCL: return "NCCL error";
+    case VKQ_ERR_PEER: return "a peer rank is out of step, or the channel failed earlier";
     default: return "unknown status";
     }
 }
@@ -331,23 +332,93 @@ int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, in
                        void *sync, int world, int rank, void *workspace, size_t workspace_bytes, void *stream) {
     int st = enter(device);
     if (st) return st;
-    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, reinterpret_cast<float *>(sync));
-    if (st) return st;
+    const int bb = block_bytes(qtype);
+    if (bb == 0) {
+        set_error("unsupported qtype %d (expected 12, 13 or 14)", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!w || !x || !sync || !peer_out || !peer_flags || K <= 0 || N <= 0 || M <= 0) {
+        set_error("vkq_gemv_allgather: null pointer or non-positive size");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
     if (M > 8) {
         set_error("vkq_gemv_allgather serves 1 <= M <= 8 (got %lld)", (long long)M);
         return VKQ_ERR_UNSUPPORTED;
     }
-    if (!peer_out || !peer_flags || world < 1 || rank < 0 || rank >= world || N % 32 != 0 || col_lo < 0 ||
-        col_hi > N || col_hi <= col_lo || col_lo % 32 != 0 || col_hi % 32 != 0) {
-        set_error("vkq_gemv_allgather: invalid peer arrays, world/rank (%d/%d) or columns [%lld, %lld) of N=%lld "
-                  "(multiples of 32 needed)",
-                  world, rank, (long long)col_lo, (long long)col_hi, (long long)N);
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || N % 32 != 0 || col_lo < 0 || col_hi > N ||
+        col_hi <= col_lo || col_lo % 32 != 0 || col_hi % 32 != 0) {
+        set_error("vkq_gemv_allgather: invalid world/rank (%d/%d, at most %d ranks) or columns [%lld, %lld) of "
+                  "N=%lld (multiples of 32 needed)",
+                  world, rank, kMaxRanks, (long long)col_lo, (long long)col_hi, (long long)N);
         return VKQ_ERR_INVALID_ARGUMENT;
     }
+    if (reinterpret_cast<uintptr_t>(w) & 15u) {
+        set_error("weight pointer must be 16-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    const int64_t rb = shard_row_blocks(K, N, col_lo, col_hi);
+    if (w_bytes < K * rb * bb) {
+        set_error("the shard holds %lld bytes; columns [%lld, %lld) of a [%lld x %lld] weight need %lld "
+                  "(vkq_shard_bytes)",
+                  (long long)w_bytes, (long long)col_lo, (long long)col_hi, (long long)K, (long long)N,
+                  (long long)(K * rb * bb));
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    GatherArgs g{};
+    for (int r = 0; r < world; r++) {
+        if (!peer_out[r] || !peer_flags[r]) {
+            set_error("vkq_gemv_allgather: null peer buffer for rank %d", r);
+            return VKQ_ERR_INVALID_ARGUMENT;
+        }
+        g.peer_y[r] = static_cast<float *>(peer_out[r]);
+        g.peer_flags[r] = static_cast<unsigned *>(peer_flags[r]);
+    }
+    if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(g.peer_y[rank]) & 15u)) {
+        set_error("x must be 4-byte and the output buffers 16-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    g.sync = static_cast<unsigned *>(sync);
+    g.world = world;
+    g.rank = rank;
+    g.y_ld = N;
+    g.col_off = col_lo;
+    g.rs = rb * 256;
+    g.ld = N;
+    g.n_base = col_lo;
+    g.wait_ns = peer_wait_ns();
     GemvShape s{qtype, K, col_hi - col_lo, M};
-    GatherArgs g{reinterpret_cast<float *const *>(peer_out), reinterpret_cast<unsigned *const *>(peer_flags),
-                 static_cast<unsigned *>(sync), world, rank, N, col_lo, N, col_lo};
     return gemv_launch(s, w, w_bytes, x, nullptr, workspace, workspace_bytes, (cudaStream_t)stream, device, &g);
+}
+
+int vkq_silu_mul(int device, const float *gate, const float *up, float *out, int64_t n, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (!gate || !up || !out || n <= 0) {
+        set_error("invalid arguments to vkq_silu_mul");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(out)) &
+        15u) {
+        set_error("vkq_silu_mul needs 16-byte aligned buffers");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(silu_mul(gate, up, out, n, (cudaStream_t)stream, device), "silu_mul");
+}
+
+int vkq_rms_norm(int device, const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,
+                 void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (!x || !weight || !out || rows <= 0 || n <= 0 || rows > 0x7FFFFFFF || !(eps >= 0.0f)) {
+        set_error("invalid arguments to vkq_rms_norm");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(out)) &
+        3u) {
+        set_error("vkq_rms_norm needs 4-byte aligned buffers");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(rms_norm(x, weight, out, rows, n, eps, (cudaStream_t)stream), "rms_norm");
 }
 
 int vkq_device_status(int device, int *code) {

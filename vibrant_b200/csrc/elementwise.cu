@@ -1,0 +1,96 @@
+// elementwise.cu -- the activation and normalisation steps between the
+// linear layers of a decode step, on sm_100a.
+//
+//  * silu_mul: out = SiLU(gate) * up = gate / (1 + exp(-gate)) * up, one pass
+//    over both inputs (the reference runs silu_f32 then mul_f32,
+//    internal/gpu/cuda/kernels.cu:306-341, as tensor.SiLU and tensor.Mul in
+//    internal/transformer/feedforward.go:92-94);
+//  * rms_norm: out[r] = (x[r] / sqrt(mean(x[r]^2) + eps)) * weight, one CTA
+//    per row with a fixed-order reduction (kernels.cu:209-288).
+// Both are HBM-bound streams of a few tens of KB in a decode step: their cost
+// is the launch, so they take part in programmatic dependent launch like the
+// GEMV (the next kernel's prologue overlaps their tail).
+#include <cstdint>
+
+#include "../../include/vkq.h"
+#include "kq_device.cuh"
+#include "vkq_internal.h"
+
+namespace vkq {
+
+__global__ void __launch_bounds__(256) silu_mul_kernel(const float *__restrict__ gate, const float *__restrict__ up,
+                                                       float *__restrict__ out, int64_t n) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t n4 = n / 4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 g = reinterpret_cast<const float4 *>(gate)[i];
+        const float4 u = reinterpret_cast<const float4 *>(up)[i];
+        float4 o;
+        o.x = g.x / (1.0f + expf(-g.x)) * u.x;
+        o.y = g.y / (1.0f + expf(-g.y)) * u.y;
+        o.z = g.z / (1.0f + expf(-g.z)) * u.z;
+        o.w = g.w / (1.0f + expf(-g.w)) * u.w;
+        reinterpret_cast<float4 *>(out)[i] = o;
+    }
+    for (int64_t i = 4 * n4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = gate[i] / (1.0f + expf(-gate[i])) * up[i];
+}
+
+constexpr int kNormThreads = 512;
+
+__global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float *__restrict__ x,
+                                                                const float *__restrict__ weight,
+                                                                float *__restrict__ out, int64_t n, float eps) {
+    __shared__ float part[kNormThreads / 32];
+    __shared__ float rms;
+    pdl_wait();
+    pdl_launch_dependents();
+    const float *xr = x + (int64_t)blockIdx.x * n;
+    float *yr = out + (int64_t)blockIdx.x * n;
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < n; i += kNormThreads) s = fmaf(xr[i], xr[i], s);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < kNormThreads / 32; w++) t += part[w];
+        rms = sqrtf(t / (float)n + eps);
+    }
+    __syncthreads();
+    const float r = rms;
+    for (int64_t i = threadIdx.x; i < n; i += kNormThreads) yr[i] = (xr[i] / r) * weight[i];
+}
+
+static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, cudaStream_t s, void **args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, cudaStream_t s, int device) {
+    const int sms = device_sm_count(device);
+    int64_t blocks = (n / 4 + 255) / 256;
+    if (blocks < 1) blocks = 1;
+    if (blocks > 4 * sms) blocks = 4 * sms;
+    void *args[] = {(void *)&gate, (void *)&up, (void *)&out, (void *)&n};
+    return launch_pdl((const void *)silu_mul_kernel, dim3((unsigned)blocks), dim3(256), s, args);
+}
+
+cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,
+                     cudaStream_t s) {
+    void *args[] = {(void *)&x, (void *)&weight, (void *)&out, (void *)&n, (void *)&eps};
+    return launch_pdl((const void *)rms_norm_kernel, dim3((unsigned)rows), dim3(kNormThreads), s, args);
+}
+
+}  // namespace vkq

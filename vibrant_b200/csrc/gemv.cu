@@ -86,25 +86,61 @@ struct GemvParams {
 // Row-sharded all-gather: column n of this launch's columns is stored into
 // every rank's output [M][y_ld] at column col_off + n.  A separate kernel
 // parameter (growing GemvParams changes the plain kernel's code generation).
+//
+// The weight is this rank's row-block shard (vkq_shard_weight): row k of the
+// shard holds the super-blocks that cover columns [n_base, n_base + N) of row
+// k of the full [K, ld] weight, starting at the block that holds column
+// n_base, in rs / 256 block slots.  Value n of row k therefore sits at
+// position k * rs + ((k * ld + n_base) & 255) + n of the shard's stream, which
+// keeps every value at the in-block position it had in the full weight (a
+// block that straddles two rows or two shards is copied whole and the values
+// outside the row's columns are never read).
+//
+// Protocol (every rank makes the same sequence of calls on one channel):
+//  * seq = sync[0] + 1 is this call's number; CTA 0 posts "started seq" into
+//    every rank's flag array (slot `rank`) once the preceding work on this
+//    rank's stream has completed (after griddepcontrol.wait);
+//  * a CTA stores into other ranks' buffers only after every rank has posted
+//    "started seq" (so each target has finished with the previous contents);
+//    a flag beyond seq, or a wait that runs out, marks the call failed
+//    (sync[2], sticky) and the CTA then stores into its own buffer only;
+//  * the last CTA to finish posts "done seq" to every rank (after a system
+//    fence) unless the call failed, and waits until every rank's "done seq"
+//    is in its own flag array: the kernel's completion means the whole result
+//    is in place.  A failed channel posts nothing more and fails every later
+//    call at once (no waits) until the host resets it.
+constexpr int kMaxPeers = 8;
 struct GatherParams {
-    float *const *peer_y;          // [world] output buffers (this process's mappings)
-    unsigned *const *peer_flags;   // [world] flag arrays: [0, world) started, [world, 2 world) done
-    unsigned *sync;                // this rank's [call counter, finished-CTA counter]
+    float *peer_y[kMaxPeers];         // every rank's output buffer (addresses valid on this device)
+    unsigned *peer_flags[kMaxPeers];  // every rank's flags: [0, world) started, [world, 2 world) done
+    unsigned *sync;                   // this rank's [last call, finished CTAs, failed]
     int world, rank;
     int64_t y_ld, col_off;
-    int64_t ld, n_base;  // W[k][n_base + n] is value k * ld + n_base + n
+    int64_t rs, ld, n_base;           // shard row stride (values), full row length, first column
+    uint64_t wait_ns;                 // budget of each wait on the peers
 };
 
 __device__ __forceinline__ void set_status(int code) { atomicExch(&g_gemv_status, code); }
 
 // Output stores: the local y, or (all-gather) the same position of every
-// rank's output buffer through peer memory (plain stores over NVLink).
-__device__ __forceinline__ void store_peers(const GatherParams &g, int64_t m, int64_t c, float v) {
+// rank's output buffer through peer memory (plain stores over NVLink); only
+// this rank's own buffer when the call has failed (peers == false).
+__device__ __forceinline__ void store_peers(const GatherParams &g, bool peers, int64_t m, int64_t c, float v) {
     const int64_t off = m * g.y_ld + g.col_off + c;
+    if (!peers) {
+        g.peer_y[g.rank][off] = v;
+        return;
+    }
+#pragma unroll 1
     for (int r = 0; r < g.world; r++) g.peer_y[r][off] = v;
 }
-__device__ __forceinline__ void store_peers4(const GatherParams &g, int64_t m, int64_t c, float4 v) {
+__device__ __forceinline__ void store_peers4(const GatherParams &g, bool peers, int64_t m, int64_t c, float4 v) {
     const int64_t off = m * g.y_ld + g.col_off + c;  // 16-byte aligned: widths and offsets are multiples of 32
+    if (!peers) {
+        *reinterpret_cast<float4 *>(g.peer_y[g.rank] + off) = v;
+        return;
+    }
+#pragma unroll 1
     for (int r = 0; r < g.world; r++) *reinterpret_cast<float4 *>(g.peer_y[r] + off) = v;
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
@@ -115,16 +151,21 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
 __device__ __forceinline__ void st_release_sys(unsigned *a, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
 }
-// Bounded wait until flags f[0..count) have all reached seq (32-bit counters
-// compared by signed difference); false when the budget runs out.
-__device__ __forceinline__ bool wait_flags(const unsigned *f, int count, unsigned seq, uint64_t budget_ns) {
+// Bounded wait until flags f[0..count) all equal seq.  Returns 0 on success,
+// kStatusPeer at once when a flag is beyond seq (a rank is out of step), and
+// kStatusTimeout when the budget runs out.
+__device__ __forceinline__ int wait_flags_eq(const unsigned *f, int count, unsigned seq, uint64_t budget_ns) {
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         bool all = true;
-        for (int r = 0; r < count && all; r++) all = (int)(ld_acquire_sys(f + r) - seq) >= 0;
-        if (all) return true;
-        if (globaltimer_ns() - t0 > budget_ns) return false;
-        __nanosleep(100);
+        for (int r = 0; r < count; r++) {
+            const int d = (int)(ld_acquire_sys(f + r) - seq);
+            if (d > 0) return kStatusPeer;
+            all = all && d == 0;
+        }
+        if (all) return 0;
+        if (globaltimer_ns() - t0 > budget_ns) return kStatusTimeout;
+        __nanosleep(200);
     }
 }
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
@@ -362,7 +403,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     //   issue side: byte offset of the row chunk's 16-byte aligned span of
     //   super-blocks and its length (bulk copy), plus the < 16 bytes past the
     //   last 16-byte boundary of w (copied by hand);
-    //   decode side: the low 32 bits of v0 = k*ld + n_base + n0 (in-block
+    //   decode side: the low 32 bits of v0 = k*N + n0, or the shard position
+    //   k*rs + ((k*ld + n_base) & 255) + n0 of the all-gather (in-block
     //   offset of the row's first value and the 16-byte lead of its first
     //   block), the first column n0 of the row's tile, and x of the row.
     auto row_tk = [&](int r, uint32_t &t, uint32_t &k) {
@@ -379,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             uint32_t t, k;
             row_tk(r, t, k);
             const int64_t n0 = (int64_t)t * TN, n1 = imin64(n0 + TN, N);
-            const int64_t base = G ? (int64_t)k * gq.ld + gq.n_base : (int64_t)k * N;
+            const int64_t base = G ? (int64_t)k * gq.rs + (((int64_t)k * gq.ld + gq.n_base) & 255) : (int64_t)k * N;
             const int64_t a_lo = (((base + n0) >> 8) * B) & ~int64_t(15);
             const int64_t byte_hi = ((base + n1 + 255) >> 8) * B;
             int64_t c_hi = imin64((byte_hi + 15) & ~int64_t(15), p.w_floor16);
@@ -417,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             uint32_t t, k;
             row_tk(r, t, k);
             c_n0 = t * TN;
-            if constexpr (G) c_v0 = k * (uint32_t)gq.ld + (uint32_t)gq.n_base + c_n0;
+            if constexpr (G) c_v0 = k * (uint32_t)gq.rs + ((k * (uint32_t)gq.ld + (uint32_t)gq.n_base) & 255u) + c_n0;
             else c_v0 = k * Nu + c_n0;
         }
     };
@@ -451,20 +493,49 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     }
 
     // All-gather: this call's number, and (CTA 0) the "started" flag on every
-    // rank.  A CTA's first output store waits until every rank has started
-    // this call (so it has finished reading the previous result).
+    // rank.  A CTA's first store into other ranks' buffers waits until every
+    // rank has started this call (so it has finished with the previous
+    // contents).  flag[1] carries seq, flag[2] whether peer stores are allowed.
     unsigned seq = 0;
-    bool peers_started = !(G && gq.world > 1);
+    bool peers_checked = !(G && gq.world > 1);
+    bool peers_ok = true;
     if (G && gq.world > 1) {
         if (tid == 0) {
             seq = *reinterpret_cast<volatile unsigned *>(&gq.sync[0]) + 1u;
-            if (blockIdx.x == 0)
+            const bool failed = *reinterpret_cast<volatile unsigned *>(&gq.sync[2]) != 0u;
+            if (blockIdx.x == 0 && !failed)
                 for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.rank, seq);
+            if (failed) set_status(kStatusPeer);
             flag[1] = (int)seq;
+            flag[2] = failed ? 0 : 1;
         }
         named_bar_sync(1, kNW * 32);
         seq = (unsigned)flag[1];
+        if (!flag[2]) {  // the channel failed earlier: no waits, own buffer only
+            peers_checked = true;
+            peers_ok = false;
+        }
     }
+    // Before this CTA's first store into peers' buffers: every rank has
+    // started this call, or the call is marked failed (sticky) and the CTA
+    // keeps to its own buffer.  Called by every thread of the CTA.
+    auto check_peers = [&]() {
+        if constexpr (G) {
+            if (!peers_checked) {
+                if (tid == 0) {
+                    const int st = wait_flags_eq(gq.peer_flags[gq.rank], gq.world, seq, gq.wait_ns);
+                    if (st != 0) {
+                        set_status(st);
+                        atomicExch(&gq.sync[2], 1u);
+                    }
+                    flag[2] = st == 0 ? 1 : 0;
+                }
+                named_bar_sync(1, kNW * 32);
+                peers_ok = flag[2] != 0;
+                peers_checked = true;
+            }
+        }
+    };
 
     const int64_t first_tile = f0 / K;
     const int64_t last_tile = (f1 - 1) / K;
@@ -549,17 +620,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
                 for (int i = 0; i < VH / 2; i++) acc[h][m][i] = make_float2(0.f, 0.f);
             }
         }
-        if constexpr (G) {
-            if (!peers_started) {  // first output store of this CTA in an all-gather call
-                if (tid == 0 && !wait_flags(gq.peer_flags[gq.rank], gq.world, seq, kWaitNs)) set_status(kStatusTimeout);
-                peers_started = true;
-            }
-        }
+        const bool whole = (tile * K >= f0) && ((tile + 1) * K <= f1);
+        if (whole) check_peers();  // first store of this CTA into the ranks' outputs
         named_bar_sync(1, kNW * 32);
         // 3. the slots added in order, stored coalesced
         const int64_t n0 = tile * TN;
         const int ncols = (int)imin64(TN, N - n0);
-        const bool whole = (tile * K >= f0) && ((tile + 1) * K <= f1);
         const int slot = (tile == first_tile) ? 0 : 1;
         for (int idx = tid; idx < MR * TN; idx += kNW * 32) {
             const int m = idx / TN, c = idx % TN;
@@ -572,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
                 for (int w = 2; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
             }
             if (whole) {
-                if constexpr (G) store_peers(gq, m, n0 + c, sum);
+                if constexpr (G) store_peers(gq, peers_ok, m, n0 + c, sum);
                 else p.y[(int64_t)m * N + n0 + c] = sum;
             }
             else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = sum;
@@ -627,9 +693,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     };
     auto to_output = [&](int64_t tile) {
         const int64_t n0 = tile * TN;
+        const bool peers = peers_ok;
         return [=, &gq, &p](int m, int c, float4 v) {
             if constexpr (G) {
-                store_peers4(gq, m, n0 + c, v);
+                store_peers4(gq, peers, m, n0 + c, v);
             } else {
                 float *yo = p.y + (int64_t)m * N + n0 + c;
                 yo[0] = v.x; yo[1] = v.y; yo[2] = v.z; yo[3] = v.w;
@@ -658,6 +725,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         };
         const int n1 = (int)(c_hi - c_lo + 1);
         if (gl == gh) {
+            check_peers();
             sum_rows(tile, part, n1, to_output(tile));
             named_bar_sync(1, kNW * 32);
             if (tid == 0) atomicExch(cnt1, 0);
@@ -677,6 +745,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         if (!flag[0]) return;
         __threadfence();
         auto gpart = [&](int j) { return p.gpartials + (size_t)(tile + gl + j) * MR * TN; };
+        check_peers();
         sum_rows(tile, gpart, (int)(gh - gl + 1), to_output(tile));
         named_bar_sync(1, kNW * 32);
         if (tid == 0) atomicExch(&p.counters[tile], 0);
@@ -762,7 +831,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     if (pend_first) combine(first_tile, old_first);
     if (pend_last) combine(last_tile, old_last);
     // All-gather: the last CTA to finish tells every rank this rank's shard
-    // is in place, then waits until every rank's shard is in its own buffer.
+    // is in place (unless the call failed), then waits until every rank's
+    // shard is in its own buffer.
     if (G && gq.world > 1) {
         named_bar_sync(1, kNW * 32);  // every store of this CTA is issued
         if (tid == 0) {
@@ -772,9 +842,14 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
                 gq.sync[1] = 0u;
                 gq.sync[0] = seq;
                 __threadfence_system();
-                for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, seq);
-                if (!wait_flags(gq.peer_flags[gq.rank] + gq.world, gq.world, seq, kWaitNs))
-                    set_status(kStatusTimeout);
+                if (*reinterpret_cast<volatile unsigned *>(&gq.sync[2]) == 0u) {
+                    for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, seq);
+                    const int st = wait_flags_eq(gq.peer_flags[gq.rank] + gq.world, gq.world, seq, gq.wait_ns);
+                    if (st != 0) {
+                        set_status(st);
+                        atomicExch(&gq.sync[2], 1u);
+                    }
+                }
             }
         }
     }
@@ -923,14 +998,15 @@ static cudaError_t launch_fast(const GemvParams &gp, const GatherParams &gq, con
 
 template <int QT>
 static cudaError_t dispatch_mr(const GemvParams &gp, const GatherParams &gq, const Plan &pl, cudaStream_t st) {
+    const bool gather = gq.world > 0;
     switch (pl.mr) {
     case 1:
         if (pl.vpt == 64)
-            return gq.peer_y ? launch_fast<QT, 1, 64, true>(gp, gq, pl, st) : launch_fast<QT, 1, 64, false>(gp, gq, pl, st);
-        return gq.peer_y ? launch_fast<QT, 1, 32, true>(gp, gq, pl, st) : launch_fast<QT, 1, 32, false>(gp, gq, pl, st);
-    case 2: return gq.peer_y ? launch_fast<QT, 2, 32, true>(gp, gq, pl, st) : launch_fast<QT, 2, 32, false>(gp, gq, pl, st);
-    case 4: return gq.peer_y ? launch_fast<QT, 4, 16, true>(gp, gq, pl, st) : launch_fast<QT, 4, 16, false>(gp, gq, pl, st);
-    default: return gq.peer_y ? launch_fast<QT, 8, 8, true>(gp, gq, pl, st) : launch_fast<QT, 8, 8, false>(gp, gq, pl, st);
+            return gather ? launch_fast<QT, 1, 64, true>(gp, gq, pl, st) : launch_fast<QT, 1, 64, false>(gp, gq, pl, st);
+        return gather ? launch_fast<QT, 1, 32, true>(gp, gq, pl, st) : launch_fast<QT, 1, 32, false>(gp, gq, pl, st);
+    case 2: return gather ? launch_fast<QT, 2, 32, true>(gp, gq, pl, st) : launch_fast<QT, 2, 32, false>(gp, gq, pl, st);
+    case 4: return gather ? launch_fast<QT, 4, 16, true>(gp, gq, pl, st) : launch_fast<QT, 4, 16, false>(gp, gq, pl, st);
+    default: return gather ? launch_fast<QT, 8, 8, true>(gp, gq, pl, st) : launch_fast<QT, 8, 8, false>(gp, gq, pl, st);
     }
 }
 
@@ -984,17 +1060,25 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
     gp.row_cap = pl.row_cap;
     gp.stages = pl.stages;
     GatherParams gq{};
-    gq.world = 1;
+    gq.world = 0;  // 0: the plain kernel
     if (gather) {
-        gq.peer_y = gather->peer_y;
-        gq.peer_flags = gather->peer_flags;
+        if (gather->world < 1 || gather->world > kMaxPeers) {
+            set_error("the all-gather serves 1 to %d ranks (got %d)", kMaxPeers, gather->world);
+            return 1;
+        }
+        for (int r = 0; r < gather->world; r++) {
+            gq.peer_y[r] = gather->peer_y[r];
+            gq.peer_flags[r] = gather->peer_flags[r];
+        }
         gq.sync = gather->sync;
         gq.world = gather->world;
         gq.rank = gather->rank;
         gq.y_ld = gather->y_ld;
         gq.col_off = gather->col_off;
-        gq.ld = gather->w_ld;
+        gq.rs = gather->rs;
+        gq.ld = gather->ld;
         gq.n_base = gather->n_base;
+        gq.wait_ns = gather->wait_ns;
     }
     switch (s.qtype) {
     case kQ4K: e = dispatch_mr<kQ4K>(gp, gq, pl, stream); break;

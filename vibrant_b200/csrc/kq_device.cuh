@@ -21,6 +21,7 @@ template <> struct QT_<kQ6K> { static constexpr int BYTES = 210; };
 
 // Device status word values (mirrors vkq_status).
 constexpr int kStatusTimeout = 6;
+constexpr int kStatusPeer = 8;  // a peer rank is out of step, or its channel already failed
 
 // ---- float16 -> float32 exactly as the reference does it -----------------
 // internal/tensor/tensor.go:629-676: subnormals are normalised exactly,

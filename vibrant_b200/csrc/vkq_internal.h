@@ -29,17 +29,23 @@ struct GemvShape {
 // Workspace bytes the GEMV plan needs (0 when it needs none).
 size_t gemv_workspace_bytes(const GemvShape &s, int device);
 // Row-sharded all-gather through peer memory: the launch computes columns
-// [n_base, n_base + N) of a weight with rows of w_ld values and stores column
-// n_base + n of the result into every rank's output [M][y_ld] at column
-// col_off + n; see vkq_gemv_allgather.
+// [n_base, n_base + N) of a [K, ld] weight from this rank's row-block shard
+// (row stride rs values) and stores column n_base + n of the result into every
+// rank's output [M][y_ld] at column col_off + n; see vkq_gemv_allgather.
+constexpr int kMaxRanks = 8;
 struct GatherArgs {
-    float *const *peer_y;          // device array of `world` output pointers
-    unsigned *const *peer_flags;   // device array of `world` flag arrays (2 * world words each)
-    unsigned *sync;                // this rank's two counters
+    float *peer_y[kMaxRanks];         // every rank's output buffer (device addresses usable here)
+    unsigned *peer_flags[kMaxRanks];  // every rank's flag array (2 * world words each)
+    unsigned *sync;                   // this rank's channel words (4 uint32)
     int world, rank;
     int64_t y_ld, col_off;
-    int64_t w_ld, n_base;
+    int64_t rs, ld, n_base;
+    uint64_t wait_ns;
 };
+// Budget of each wait on peer ranks (ns): VKQ_PEER_WAIT_MS, default 2000 ms.
+uint64_t peer_wait_ns();
+// Block slots per row of the row-block shard of columns [lo, hi).
+int64_t shard_row_blocks(int64_t K, int64_t N, int64_t lo, int64_t hi);
 // Returns a vkq_status code; on failure writes a message with set_error.
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
                 size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather = nullptr);
@@ -54,6 +60,11 @@ size_t gemm_workspace_bytes(const GemvShape &s, int device);
 int gemm_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
                 size_t ws_bytes, cudaStream_t stream, int device);
 int gemm_read_status();  // reads and clears this TU's device status word (synchronous)
+
+// SiLU(gate) * up and row-wise RMSNorm (elementwise.cu); 16-byte aligned buffers.
+cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, cudaStream_t s, int device);
+cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,
+                     cudaStream_t s);
 
 void set_error(const char *fmt, ...);
 bool vkq_last_error_empty();

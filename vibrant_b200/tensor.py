@@ -106,16 +106,40 @@ def dequant_transpose(w: QuantWeight, stream=None) -> torch.Tensor:
     return out
 
 
-# ---- row-sharded matmul across the GPUs of one node (one process per GPU) ----
+# ---- row-sharded matmul across the GPUs of one node ----
 
 def shard_columns(N: int, world: int) -> tuple[int, list[tuple[int, int]]]:
     """Equal shard width (a multiple of 32, as the fast GEMV and the peer
     all-gather need) and each rank's [lo, hi) output columns; the last
-    rank's range may be shorter than the width (its tail is padding)."""
+    rank's range may be shorter than the width.  Same plan as
+    vkq_shard_columns."""
     width = -(-N // world)
     width = -(-width // 32) * 32
     bounds = [(min(r * width, N), min((r + 1) * width, N)) for r in range(world)]
     return width, bounds
+
+
+class ShardedWeight:
+    """Rank `rank`'s row-block shard of a quantized [K, N] weight, on its
+    device: only the super-blocks under the rank's output columns (blocks
+    straddling rows or shards duplicated), built on the host from the full
+    raw bytes with vkq_shard_weight and uploaded as raw blocks."""
+
+    def __init__(self, qtype: int, K: int, N: int, world: int, rank: int, full_bytes, device="cuda"):
+        self.qtype, self.K, self.N, self.world, self.rank = qtype, K, N, world, rank
+        self.lo, self.hi = vkq.shard_columns(N, world, rank)
+        host = vkq.shard_weight(qtype, np.ascontiguousarray(full_bytes, dtype=np.uint8), K, N, self.lo, self.hi)
+        self.buf = torch.from_numpy(host).to(device=device)
+        if self.buf.data_ptr() % 16:
+            raise ValueError("shard buffer is not 16-byte aligned")
+
+    @property
+    def nbytes(self) -> int:
+        return self.buf.numel()
+
+    @property
+    def width(self) -> int:
+        return self.hi - self.lo
 
 
 class _DeviceArray:
@@ -127,16 +151,16 @@ class _DeviceArray:
 
 
 class PeerGather:
-    """Output buffers and flags for vkq_gemv_allgather, created collectively
-    by every rank of a process group (one process per GPU).
+    """One all-gather channel for vkq_gemv_allgather, created collectively by
+    every rank of a process group (one process per GPU).
 
-    Every rank keeps the full quantized weight [K, N]; rank r computes output
-    columns bounds[r] = [lo, hi) of shard_columns(N, world) and the kernel
-    stores them into every rank's output [m_max, N].  Each rank allocates its
-    output and a flag array with vkq_ipc_alloc, the 64-byte handles are
-    exchanged over the group and every rank maps every other rank's buffers
-    (vkq_ipc_open).  `gemv` then leaves the whole x @ W in `out` on every
-    rank, with no collective library call on the data path."""
+    Rank r holds ShardedWeight(..., world, r) and computes output columns
+    vkq_shard_columns(N, world, r); the kernel stores them into every rank's
+    output [m_max, N].  Each rank allocates its output and a flag array with
+    vkq_ipc_alloc, the 64-byte handles are exchanged over the group and every
+    rank maps every other rank's buffers (vkq_ipc_open).  `gemv` then leaves
+    the whole x @ W in `out` on every rank, with no collective library call on
+    the data path.  Every rank must make the same sequence of calls."""
 
     def __init__(self, group, rank: int, world: int, device: int, N: int, m_max: int = 8):
         import torch.distributed as dist
@@ -152,39 +176,50 @@ class PeerGather:
         handles: list = [None] * world
         dist.all_gather_object(handles, (h_out, h_flags), group=group)
         self._mapped: list[int] = []
-        outs, flags = [], []
+        self.peer_out, self.peer_flags = [], []
         for r, (ho, hf) in enumerate(handles):
             if r == rank:
-                outs.append(self.out_ptr)
-                flags.append(self.flags_ptr)
+                self.peer_out.append(self.out_ptr)
+                self.peer_flags.append(self.flags_ptr)
                 continue
             po, pf = vkq.ipc_open(ho, device), vkq.ipc_open(hf, device)
             self._mapped += [po, pf]
-            outs.append(po)
-            flags.append(pf)
-        dev = f"cuda:{device}"
-        self.peer_out = torch.tensor(outs, dtype=torch.int64, device=dev)
-        self.peer_flags = torch.tensor(flags, dtype=torch.int64, device=dev)
-        self.out = torch.as_tensor(_DeviceArray(self.out_ptr, (m_max, N)), device=dev)
+            self.peer_out.append(po)
+            self.peer_flags.append(pf)
+        self.out = torch.as_tensor(_DeviceArray(self.out_ptr, (m_max, N)), device=f"cuda:{device}")
+        self.flag_words = torch.as_tensor(_DeviceArray(self.flags_ptr, (2 * world,), "<u4"),
+                                          device=f"cuda:{device}")
+        self.sync_words = torch.as_tensor(_DeviceArray(self.sync_ptr, (4,), "<u4"), device=f"cuda:{device}")
 
-    def gemv(self, x: torch.Tensor, w: QuantWeight, ws: torch.Tensor | None = None,
+    def gemv(self, x: torch.Tensor, w: ShardedWeight, ws: torch.Tensor | None = None,
              stream: torch.cuda.Stream | None = None) -> torch.Tensor:
         """x @ W across the group: returns out[:M] (vkq_gemv_allgather)."""
         if w.N != self.N or x.shape[1] != w.K or x.dtype != torch.float32:
             raise ValueError("the weight or x does not match the group")
+        if (w.world, w.rank) != (self.world, self.rank):
+            raise ValueError("the shard was built for another rank")
         M = x.shape[0]
         if M > self.m_max:
             raise ValueError(f"M={M} exceeds the group's m_max={self.m_max}")
         x = x.contiguous()
-        lo, hi = self.bounds[self.rank]
         if ws is None:
-            ws = workspace(workspace_bytes(w.qtype, M, w.K, hi - lo, self.device), self.device)
+            ws = workspace(workspace_bytes(w.qtype, M, w.K, w.width, self.device), self.device)
         st = stream if stream is not None else torch.cuda.current_stream(x.device)
-        vkq.gemv_allgather(w.qtype, w.buf.data_ptr(), w.nbytes, w.K, w.N, lo, hi, x.data_ptr(), M,
-                           self.peer_out.data_ptr(), self.peer_flags.data_ptr(), self.sync_ptr, self.world,
-                           self.rank, ws.data_ptr() if ws is not None else None,
-                           ws.numel() if ws is not None else 0, device=self.device, stream=st)
+        vkq.gemv_allgather(w.qtype, w.buf.data_ptr(), w.nbytes, w.K, w.N, w.lo, w.hi, x.data_ptr(), M,
+                           self.peer_out, self.peer_flags, self.sync_ptr, self.world, self.rank,
+                           ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                           device=self.device, stream=st)
         return self.out[:M]
+
+    def reset(self) -> None:
+        """Collective: zero every rank's channel (after a failed call)."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self.flag_words.zero_()
+        self.sync_words.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
     def close(self) -> None:
         """Collective: unmap the peers' buffers, then free this rank's."""
@@ -197,3 +232,39 @@ class PeerGather:
         dist.barrier(group=self.group)
         for p in (self.out_ptr, self.flags_ptr, self.sync_ptr):
             vkq.ipc_free(p, self.device)
+
+
+class Comm:
+    """In-process form (vkq_comm_init): one process drives every listed GPU.
+    `gemv` runs one sharded call on every device and returns the per-device
+    outputs [M, N], each holding the whole product once the streams finish."""
+
+    def __init__(self, devices: list[int]):
+        self.devices = list(devices)
+        self.world = len(self.devices)
+        self.handle = vkq.comm_init(self.devices)
+        self.streams = [torch.cuda.Stream(device=d) for d in self.devices]
+
+    def shards(self, qtype: int, K: int, N: int, full_bytes) -> list[ShardedWeight]:
+        return [ShardedWeight(qtype, K, N, self.world, r, full_bytes, device=f"cuda:{d}")
+                for r, d in enumerate(self.devices)]
+
+    def gemv(self, xs: list[torch.Tensor], shards: list[ShardedWeight], ys: list[torch.Tensor]) -> list[torch.Tensor]:
+        w0 = shards[0]
+        M = xs[0].shape[0]
+        wss = []
+        for r, d in enumerate(self.devices):
+            wss.append(workspace(workspace_bytes(w0.qtype, M, w0.K, shards[r].width, d), d))
+        vkq.gemv_sharded(self.handle, w0.qtype, [s.buf.data_ptr() for s in shards], [s.nbytes for s in shards],
+                         w0.K, w0.N, [x.data_ptr() for x in xs], M, [y.data_ptr() for y in ys],
+                         [ws.data_ptr() if ws is not None else 0 for ws in wss],
+                         [ws.numel() if ws is not None else 0 for ws in wss], self.streams)
+        return ys
+
+    def reset(self) -> None:
+        vkq.comm_reset(self.handle)
+
+    def close(self) -> None:
+        if self.handle:
+            vkq.comm_destroy(self.handle)
+            self.handle = 0

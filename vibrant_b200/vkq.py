@@ -17,7 +17,7 @@ BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
 QTYPE_NAMES = {Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
 
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_MISALIGNED, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE_TIMEOUT, \
-    ERR_NCCL = range(8)
+    ERR_NCCL, ERR_PEER = range(9)
 
 # every symbol declared in include/vkq.h, with (restype, argtypes)
 _vp = ctypes.c_void_p
@@ -44,6 +44,18 @@ SIGNATURES = {
     "vkq_ipc_free": (_int, [_int, _vp]),
     "vkq_gemv_allgather": (_int, [_int, _int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _int,
                                   _int, _vp, _sz, _vp]),
+    "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
+    "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "vkq_shard_columns": (_int, [_i64, _int, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "vkq_shard_bytes": (_int, [_int, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "vkq_shard_weight": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64]),
+    "vkq_comm_init": (_int, [_int, ctypes.POINTER(_int), ctypes.POINTER(_vp)]),
+    "vkq_comm_reset": (_int, [_vp]),
+    "vkq_comm_destroy": (_int, [_vp]),
+    "vkq_comm_size": (_int, [_vp]),
+    "vkq_gemv_sharded": (_int, [_vp, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64, _i64, ctypes.POINTER(_vp),
+                                _i64, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_sz),
+                                ctypes.POINTER(_vp)]),
 }
 
 
@@ -134,6 +146,17 @@ def gemv_noalloc(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: in
     _check(load().vkq_gemv_noalloc(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, _stream_ptr(stream)))
 
 
+def silu_mul(gate_ptr: int, up_ptr: int, out_ptr: int, n: int, device: int = -1, stream=None) -> None:
+    """vkq_silu_mul: out = SiLU(gate) * up."""
+    _check(load().vkq_silu_mul(device, gate_ptr, up_ptr, out_ptr, n, _stream_ptr(stream)))
+
+
+def rms_norm(x_ptr: int, w_ptr: int, out_ptr: int, rows: int, n: int, eps: float, device: int = -1,
+             stream=None) -> None:
+    """vkq_rms_norm: out[r] = x[r] / sqrt(mean(x[r]^2) + eps) * weight."""
+    _check(load().vkq_rms_norm(device, x_ptr, w_ptr, out_ptr, rows, n, eps, _stream_ptr(stream)))
+
+
 def device_status(device: int = -1) -> int:
     code = _int()
     _check(load().vkq_device_status(device, ctypes.byref(code)))
@@ -165,10 +188,62 @@ def ipc_free(ptr: int, device: int = -1) -> None:
 
 
 def gemv_allgather(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, col_lo: int, col_hi: int, x_ptr: int,
-                   M: int, peer_out_ptr: int, peer_flags_ptr: int, sync_ptr: int, world: int, rank: int,
+                   M: int, peer_out: list[int], peer_flags: list[int], sync_ptr: int, world: int, rank: int,
                    ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
-    """vkq_gemv_allgather: columns [col_lo, col_hi) of x @ W on this rank,
-    stored into every rank's output [M, N] through peer memory (include/vkq.h)."""
-    _check(load().vkq_gemv_allgather(device, qtype, w_ptr, w_bytes, K, N, col_lo, col_hi, x_ptr, M, peer_out_ptr,
-                                     peer_flags_ptr, sync_ptr, world, rank, ws_ptr, ws_bytes,
-                                     _stream_ptr(stream)))
+    """vkq_gemv_allgather: columns [col_lo, col_hi) of x @ W from this rank's
+    row-block shard, stored into every rank's output [M, N] through peer
+    memory; peer_out / peer_flags are host lists of device pointers."""
+    po = (_vp * world)(*peer_out)
+    pf = (_vp * world)(*peer_flags)
+    _check(load().vkq_gemv_allgather(device, qtype, w_ptr, w_bytes, K, N, col_lo, col_hi, x_ptr, M, po, pf, sync_ptr,
+                                     world, rank, ws_ptr, ws_bytes, _stream_ptr(stream)))
+
+
+def shard_columns(N: int, world: int, rank: int) -> tuple[int, int]:
+    """vkq_shard_columns: the [lo, hi) output columns of a rank."""
+    lo, hi = _i64(), _i64()
+    _check(load().vkq_shard_columns(N, world, rank, ctypes.byref(lo), ctypes.byref(hi)))
+    return lo.value, hi.value
+
+
+def shard_bytes(qtype: int, K: int, N: int, col_lo: int, col_hi: int) -> tuple[int, int]:
+    """vkq_shard_bytes: (block slots per row, bytes) of a row-block shard."""
+    rb, nb = _i64(), _i64()
+    _check(load().vkq_shard_bytes(qtype, K, N, col_lo, col_hi, ctypes.byref(rb), ctypes.byref(nb)))
+    return rb.value, nb.value
+
+
+def shard_weight(qtype: int, w, K: int, N: int, col_lo: int, col_hi: int):
+    """vkq_shard_weight on host bytes (numpy uint8): the row-block shard of
+    columns [col_lo, col_hi) as a new numpy uint8 array."""
+    import numpy as np
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    _, nb = shard_bytes(qtype, K, N, col_lo, col_hi)
+    out = np.empty(nb, np.uint8)
+    _check(load().vkq_shard_weight(qtype, w.ctypes.data, w.size, K, N, col_lo, col_hi, out.ctypes.data, nb))
+    return out
+
+
+def comm_init(devices: list[int]) -> int:
+    """vkq_comm_init: an in-process communicator over `devices` (handle)."""
+    arr = (_int * len(devices))(*devices)
+    h = _vp()
+    _check(load().vkq_comm_init(len(devices), arr, ctypes.byref(h)))
+    return h.value
+
+
+def comm_reset(comm: int) -> None:
+    _check(load().vkq_comm_reset(comm))
+
+
+def comm_destroy(comm: int) -> None:
+    _check(load().vkq_comm_destroy(comm))
+
+
+def gemv_sharded(comm: int, qtype: int, w_shards: list[int], w_bytes: list[int], K: int, N: int, x: list[int], M: int,
+                 y: list[int], workspaces: list[int], ws_bytes: list[int], streams: list) -> None:
+    """vkq_gemv_sharded: one call on every device of the communicator."""
+    n = len(w_shards)
+    _check(load().vkq_gemv_sharded(comm, qtype, (_vp * n)(*w_shards), (_i64 * n)(*w_bytes), K, N, (_vp * n)(*x), M,
+                                   (_vp * n)(*y), (_vp * n)(*workspaces), (_sz * n)(*ws_bytes),
+                                   (_vp * n)(*[_stream_ptr(s) for s in streams])))
