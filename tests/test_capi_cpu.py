@@ -95,3 +95,14 @@ def test_exact_encoders_round_trip(oracle):
     assert np.array_equal(oracle.dequantize(12, helpers.encode_q45k_exact(v4, 12))[:300], v4.astype(np.float32))
     v5 = np.arange(32).repeat(10)[:300]
     assert np.array_equal(oracle.dequantize(13, helpers.encode_q45k_exact(v5, 13))[:300], v5.astype(np.float32))
+
+
+def test_build_never_flushes_subnormals():
+    """The decode feeds raw quants to fma as subnormal operands (q * 2^-149)
+    and the dequantization keeps subnormal results: a flush-to-zero build
+    would turn every weight into zero (or -dmin*m).  nvcc exposes no macro for
+    it, so the build flags pin it."""
+    from vibrant_b200 import build
+    flags = build.NVCC_FLAGS
+    assert "-ftz=false" in flags
+    assert not any(f in flags for f in ("--use_fast_math", "-use_fast_math", "-ftz=true", "--ftz=true"))

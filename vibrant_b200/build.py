@@ -23,7 +23,13 @@ LIBDIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIBDIR, "libvkq.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
+# -ftz=false -prec-div=true -prec-sqrt=true: the decode uses raw quants as
+# subnormal fma operands and the bit-exact dequantization keeps subnormal
+# results, so no flush-to-zero (and no --use_fast_math) may ever reach these
+# kernels; nvcc exposes no macro a source file could check, so the flags are
+# pinned here and tests/test_capi_cpu.py checks them.
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-ftz=false", "-prec-div=true", "-prec-sqrt=true",
+              "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden", "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]
 
 

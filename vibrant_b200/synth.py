@@ -47,6 +47,29 @@ def random_bytes(qtype: int, K: int, N: int, seed: int) -> np.ndarray:
     return rng.integers(0, 256, size=n_blocks(K, N) * BLOCK_BYTES[qtype], dtype=np.uint8)
 
 
+def weights_device(qtype: int, K: int, N: int, seed: int, device):
+    """Super-blocks with the same value distributions as `weights`, drawn on
+    the GPU with torch's generator (for model-scale workloads whose GBs of
+    weights would take minutes to draw on the host); returns a uint8 tensor."""
+    import torch
+    nb = n_blocks(K, N)
+    bb = BLOCK_BYTES[qtype]
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    b = torch.randint(0, 256, (nb, bb), dtype=torch.uint8, generator=g, device=device)
+    if qtype in (Q4_K, Q5_K):
+        d = (torch.randn(nb, generator=g, device=device).abs() * 0.01).half()
+        dm = (torch.randn(nb, generator=g, device=device).abs() * 0.005).half()
+        b[:, 0:2] = d.view(torch.uint8).view(nb, 2)
+        b[:, 2:4] = dm.view(torch.uint8).view(nb, 2)
+    else:
+        b[:, 192:208] = torch.randint(-32, 32, (nb, 16), dtype=torch.int8, generator=g,
+                                      device=device).view(torch.uint8)
+        d = (torch.randn(nb, generator=g, device=device).abs() * 0.002).half()
+        b[:, 208:210] = d.view(torch.uint8).view(nb, 2)
+    return b.view(-1)
+
+
 def activations(M: int, K: int, seed: int) -> np.ndarray:
     return np.random.default_rng(seed).standard_normal((M, K), dtype=np.float32)
 
@@ -60,3 +83,32 @@ WORKLOADS = {
     # prefill GEMM of the FFN projection, 512 tokens
     "q5k_prefill_gemm_512x2048x11008": dict(qtype=Q5_K, K=2048, N=11008, M=512, seed=3),
 }
+
+# Whole-model decode workloads: the linear layers of one decode step.
+# 3B class: 36 layers, hidden 2048, 16 query / 2 KV heads of dim 128, FFN
+# 11008, vocabulary 151936; q/k/v/o/gate/up Q4_K, down and the LM head Q6_K.
+MODEL_3B = dict(layers=36, hidden=2048, q_out=16 * 128, kv_out=2 * 128, ffn=11008, vocab=151936,
+                q4=Q4_K, down=Q6_K, head=Q6_K)
+# 14B/32B class batched decode: hidden 5120, FFN 27648, 64 layers, 40 query /
+# 8 KV heads of dim 128, every linear layer Q4_K.
+MODEL_14B = dict(layers=64, hidden=5120, q_out=40 * 128, kv_out=8 * 128, ffn=27648)
+
+
+def layer_shapes(model: dict) -> list[tuple[str, int, int, int]]:
+    """(role, qtype, K, N) of the linear layers of one transformer layer, in
+    the order the reference calls them (internal/transformer/attention.go:120,
+    124, 128, 183; feedforward.go:87, 90, 98)."""
+    h, f = model["hidden"], model["ffn"]
+    q4 = model.get("q4", Q4_K)
+    down = model.get("down", Q4_K)
+    return [("q", q4, h, model["q_out"]), ("k", q4, h, model["kv_out"]), ("v", q4, h, model["kv_out"]),
+            ("o", q4, model["q_out"], h), ("gate", q4, h, f), ("up", q4, h, f), ("down", down, f, h)]
+
+
+def model_bytes(model: dict, with_head: bool = True) -> int:
+    """Algorithmic weight bytes of one decode step (all layers, and the LM head)."""
+    per = sum(n_blocks(K, N) * BLOCK_BYTES[qt] for _, qt, K, N in layer_shapes(model))
+    total = per * model["layers"]
+    if with_head and "vocab" in model:
+        total += n_blocks(model["hidden"], model["vocab"]) * BLOCK_BYTES[model["head"]]
+    return total

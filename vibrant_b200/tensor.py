@@ -119,17 +119,41 @@ def shard_columns(N: int, world: int) -> tuple[int, list[tuple[int, int]]]:
     return width, bounds
 
 
-class ShardedWeight:
-    """Rank `rank`'s row-block shard of a quantized [K, N] weight, on its
-    device: only the super-blocks under the rank's output columns (blocks
-    straddling rows or shards duplicated), built on the host from the full
-    raw bytes with vkq_shard_weight and uploaded as raw blocks."""
+def shard_device(full: torch.Tensor, qtype: int, K: int, N: int, lo: int, hi: int) -> torch.Tensor:
+    """Row-block shard of columns [lo, hi) built on the device from the full
+    raw weight already there: the same bytes as vkq_shard_weight (for weights
+    drawn on the GPU, whose GBs would be slow to bring back to the host)."""
+    B = vkq.BLOCK_BYTES[qtype]
+    rb, _ = vkq.shard_bytes(qtype, K, N, lo, hi)
+    blocks = full.view(-1, B)
+    dev = full.device
+    k = torch.arange(K, device=dev, dtype=torch.int64)
+    v0 = k * N + lo
+    count = ((v0 & 255) + (hi - lo) - 1) // 256 + 1
+    j = torch.arange(rb, device=dev, dtype=torch.int64)
+    valid = j[None, :] < count[:, None]
+    idx = torch.where(valid, (v0 >> 8)[:, None] + j[None, :], torch.zeros_like(j)[None, :])
+    out = blocks[idx.reshape(-1)].view(K, rb, B)
+    out[~valid] = 0
+    return out.reshape(-1)
 
-    def __init__(self, qtype: int, K: int, N: int, world: int, rank: int, full_bytes, device="cuda"):
+
+class ShardedWeight:
+    """A rank's row-block shard of a quantized [K, N] weight, on its device:
+    only the super-blocks under the rank's output columns (blocks straddling
+    rows or shards duplicated).  Built from the full raw bytes on the host
+    with vkq_shard_weight (numpy input), or on the device (torch input).
+    `bounds` overrides the column range of vkq_shard_columns(N, world, rank)."""
+
+    def __init__(self, qtype: int, K: int, N: int, world: int, rank: int, full_bytes, device="cuda",
+                 bounds: tuple[int, int] | None = None):
         self.qtype, self.K, self.N, self.world, self.rank = qtype, K, N, world, rank
-        self.lo, self.hi = vkq.shard_columns(N, world, rank)
-        host = vkq.shard_weight(qtype, np.ascontiguousarray(full_bytes, dtype=np.uint8), K, N, self.lo, self.hi)
-        self.buf = torch.from_numpy(host).to(device=device)
+        self.lo, self.hi = bounds if bounds is not None else vkq.shard_columns(N, world, rank)
+        if isinstance(full_bytes, torch.Tensor) and full_bytes.is_cuda:
+            self.buf = shard_device(full_bytes, qtype, K, N, self.lo, self.hi).to(device)
+        else:
+            host = vkq.shard_weight(qtype, np.ascontiguousarray(full_bytes, dtype=np.uint8), K, N, self.lo, self.hi)
+            self.buf = torch.from_numpy(host).to(device=device)
         if self.buf.data_ptr() % 16:
             raise ValueError("shard buffer is not 16-byte aligned")
 
@@ -140,6 +164,14 @@ class ShardedWeight:
     @property
     def width(self) -> int:
         return self.hi - self.lo
+
+    def as_weight(self) -> "QuantWeight":
+        """The shard as a plain [K, hi - lo] weight: valid when the columns
+        are whole super-block columns (N, lo and hi multiples of 256), where
+        the shard is exactly that weight's stream."""
+        if self.N % 256 or self.lo % 256 or self.hi % 256:
+            raise ValueError("the shard is a plain weight only for whole super-block columns")
+        return QuantWeight(self.qtype, self.K, self.width, self.buf, device=self.buf.device)
 
 
 class _DeviceArray:
