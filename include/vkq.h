@@ -114,7 +114,10 @@ VKQ_API int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, in
                const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
                void *stream);
 
-/* The fp32 CUDA-core path of vkq_matmul, for 1 <= M <= 8 (decode). */
+/* The fp32-class GEMV path of vkq_matmul, for 1 <= M <= 8 (decode): the
+ * tensor-core kernel for M <= 4 (dequantized quants and per-sub-block scaled
+ * x split into three bf16 parts, fp32 accumulate) or the CUDA-core kernel;
+ * both within max relative error 1e-5 of sum_k |x w|. */
 VKQ_API int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
              const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
              void *stream);
@@ -127,6 +130,14 @@ VKQ_API int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int6
 VKQ_API int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                      const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
                      void *stream);
+
+/* Selects the kernel that serves vkq_gemv / vkq_matmul for 1 <= M <= 8,
+ * process-wide: 0 automatic (the default), 1 the CUDA-core kernel, 2 the
+ * tensor-core kernel (M <= 4; both in the 1e-5 tolerance class).  Returns
+ * the previous choice, or -1 for an invalid one.  No counterpart in the
+ * reference (it has one fp32 kernel, internal/gpu/cuda/kernels.cu:61-77);
+ * for tests and measurements. */
+VKQ_API int vkq_set_gemv_path(int path);
 
 /* The fp32 GEMV of vkq_gemv without a workspace argument, for callers that
  * cannot allocate device memory: a host whose allocator owns every byte of

@@ -11,6 +11,8 @@
  */
 #include "kq_oracle.h"
 
+#include <float.h>
+#include <math.h>
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
@@ -395,5 +397,82 @@ int ko_matmul_dequant_untransposed(int qtype, const float *a, int64_t M, int64_t
         for (int64_t n = 0; n < N; n++) wt[n * K + k] = w_scratch[k * N + n];
     dispatch_transposed(a, wt, M, K, N, c, nthreads);
     free(wt);
+    return 0;
+}
+
+/* QuantizeQ4_K (internal/tensor/quant_q4k.go:215-282), serialized in the
+ * byte order of QuantizeQ4_KTensor (matmul_quant_helpers.go:116-145): per
+ * block min/max, scale = (max - min) / 15 (at least 1e-10), D = f16(scale),
+ * Dmin = f16(min), the scale bytes 0 and 6 set to 32 and the rest zero, and
+ * q = uint8((x - min) / scale) clamped to 15, packed low nibble first.  The
+ * reference's test quantizer: only sub-block 0 gets a non-zero scale. */
+int ko_quantize_q4k(const float *in, int64_t n, uint8_t *out) {
+    if (n <= 0) return -1;
+    const int64_t nb = (n + 255) / 256;
+    memset(out, 0, (size_t)(nb * KO_Q4K_BYTES));
+    for (int64_t b = 0; b < nb; b++) {
+        uint8_t *blk = out + b * KO_Q4K_BYTES;
+        const int64_t off = b * 256, end = off + 256 < n ? off + 256 : n;
+        float mn = FLT_MAX, mx = -FLT_MAX;
+        for (int64_t i = off; i < end; i++) {
+            if (in[i] < mn) mn = in[i];
+            if (in[i] > mx) mx = in[i];
+        }
+        float scale = (mx - mn) / 15.0f;
+        if (scale < 1e-10f) scale = 1e-10f;
+        const uint16_t d = ko_f32_to_f16(scale), dm = ko_f32_to_f16(mn);
+        blk[0] = (uint8_t)d;
+        blk[1] = (uint8_t)(d >> 8);
+        blk[2] = (uint8_t)dm;
+        blk[3] = (uint8_t)(dm >> 8);
+        blk[4 + 0] = 32;
+        blk[4 + 6] = 32;
+        for (int64_t i = off; i < end; i++) {
+            const int64_t idx = i - off;
+            uint8_t q = (uint8_t)((in[i] - mn) / scale);
+            if (q > 15) q = 15;
+            if (idx % 2 == 0) blk[16 + idx / 2] = q & 0x0F;
+            else blk[16 + idx / 2] |= (uint8_t)((q & 0x0F) << 4);
+        }
+    }
+    return 0;
+}
+
+/* QuantizeQ6_K (internal/tensor/quant_q6k.go:214-294), serialized in the
+ * byte order of QuantizeQ6_KTensor (matmul_quant_helpers.go:62-92): d =
+ * max(|max|, |min|) / 32 (at least 1e-10), D = f16(d), every group scale 1,
+ * q = int(x / d + 32.5) clamped to [0, 63]: low nibbles into Ql, high bit
+ * pairs into Qh. */
+int ko_quantize_q6k(const float *in, int64_t n, uint8_t *out) {
+    if (n <= 0) return -1;
+    const int64_t nb = (n + 255) / 256;
+    memset(out, 0, (size_t)(nb * KO_Q6K_BYTES));
+    for (int64_t b = 0; b < nb; b++) {
+        uint8_t *blk = out + b * KO_Q6K_BYTES;
+        const int64_t off = b * 256, end = off + 256 < n ? off + 256 : n;
+        float mn = FLT_MAX, mx = -FLT_MAX;
+        for (int64_t i = off; i < end; i++) {
+            if (in[i] < mn) mn = in[i];
+            if (in[i] > mx) mx = in[i];
+        }
+        const double amax = fabs((double)mx) > fabs((double)mn) ? fabs((double)mx) : fabs((double)mn);
+        float d = (float)amax / 32.0f;
+        if (d < 1e-10f) d = 1e-10f;
+        const uint16_t dh = ko_f32_to_f16(d);
+        for (int j = 0; j < 16; j++) blk[192 + j] = 1;
+        blk[208] = (uint8_t)dh;
+        blk[209] = (uint8_t)(dh >> 8);
+        for (int64_t i = off; i < end; i++) {
+            const int64_t idx = i - off;
+            const float scale = 1.0f;  /* Scales[idx / 16] */
+            const float scaled = in[i] / (d * scale);
+            int q = (int)(scaled + 32.5f);
+            if (q < 0) q = 0;
+            if (q > 63) q = 63;
+            if (idx % 2 == 0) blk[idx / 2] = (uint8_t)(q & 0x0F);
+            else blk[idx / 2] |= (uint8_t)((q & 0x0F) << 4);
+            blk[128 + idx / 4] |= (uint8_t)(((q >> 4) & 0x03) << ((idx % 4) * 2));
+        }
+    }
     return 0;
 }

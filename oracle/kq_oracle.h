@@ -111,6 +111,13 @@ int ko_matmul_dequant_untransposed(int qtype, const float *a, int64_t M, int64_t
                                    const uint8_t *bq, int64_t N, float *c, float *w_scratch,
                                    int nthreads);
 
+/* The reference's test quantizers (QuantizeQ4_K quant_q4k.go:215-282,
+ * QuantizeQ6_K quant_q6k.go:214-294), serialized as QuantizeQ4_KTensor /
+ * QuantizeQ6_KTensor do (matmul_quant_helpers.go:62-145): n floats ->
+ * ceil(n/256) blocks. */
+int ko_quantize_q4k(const float *in, int64_t n, uint8_t *out);
+int ko_quantize_q6k(const float *in, int64_t n, uint8_t *out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -51,6 +51,8 @@ def lib() -> ctypes.CDLL:
         L.ko_matmul_quant.argtypes = [ctypes.c_int, f32p, i64, i64, u8p, i64, f32p, f32p, ctypes.c_int]
         L.ko_matmul_dequant_untransposed.argtypes = [ctypes.c_int, f32p, i64, i64, u8p, i64, f32p, f32p,
                                                      ctypes.c_int]
+        L.ko_quantize_q4k.argtypes = [f32p, i64, u8p]
+        L.ko_quantize_q6k.argtypes = [f32p, i64, u8p]
         _lib = L
     return _lib
 
@@ -151,3 +153,14 @@ def matmul_single_row_u(x: np.ndarray, w: np.ndarray) -> np.ndarray:
 def dot_abs_bound(x: np.ndarray, w: np.ndarray) -> np.ndarray:
     """sum_k |x[m,k] * W[k,n]| in float64 -- the denominator of the matmul error metric."""
     return np.abs(x.astype(np.float64)) @ np.abs(w.astype(np.float64))
+
+
+def quantize(qtype: int, values: np.ndarray) -> np.ndarray:
+    """The reference's test quantizer for Q4_K or Q6_K (QuantizeQ4_K /
+    QuantizeQ6_K), as raw super-block bytes."""
+    v = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    nb = (v.size + 255) // 256
+    out = np.zeros(nb * BLOCK_BYTES[qtype], np.uint8)
+    fn = {Q4_K: lib().ko_quantize_q4k, Q6_K: lib().ko_quantize_q6k}[qtype]
+    assert fn(_f32p(v), v.size, _u8p(out)) == 0
+    return out

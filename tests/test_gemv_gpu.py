@@ -1,5 +1,7 @@
-"""Parity of the fp32 GEMV (vkq_gemv / vkq_matmul with M <= 8) with the
-oracle: max |y - y_ref| / sum_k |x_k W_kn| <= 1e-5, through the C ABI."""
+"""Parity of the fp32-class GEMV (vkq_gemv / vkq_matmul with M <= 8) with the
+oracle: max |y - y_ref| / sum_k |x_k W_kn| <= 1e-5, through the C ABI.  Every
+test runs on both kernels (vkq_set_gemv_path): the CUDA-core kernel and the
+tensor-core kernel (which serves M <= 4; larger M falls back to CUDA cores)."""
 import glob
 import os
 
@@ -10,6 +12,14 @@ import helpers
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(params=["simt", "tc"], autouse=True)
+def gemv_path(request):
+    from vibrant_b200 import vkq
+    old = vkq.set_gemv_path(vkq.GEMV_SIMT if request.param == "simt" else vkq.GEMV_TC)
+    yield request.param
+    vkq.set_gemv_path(old)
 
 
 @pytest.fixture(scope="module")

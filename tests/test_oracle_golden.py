@@ -304,3 +304,83 @@ def test_cuda_matmul_golden_values_through_oracle(oracle):
     y2 = oracle.matmul_dequant_untransposed(14, np.array([[1, 2, 3], [4, 5, 6]], np.float32),
                                             np.frombuffer(bytes(b2), np.uint8), 3, 2)
     assert y2.reshape(-1).tolist() == [22.0, 28.0, 49.0, 64.0]
+
+
+# ---- the reference's test quantizers (for parity on quantized Gaussian weights) ----
+
+def _np_f32_to_f16(f):
+    """float32ToFloat16 of internal/tensor/tensor.go:606-627 (truncating)."""
+    f = np.float32(f)
+    if f == 0:
+        return 0
+    bits = int(np.array([f], np.float32).view(np.uint32)[0])
+    sign, exp, mant = (bits >> 31) & 1, ((bits >> 23) & 0xFF) - 127 + 15, (bits >> 13) & 0x3FF
+    if exp <= 0:
+        return sign << 15
+    if exp >= 31:
+        return (sign << 15) | 0x7C00
+    return (sign << 15) | (exp << 10) | mant
+
+
+def _np_quantize(qtype, x):
+    """Independent numpy restatement of QuantizeQ4_K / QuantizeQ6_K
+    (quant_q4k.go:215-282, quant_q6k.go:214-294) in the serialized layouts."""
+    x = np.asarray(x, np.float32)
+    nb = (x.size + 255) // 256
+    bb = 144 if qtype == 12 else 210
+    out = np.zeros((nb, bb), np.uint8)
+    for b in range(nb):
+        v = x[b * 256:(b + 1) * 256]
+        mn, mx = np.float32(v.min()), np.float32(v.max())
+        if qtype == 12:
+            scale = np.float32((mx - mn) / np.float32(15.0))
+            scale = max(scale, np.float32(1e-10))
+            d, dm = _np_f32_to_f16(scale), _np_f32_to_f16(mn)
+            out[b, 0], out[b, 1], out[b, 2], out[b, 3] = d & 255, d >> 8, dm & 255, dm >> 8
+            out[b, 4], out[b, 10] = 32, 32
+            q = np.minimum(((v - mn) / scale).astype(np.float32).astype(np.int64), 15)
+            for i, qi in enumerate(q):
+                out[b, 16 + i // 2] |= (int(qi) & 15) << (4 * (i % 2))
+        else:
+            amax = np.float32(max(abs(float(mx)), abs(float(mn))))
+            d = max(np.float32(amax / np.float32(32.0)), np.float32(1e-10))
+            dh = _np_f32_to_f16(d)
+            out[b, 192:208] = 1
+            out[b, 208], out[b, 209] = dh & 255, dh >> 8
+            q = np.clip(np.trunc((v / d).astype(np.float32) + np.float32(32.5)).astype(np.int64), 0, 63)
+            for i, qi in enumerate(q):
+                out[b, i // 2] |= (int(qi) & 15) << (4 * (i % 2))
+                out[b, 128 + i // 4] |= ((int(qi) >> 4) & 3) << (2 * (i % 4))
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("qtype", [12, 14])
+@pytest.mark.parametrize("n", [256, 256 * 3 + 100, 4096])
+def test_quantizers_match_independent_restatement(oracle, qtype, n):
+    x = np.random.default_rng(n + qtype).standard_normal(n).astype(np.float32) * 0.05
+    assert np.array_equal(oracle.quantize(qtype, x), _np_quantize(qtype, x))
+
+
+def test_quantize_q6k_known_answers(oracle):
+    # quant_q6k_test.go:306-330: input i - 128 gives one block with a
+    # reasonable D and every group scale non-zero
+    x = (np.arange(256) - 128).astype(np.float32)
+    b = oracle.quantize(14, x)
+    assert b.size == 210
+    d = oracle.f16_to_f32(int(b[208]) | int(b[209]) << 8)
+    assert 0 < d <= 1000 and d == 4.0
+    assert (b[192:208] != 0).all()
+    # 3.4 blocks (quant_q6k_test.go TestQuantizeQ6_K_MultipleBlocks) -> 4 blocks
+    assert oracle.quantize(14, (np.arange(256 * 3 + 100) % 100 - 50).astype(np.float32)).size == 4 * 210
+    # the round trip stays within one quantization step of the input
+    assert np.abs(oracle.dequantize(14, b) - x).max() <= d
+
+
+def test_quantize_q4k_round_trip_completes(oracle):
+    # quant_q4k_test.go:8-46: the simplified test quantizer round-trips (with a
+    # large error: only sub-block 0 carries a scale)
+    x = np.sin(np.arange(256) * 0.1).astype(np.float32)
+    b = oracle.quantize(12, x)
+    assert b.size == 144 and b[4] == 32 and b[10] == 32
+    y = oracle.dequantize(12, b)
+    assert np.isfinite(y).all() and (y[32:] == y[32:][0]).all()

@@ -1,0 +1,101 @@
+"""Parity on weights that look like real k-quant weights: Gaussian data
+quantized by the reference's own test quantizers (QuantizeQ4_K,
+internal/tensor/quant_q4k.go:215-282; QuantizeQ6_K, quant_q6k.go:214-294,
+restated in the oracle).  Q6_K quants then cluster around the zero point
+q = 32 (the case where a GEMV that accumulates a*q and subtracts 32*sum(a)
+loses the most), and Q4_K blocks carry large negative mins.
+
+Both GEMV kernels (CUDA cores and tensor cores) at 1e-5 of sum_k |x w| for
+M = 1..4, including row-straddling shapes (N % 256 == 128), and the
+tensor-core GEMM at 2e-2 on every output of a 512-row prefill; plus
+activations of extreme magnitude."""
+import numpy as np
+import pytest
+
+import helpers
+
+pytestmark = pytest.mark.gpu
+
+
+def _weights(oracle, qt, K, N, seed, sigma=0.02):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(K * N) * sigma).astype(np.float32)
+    wq = oracle.quantize(qt, w)
+    wd = oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+    return wq, wd
+
+
+@pytest.fixture(params=["simt", "tc"])
+def path(request):
+    from vibrant_b200 import vkq
+    old = vkq.set_gemv_path(vkq.GEMV_SIMT if request.param == "simt" else vkq.GEMV_TC)
+    yield request.param
+    vkq.set_gemv_path(old)
+
+
+@pytest.mark.parametrize("qt,K,N", [(14, 2048, 2048), (12, 2048, 11008), (14, 1024, 19072), (14, 11008, 2048),
+                                    (12, 512, 4352)])
+@pytest.mark.parametrize("M", [1, 2, 3, 4])
+def test_gemv_on_quantized_gaussian_weights(oracle, path, qt, K, N, M):
+    import torch
+    from vibrant_b200 import synth
+    from vibrant_b200 import tensor as vt
+    wq, wd = _weights(oracle, qt, K, N, seed=K + N + qt)
+    x = synth.activations(M, K, seed=M + K)
+    w = vt.QuantWeight(qt, K, N, wq)
+    y = vt.matmul(torch.from_numpy(x).cuda(), w).cpu().numpy()
+    assert helpers.matmul_error(y, x, wd) <= helpers.GEMV_TOL
+    from vibrant_b200 import vkq
+    assert vkq.device_status(0) == vkq.OK
+
+
+def test_q6k_quants_cluster_at_the_zero_point(oracle):
+    """The premise of the test above: with Gaussian data most Q6_K quants
+    lie near 32 (|q - 32| <= 8 for most values)."""
+    wq, _ = _weights(oracle, 14, 64, 1024, seed=1)
+    b = wq.reshape(-1, 210)
+    lo = np.stack([b[:, i // 2] >> (4 * (i % 2)) & 15 for i in range(256)], 1).astype(int)
+    hi = np.stack([b[:, 128 + i // 4] >> (2 * (i % 4)) & 3 for i in range(256)], 1).astype(int)
+    q = lo | (hi << 4)
+    assert np.mean(np.abs(q - 32) <= 8) > 0.8
+
+
+@pytest.mark.parametrize("qt", [12, 14])
+def test_gemm_full_size_prefill_every_output(oracle, qt):
+    """The tcgen05 GEMM on quantized Gaussian weights, 512 x 2048 x 11008 (Q4_K)
+    or 512 x 2048 x 2048 (Q6_K): every one of the M x N outputs within 2e-2."""
+    import torch
+    from vibrant_b200 import synth
+    from vibrant_b200 import tensor as vt
+    K, N, M = 2048, (11008 if qt == 12 else 2048), 512
+    wq, wd = _weights(oracle, qt, K, N, seed=77 + qt)
+    x = synth.activations(M, K, seed=5)
+    w = vt.QuantWeight(qt, K, N, wq)
+    y = vt.matmul(torch.from_numpy(x).cuda(), w, path="gemm").cpu().numpy()
+    assert np.isfinite(y).all()
+    assert helpers.matmul_error(y, x, wd) <= helpers.GEMM_TOL
+
+
+@pytest.mark.parametrize("kernel", ["simt", "tc", "gemm"])
+def test_extreme_activation_magnitudes(oracle, kernel):
+    """Activations from 1e-30 to 1e20 (the GEMM scales x by 2^49 before its
+    bf16 conversion, which stays finite below 2^79 ~ 6e23)."""
+    import torch
+    from vibrant_b200 import synth, vkq
+    from vibrant_b200 import tensor as vt
+    qt, K, N = 12, 512, 2048
+    wq = synth.weights(qt, K, N, seed=3)
+    wd = oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+    M = 16 if kernel == "gemm" else 2
+    x = synth.activations(M, K, seed=4)
+    x[:, ::7] *= np.float32(1e20)
+    x[:, 3::7] *= np.float32(1e-30)
+    w = vt.QuantWeight(qt, K, N, wq)
+    old = vkq.set_gemv_path(vkq.GEMV_TC if kernel == "tc" else vkq.GEMV_SIMT)
+    try:
+        y = vt.matmul(torch.from_numpy(x).cuda(), w, path="gemm" if kernel == "gemm" else "auto").cpu().numpy()
+    finally:
+        vkq.set_gemv_path(old)
+    assert np.isfinite(y).all()
+    tol = helpers.GEMM_TOL if kernel == "gemm" else helpers.GEMV_TOL
+    assert helpers.matmul_error(y, x, wd) <= tol

@@ -390,6 +390,15 @@ int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, in
     return gemv_launch(s, w, w_bytes, x, nullptr, workspace, workspace_bytes, (cudaStream_t)stream, device, &g);
 }
 
+int vkq_set_gemv_path(int path) {
+    t_err[0] = '\0';
+    if (path < 0 || path > 2) {
+        set_error("vkq_set_gemv_path: 0 (automatic), 1 (CUDA cores) or 2 (tensor cores)");
+        return -1;
+    }
+    return set_gemv_path(path);
+}
+
 int vkq_silu_mul(int device, const float *gate, const float *up, float *out, int64_t n, void *stream) {
     int st = enter(device);
     if (st) return st;
@@ -432,8 +441,10 @@ int vkq_device_status(int device, int *code) {
     if (e != cudaSuccess) return check_launch(e, "cudaDeviceSynchronize");
     int g = gemv_read_status();
     const int g2 = gemm_read_status();
+    const int g3 = gemv_tc_read_status();
     if (g == 0) g = g2;
-    if (g < 0 || g2 < 0) {
+    if (g == 0) g = g3;
+    if (g < 0 || g2 < 0 || g3 < 0) {
         set_error("cannot read the device status word");
         return VKQ_ERR_CUDA;
     }

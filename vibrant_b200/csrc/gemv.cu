@@ -969,10 +969,26 @@ static Plan make_plan(const GemvShape &s, int device) {
     return pl;
 }
 
+// Which kernel serves a plain GEMV (vkq_set_gemv_path): 0 chooses, 1 the
+// CUDA-core kernel of this file, 2 the tensor-core kernel (gemv_tc.cu).
+static int g_gemv_path = 0;
+
+int set_gemv_path(int path) {
+    const int old = g_gemv_path;
+    g_gemv_path = path;
+    return old;
+}
+
+static bool use_tensor_cores(const GemvShape &s) {
+    if (g_gemv_path == 1 || !gemv_tc_supported(s)) return false;
+    return true;
+}
+
 size_t gemv_workspace_bytes(const GemvShape &s, int device) {
     Plan pl = make_plan(s, device);
-    if (pl.generic) return 0;
-    return kWorkspaceCounterHead + pl.partial_bytes;
+    const size_t simt = pl.generic ? 0 : kWorkspaceCounterHead + pl.partial_bytes;
+    const size_t tc = gemv_tc_workspace_bytes(s, TcLayout{s.N, 0, 0}, device);
+    return simt > tc ? simt : tc;
 }
 
 template <int QT, int MR, int VPT, bool G>
@@ -1012,6 +1028,8 @@ static cudaError_t dispatch_mr(const GemvParams &gp, const GatherParams &gq, con
 
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
                 size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather) {
+    if (!gather && use_tensor_cores(s))
+        return gemv_tc_launch(s, TcLayout{s.N, 0, 0}, w, w_bytes, x, y, s.N, ws, ws_bytes, stream, device);
     Plan pl = make_plan(s, device);
     cudaError_t e;
     if (pl.generic && gather) {
@@ -1125,8 +1143,9 @@ static void *noalloc_scratch_address(int device) {
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
                         cudaStream_t stream, int device) {
     Plan pl = make_plan(s, device);
-    if (pl.generic) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);
-    const size_t need = kWorkspaceCounterHead + pl.partial_bytes;
+    const bool tc = use_tensor_cores(s);
+    if (pl.generic && !tc) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);
+    const size_t need = gemv_workspace_bytes(s, device);
     if (need > kNoAllocScratchBytes) {
         set_error("this GEMV needs %zu bytes of scratch; the fixed scratch of vkq_gemv_noalloc holds %zu", need,
                   kNoAllocScratchBytes);
@@ -1138,7 +1157,9 @@ int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, cons
         return 5;
     }
     // the tile counters must start at zero; the array keeps the last call's bytes
-    cudaError_t e = cudaMemsetAsync(base, 0, pl.counter_bytes, stream);
+    const size_t tc_counters = (size_t)((s.N + 255) / 256) * 4;
+    const size_t clear = tc && tc_counters > pl.counter_bytes ? tc_counters : pl.counter_bytes;
+    cudaError_t e = cudaMemsetAsync(base, 0, clear, stream);
     if (e != cudaSuccess) {
         set_error("clearing the fixed scratch: %s", cudaGetErrorString(e));
         return 5;

@@ -54,6 +54,21 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
                         cudaStream_t stream, int device);
 int gemv_read_status();
+// Selects the kernel of plain GEMVs: 0 automatic, 1 CUDA cores, 2 tensor cores; returns the previous choice.
+int set_gemv_path(int path);
+
+// Tensor-core GEMV (gemv_tc.cu), fp32-class results, 1 <= M <= 4, N % 32 == 0.
+// Row k of the weight starts at value position k*rs + ((k*ld + n_base) & 255)
+// of its super-block stream: {N, 0, 0} for a plain [K, N] weight, {rb*256, N,
+// lo} for a row-block shard of columns [lo, ...).
+struct TcLayout {
+    int64_t rs, ld, n_base;
+};
+bool gemv_tc_supported(const GemvShape &s);
+size_t gemv_tc_workspace_bytes(const GemvShape &s, const TcLayout &L, int device);
+int gemv_tc_launch(const GemvShape &s, const TcLayout &L, const void *w, int64_t w_bytes, const float *x, float *y,
+                   int64_t y_ld, void *ws, size_t ws_bytes, cudaStream_t stream, int device);
+int gemv_tc_read_status();
 
 // bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
 size_t gemm_workspace_bytes(const GemvShape &s, int device);

@@ -44,6 +44,7 @@ SIGNATURES = {
     "vkq_ipc_free": (_int, [_int, _vp]),
     "vkq_gemv_allgather": (_int, [_int, _int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _int,
                                   _int, _vp, _sz, _vp]),
+    "vkq_set_gemv_path": (_int, [_int]),
     "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "vkq_shard_columns": (_int, [_i64, _int, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
@@ -144,6 +145,17 @@ def gemv_noalloc(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: in
                  device: int = -1, stream=None) -> None:
     """vkq_gemv_noalloc: the GEMV with its scratch in the library's fixed device array."""
     _check(load().vkq_gemv_noalloc(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, _stream_ptr(stream)))
+
+
+GEMV_AUTO, GEMV_SIMT, GEMV_TC = 0, 1, 2
+
+
+def set_gemv_path(path: int) -> int:
+    """vkq_set_gemv_path: 0 automatic, 1 CUDA cores, 2 tensor cores (process-wide); returns the previous."""
+    old = load().vkq_set_gemv_path(path)
+    if old < 0:
+        raise VkqError(ERR_INVALID_ARGUMENT, last_error())
+    return old
 
 
 def silu_mul(gate_ptr: int, up_ptr: int, out_ptr: int, n: int, device: int = -1, stream=None) -> None:
