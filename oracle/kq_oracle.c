@@ -476,3 +476,29 @@ int ko_quantize_q6k(const float *in, int64_t n, uint8_t *out) {
     }
     return 0;
 }
+
+/* MatMulQ5K / MatMulQ6K (internal/tensor/matmul_quant.go:30-191): the
+ * reference's fused route, every output a float32 sum over k in sequential
+ * order of a[i,k] * deq(k*N + j) (the per-element dequantization equals the
+ * block dequantization bit for bit, quant_q4k_test.go:48-91).  Restated for
+ * all three types; M*N outputs of K terms each. */
+int ko_matmul_quant_sequential(int qtype, const float *a, int64_t M, int64_t K, const uint8_t *bq, int64_t N,
+                               float *c) {
+    if (ko_block_bytes(qtype) == 0 || M <= 0 || K <= 0 || N <= 0) return -1;
+    const int64_t nblocks = (K * N + 255) / 256;
+    float *w = (float *)malloc((size_t)(nblocks * 256) * sizeof(float));
+    if (!w) return -2;
+    if (ko_dequantize(qtype, bq, nblocks, w) != 0) {
+        free(w);
+        return -1;
+    }
+    for (int64_t i = 0; i < M; i++) {
+        for (int64_t j = 0; j < N; j++) {
+            float sum = 0.0f;
+            for (int64_t k = 0; k < K; k++) sum += a[i * K + k] * w[k * N + j];
+            c[i * N + j] = sum;
+        }
+    }
+    free(w);
+    return 0;
+}

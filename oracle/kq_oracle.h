@@ -111,6 +111,11 @@ int ko_matmul_dequant_untransposed(int qtype, const float *a, int64_t M, int64_t
                                    const uint8_t *bq, int64_t N, float *c, float *w_scratch,
                                    int nthreads);
 
+/* MatMulQ5K / MatMulQ6K (matmul_quant.go:30-191): c[i,j] = sequential
+ * float32 sum over k of a[i,k] * deq(k*N + j); all three types. */
+int ko_matmul_quant_sequential(int qtype, const float *a, int64_t M, int64_t K, const uint8_t *bq, int64_t N,
+                               float *c);
+
 /* The reference's test quantizers (QuantizeQ4_K quant_q4k.go:215-282,
  * QuantizeQ6_K quant_q6k.go:214-294), serialized as QuantizeQ4_KTensor /
  * QuantizeQ6_KTensor do (matmul_quant_helpers.go:62-145): n floats ->

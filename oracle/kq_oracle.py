@@ -51,6 +51,7 @@ def lib() -> ctypes.CDLL:
         L.ko_matmul_quant.argtypes = [ctypes.c_int, f32p, i64, i64, u8p, i64, f32p, f32p, ctypes.c_int]
         L.ko_matmul_dequant_untransposed.argtypes = [ctypes.c_int, f32p, i64, i64, u8p, i64, f32p, f32p,
                                                      ctypes.c_int]
+        L.ko_matmul_quant_sequential.argtypes = [ctypes.c_int, f32p, i64, i64, u8p, i64, f32p]
         L.ko_quantize_q4k.argtypes = [f32p, i64, u8p]
         L.ko_quantize_q6k.argtypes = [f32p, i64, u8p]
         _lib = L
@@ -164,3 +165,14 @@ def quantize(qtype: int, values: np.ndarray) -> np.ndarray:
     fn = {Q4_K: lib().ko_quantize_q4k, Q6_K: lib().ko_quantize_q6k}[qtype]
     assert fn(_f32p(v), v.size, _u8p(out)) == 0
     return out
+
+
+def matmul_quant_sequential(qtype: int, a: np.ndarray, bq: np.ndarray, K: int, N: int) -> np.ndarray:
+    """MatMulQ5K / MatMulQ6K (the reference's fused route): sequential-k
+    float32 sums of a[i,k] * deq(k*N + j)."""
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1, K)
+    c = np.empty((a.shape[0], N), np.float32)
+    rc = lib().ko_matmul_quant_sequential(qtype, _f32p(a), a.shape[0], K,
+                                          _u8p(np.ascontiguousarray(bq, np.uint8)), N, _f32p(c))
+    assert rc == 0
+    return c

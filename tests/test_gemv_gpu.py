@@ -251,3 +251,18 @@ def test_plans_of_different_tile_counts_share_one_workspace(tvk, oracle):
         torch.cuda.synchronize()
         assert helpers.matmul_error(y.cpu().numpy(), x, wd) <= helpers.GEMV_TOL, (i, M)
     assert vkq.device_status(0) == vkq.OK
+
+
+@pytest.mark.parametrize("qt,K,N,M", [(13, 512, 1024, 1), (14, 512, 1280, 2), (12, 256, 2048, 3)])
+def test_gemv_matches_sequential_fused_route(tvk, oracle, qt, K, N, M):
+    """Against the reference's fused route MatMulQ5K / MatMulQ6K
+    (internal/tensor/matmul_quant.go:30-191): a float32 sum over k in
+    sequential order per output; the difference of summation orders stays
+    within twice the GEMV bound."""
+    from vibrant_b200 import synth
+    wq = synth.weights(qt, K, N, seed=K * 3 + N)
+    x = synth.activations(M, K, seed=M + 100)
+    y = run_gemv(tvk, qt, K, N, wq, x)
+    ref = oracle.matmul_quant_sequential(qt, x, wq, K, N)
+    w = oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
+    assert helpers.matmul_error(y, x, w, y_ref=ref.astype(np.float64)) <= 2 * helpers.GEMV_TOL

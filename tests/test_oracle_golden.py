@@ -384,3 +384,21 @@ def test_quantize_q4k_round_trip_completes(oracle):
     assert b.size == 144 and b[4] == 32 and b[10] == 32
     y = oracle.dequantize(12, b)
     assert np.isfinite(y).all() and (y[32:] == y[32:][0]).all()
+
+
+@pytest.mark.parametrize("qtype", [12, 13, 14])
+def test_sequential_fused_route_matches_fixture_products(oracle, qtype):
+    """MatMulQ5K / MatMulQ6K's sequential-k order (matmul_quant.go:30-191)
+    agrees with the float64 product within the float32 GEMV bound, and with
+    the dispatched route (matmul_quant_test.go:15-110: fused == dequant +
+    MatMul at 1e-4)."""
+    from vibrant_b200 import synth
+    K, N, M = 384, 512, 2
+    wq = synth.weights(qtype, K, N, seed=7)
+    x = synth.activations(M, K, seed=8)
+    w = oracle.dequantize(qtype, wq)[:K * N].reshape(K, N)
+    seq = oracle.matmul_quant_sequential(qtype, x, wq, K, N)
+    disp = oracle.matmul_quant(qtype, x, wq, K, N)
+    import helpers
+    assert helpers.matmul_error(seq, x, w) <= 1e-5
+    assert np.max(np.abs(seq - disp) / (np.abs(disp) + 1e-4)) < 1e-3

@@ -533,10 +533,10 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
                 // CTA order.  No CTA-wide barrier: every wait here stays bounded.
                 const int64_t cf = (t * p.ksteps) / p.per;
                 const int64_t cl = ((t + 1) * p.ksteps - 1) / p.per;
+                __threadfence();  // this lane's partials, before the warp's arrival is counted
                 __syncwarp();
                 int last = 0;
                 if (lane == 0) {
-                    __threadfence();
                     last = atomicAdd(p.counters + t, 1) == (int)(kTNEpi * (cl - cf + 1) - 1);
                 }
                 last = __shfl_sync(0xffffffffu, last, 0);
