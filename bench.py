@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--only", default=None, help="comma list of secondary workloads to run (default: all)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
     ap.add_argument("--probe", default=None, help="QTYPE,K,N,M[,COPIES]: time one workload (profiling)")
+    ap.add_argument("--gemv", default="auto", choices=["auto", "simt", "tc"],
+                    help="GEMV kernel for M <= 8 (vkq_set_gemv_path): automatic, CUDA cores or tensor cores")
     return ap.parse_args()
 
 
@@ -804,6 +806,9 @@ def run_probe(args):
 
 def main():
     args = parse()
+    if args.gemv != "auto" and args.impl == "ours":
+        from vibrant_b200 import vkq
+        vkq.set_gemv_path({"simt": vkq.GEMV_SIMT, "tc": vkq.GEMV_TC}[args.gemv])
     if args.probe:
         run_probe(args)
     elif args.impl == "reference":

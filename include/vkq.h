@@ -249,6 +249,38 @@ VKQ_API int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_b
                                void *const *peer_flags, void *sync, int world, int rank, void *workspace,
                                size_t workspace_bytes, void *stream);
 
+/* ---- GGUF weights to the device, still quantized ----
+ * Replaces the GPU upload route of the reference: ParseGGUF
+ * (internal/gguf/parser.go:15-64) + LoadTensor (internal/gguf/loader.go:11-73)
+ * + Tensor.ToDevice, which expands k-quant tensors to float32 on the host
+ * (internal/tensor/tensor_cuda_api.go:16-53).  vkq_gguf_open memory-maps the
+ * file and parses its header, metadata (skipped) and tensor infos, with
+ * bounds checks; the tensor data section starts at the end of the infos
+ * rounded up to 32 bytes (parser.go:53-60).  Host-only except the loads. */
+typedef struct vkq_gguf vkq_gguf;
+VKQ_API int vkq_gguf_open(const char *path, vkq_gguf **gguf);
+VKQ_API int vkq_gguf_close(vkq_gguf *gguf);
+VKQ_API int64_t vkq_gguf_tensor_count(const vkq_gguf *gguf);
+VKQ_API int vkq_gguf_find(const vkq_gguf *gguf, const char *name, int64_t *index);
+/* Name (valid while the file is open), GGML type, dims in file order (unused
+ * entries 1; vibrant's [K, N] = [dims[0], dims[1]], loader.go:24-27), the
+ * absolute file offset of the data and its byte size (-1 for a type without
+ * a size rule). */
+VKQ_API int vkq_gguf_tensor_info(const vkq_gguf *gguf, int64_t index, const char **name, int *ggml_type,
+                                 int *n_dims, int64_t dims[4], int64_t *data_offset, int64_t *bytes);
+/* Byte size of a tensor: calculateTensorSize (internal/gguf/metadata.go:170-204),
+ * which covers Q4_K where LoadTensor's expectedSize (loader.go:35-48) does not. */
+VKQ_API int vkq_gguf_tensor_bytes(int ggml_type, int n_dims, const int64_t *dims, int64_t *bytes);
+/* Copies a tensor's raw bytes to device memory `dst` (dst_bytes >= its size)
+ * through pinned staging buffers on `stream`; returns when the copy is done. */
+VKQ_API int vkq_gguf_load_tensor(vkq_gguf *gguf, int64_t index, int device, void *dst, int64_t dst_bytes,
+                                 void *stream);
+/* Copies the row-block shard of columns [col_lo, col_hi) of a 2D k-quant
+ * weight (the layout of vkq_shard_weight) to device memory, gathering it from
+ * the mapping: each rank reads and uploads only its shard. */
+VKQ_API int vkq_gguf_load_shard(vkq_gguf *gguf, int64_t index, int64_t col_lo, int64_t col_hi, int device,
+                                void *dst, int64_t dst_bytes, void *stream);
+
 /* Reads and clears the device-side status word of this library on a device
  * (set when a bounded wait inside a kernel gave up, or a peer was out of
  * step).  Synchronizes with the device.  *code receives VKQ_OK,

@@ -223,7 +223,7 @@ def test_error_paths(tvk):
         call(ws=None, wsb=0)
     assert e.value.status == vkq.ERR_WORKSPACE
     with pytest.raises(vkq.VkqError) as e:
-        call(wsb=ws.numel() - 256)
+        call(wsb=1024)  # below either kernel's need
     assert e.value.status == vkq.ERR_WORKSPACE
     with pytest.raises(vkq.VkqError) as e:
         call(x=0)

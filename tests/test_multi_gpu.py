@@ -103,7 +103,7 @@ _PROTOCOL_SCRIPT = textwrap.dedent("""
     Y = [torch.as_tensor(vt._DeviceArray(b, (M, N)), device="cuda") for b in bufs]
     F0 = torch.as_tensor(vt._DeviceArray(flags[0], (2 * world,), "<u4"), device="cuda")
     S0 = torch.as_tensor(vt._DeviceArray(sync, (4,), "<u4"), device="cuda")
-    ws = vt.workspace(vt.workspace_bytes(qt, M, K, sh.width, 0), 0)
+    ws = vt.workspace(max(vt.workspace_bytes(qt, M, K, sh.width, 0), vt.workspace_bytes(qt, M, K, N, 0)), 0)
     def call():
         vkq.gemv_allgather(qt, sh.buf.data_ptr(), sh.nbytes, K, N, sh.lo, sh.hi, x.data_ptr(), M, bufs, flags,
                            sync, world, 0, ws.data_ptr(), ws.numel(), device=0)

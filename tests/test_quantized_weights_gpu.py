@@ -50,14 +50,14 @@ def test_gemv_on_quantized_gaussian_weights(oracle, path, qt, K, N, M):
 
 
 def test_q6k_quants_cluster_at_the_zero_point(oracle):
-    """The premise of the test above: with Gaussian data most Q6_K quants
-    lie near 32 (|q - 32| <= 8 for most values)."""
+    """The premise of the test above: with Gaussian data the Q6_K quants
+    cluster around 32 (d = max|x| / 32, so |q - 32| ~ 11 |x| / sigma)."""
     wq, _ = _weights(oracle, 14, 64, 1024, seed=1)
     b = wq.reshape(-1, 210)
     lo = np.stack([b[:, i // 2] >> (4 * (i % 2)) & 15 for i in range(256)], 1).astype(int)
     hi = np.stack([b[:, 128 + i // 4] >> (2 * (i % 4)) & 3 for i in range(256)], 1).astype(int)
     q = lo | (hi << 4)
-    assert np.mean(np.abs(q - 32) <= 8) > 0.8
+    assert np.mean(np.abs(q - 32) <= 16) > 0.8 and np.mean(np.abs(q - 32) <= 4) > 0.25
 
 
 @pytest.mark.parametrize("qt", [12, 14])

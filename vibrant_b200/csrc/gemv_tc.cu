@@ -624,8 +624,13 @@ static TcPlan tc_plan(const GemvShape &s, const TcLayout &L, int sms) {
     return g;
 }
 
+// K >= 256: the factored form rounds x * s before the minimum is subtracted,
+// so its error is bounded relative to sum_k |x| (|s q| + |mn|) rather than
+// sum_k |x w|; the two differ only where a column's few terms cancel (s q ~
+// mn), which short reductions can hit: those go to the CUDA-core kernel,
+// which forms each weight before the product with x.
 bool gemv_tc_supported(const GemvShape &s) {
-    if (s.M < 1 || s.M > 4 || s.N % 32 != 0 || s.K < 1) return false;
+    if (s.M < 1 || s.M > 4 || s.N % 32 != 0 || s.K < 256) return false;
     const int64_t tiles = (s.N + kTN - 1) / kTN;
     return tiles <= (int64_t)(kWorkspaceCounterHead / 4);
 }

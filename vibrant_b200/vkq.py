@@ -47,6 +47,16 @@ SIGNATURES = {
     "vkq_set_gemv_path": (_int, [_int]),
     "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "vkq_gguf_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "vkq_gguf_close": (_int, [_vp]),
+    "vkq_gguf_tensor_count": (_i64, [_vp]),
+    "vkq_gguf_find": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "vkq_gguf_tensor_info": (_int, [_vp, _i64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_int),
+                                    ctypes.POINTER(_int), ctypes.POINTER(_i64 * 4), ctypes.POINTER(_i64),
+                                    ctypes.POINTER(_i64)]),
+    "vkq_gguf_tensor_bytes": (_int, [_int, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "vkq_gguf_load_tensor": (_int, [_vp, _i64, _int, _vp, _i64, _vp]),
+    "vkq_gguf_load_shard": (_int, [_vp, _i64, _i64, _i64, _int, _vp, _i64, _vp]),
     "vkq_shard_columns": (_int, [_i64, _int, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
     "vkq_shard_bytes": (_int, [_int, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
     "vkq_shard_weight": (_int, [_int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64]),
@@ -259,3 +269,47 @@ def gemv_sharded(comm: int, qtype: int, w_shards: list[int], w_bytes: list[int],
     _check(load().vkq_gemv_sharded(comm, qtype, (_vp * n)(*w_shards), (_i64 * n)(*w_bytes), K, N, (_vp * n)(*x), M,
                                    (_vp * n)(*y), (_vp * n)(*workspaces), (_sz * n)(*ws_bytes),
                                    (_vp * n)(*[_stream_ptr(s) for s in streams])))
+
+
+class GGUF:
+    """vkq_gguf_*: a memory-mapped GGUF file; tensors load to the device raw."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _check(load().vkq_gguf_open(path.encode(), ctypes.byref(h)))
+        self.handle = h.value
+
+    def __len__(self) -> int:
+        return load().vkq_gguf_tensor_count(self.handle)
+
+    def find(self, name: str) -> int:
+        i = _i64()
+        _check(load().vkq_gguf_find(self.handle, name.encode(), ctypes.byref(i)))
+        return i.value
+
+    def info(self, index: int) -> dict:
+        name, t, nd, dims, off, nb = ctypes.c_char_p(), _int(), _int(), (_i64 * 4)(), _i64(), _i64()
+        _check(load().vkq_gguf_tensor_info(self.handle, index, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd),
+                                           ctypes.byref(dims), ctypes.byref(off), ctypes.byref(nb)))
+        return {"name": name.value.decode(), "type": t.value, "dims": list(dims)[:nd.value], "offset": off.value,
+                "bytes": nb.value}
+
+    def load(self, index: int, dst_ptr: int, dst_bytes: int, device: int = 0, stream=None) -> None:
+        _check(load().vkq_gguf_load_tensor(self.handle, index, device, dst_ptr, dst_bytes, _stream_ptr(stream)))
+
+    def load_shard(self, index: int, col_lo: int, col_hi: int, dst_ptr: int, dst_bytes: int, device: int = 0,
+                   stream=None) -> None:
+        _check(load().vkq_gguf_load_shard(self.handle, index, col_lo, col_hi, device, dst_ptr, dst_bytes,
+                                          _stream_ptr(stream)))
+
+    def close(self) -> None:
+        if self.handle:
+            _check(load().vkq_gguf_close(self.handle))
+            self.handle = 0
+
+
+def gguf_tensor_bytes(ggml_type: int, dims: list[int]) -> int:
+    d = (_i64 * len(dims))(*dims)
+    out = _i64()
+    _check(load().vkq_gguf_tensor_bytes(ggml_type, len(dims), d, ctypes.byref(out)))
+    return out.value
