@@ -133,6 +133,7 @@ _PROTOCOL_SCRIPT = textwrap.dedent("""
     assert vkq.device_status(0) == vkq.OK
     ref = torch.empty(M, N, device="cuda")
     w = vt.QuantWeight(qt, K, N, wq)
+    vkq.set_gemv_path(vkq.GEMV_SIMT)   # the CUDA-core kernel: the same plan as the all-gather's
     vt.matmul(x, w, out=ref)
     torch.cuda.synchronize()
     assert torch.equal(ref, Y[0]), "reset channel gives a different result"

@@ -979,9 +979,13 @@ int set_gemv_path(int path) {
     return old;
 }
 
-static bool use_tensor_cores(const GemvShape &s) {
-    if (g_gemv_path == 1 || !gemv_tc_supported(s)) return false;
-    return true;
+// The tensor-core kernel serves weights whose rows start on super-block
+// boundaries (N % 256 == 0: every 256-column tile is one block per row);
+// rows that straddle blocks (the vocabulary projection, N % 256 == 128) are
+// the CUDA-core kernel's, which streams whole row chunks.
+static bool use_tensor_cores(const GemvShape &s, int device) {
+    if (g_gemv_path == 1 || s.N % 256 != 0) return false;
+    return gemv_tc_fits(s, TcLayout{s.N, 0, 0}, device);
 }
 
 size_t gemv_workspace_bytes(const GemvShape &s, int device) {
@@ -1028,7 +1032,7 @@ static cudaError_t dispatch_mr(const GemvParams &gp, const GatherParams &gq, con
 
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
                 size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather) {
-    if (!gather && use_tensor_cores(s))
+    if (!gather && use_tensor_cores(s, device))
         return gemv_tc_launch(s, TcLayout{s.N, 0, 0}, w, w_bytes, x, y, s.N, ws, ws_bytes, stream, device);
     Plan pl = make_plan(s, device);
     cudaError_t e;
@@ -1143,7 +1147,7 @@ static void *noalloc_scratch_address(int device) {
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
                         cudaStream_t stream, int device) {
     Plan pl = make_plan(s, device);
-    const bool tc = use_tensor_cores(s);
+    const bool tc = use_tensor_cores(s, device);
     if (pl.generic && !tc) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);
     const size_t need = gemv_workspace_bytes(s, device);
     if (need > kNoAllocScratchBytes) {
@@ -1157,7 +1161,7 @@ int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, cons
         return 5;
     }
     // the tile counters must start at zero; the array keeps the last call's bytes
-    const size_t tc_counters = (size_t)((s.N + 255) / 256) * 4;
+    const size_t tc_counters = (size_t)((s.N + 255) / 256) * 16;
     const size_t clear = tc && tc_counters > pl.counter_bytes ? tc_counters : pl.counter_bytes;
     cudaError_t e = cudaMemsetAsync(base, 0, clear, stream);
     if (e != cudaSuccess) {

@@ -60,6 +60,7 @@ constexpr int kTAStage = 2 * kTHalf;    // 32 KB
 constexpr int kTWRaw = 0, kTWMma = 1, kTWDec = 2, kTNDec = 16, kTWEpi = 18, kTNEpi = 4;
 constexpr int kTThreads = (kTWEpi + kTNEpi) * 32;  // 704
 constexpr int kTMaxStages = 8;
+constexpr int kNGrp = 4;                // decode groups: stages j = g (mod 4)
 constexpr uint64_t kTWaitNs = 2000000000ull;  // bounded waits: 2 s
 constexpr uint64_t kTDrainNs = 20000000ull;   // copies in flight at teardown: 20 ms
 }  // namespace
@@ -80,7 +81,7 @@ struct TcParams {
     int nc;                  // MMA N: B columns per half
     int nbuf, tmem_cols, acc_stride;
     float *partials;         // [grid][2][MR][256]
-    int *counters;           // [tiles], zero between calls
+    int *counters;           // [tiles][4] (one per row quarter), zero between calls
 };
 
 __device__ __forceinline__ void tc_set_status(int c) { atomicExch(&g_tc_status, c); }
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
                                                                const TcParams p) {
     constexpr int B = QT_<QT>::BYTES;
     constexpr int G = QT == kQ6K ? 8 : 4;   // scale groups per 128-row half
-    constexpr int GU = QT == kQ6K ? 2 : 1;  // groups per 32-value unit
+    constexpr int GH = G;                   // scale groups per 128-value row piece
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32addr(smem_raw);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
     const uint32_t b_ring = a_ring + (uint32_t)p.sa * kTAStage;
     const uint32_t r_ring = b_ring + (uint32_t)p.sa * b_stage;
     const uint32_t corr_s = (r_ring + (uint32_t)p.sr * raw_stage + 15u) & ~15u;
-    constexpr int kCorrPerBuf = kTNDec * 4 * MR * GU;  // floats
+    constexpr int kCorrPerBuf = kNGrp * 4 * GH * MR;  // floats: [group][warp][scale group][m]
     const uint32_t bars = (corr_s + 2u * kCorrPerBuf * 4u + 7u) & ~7u;
     auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
     const int RF = 0, RE = kTMaxStages, AF = 2 * kTMaxStages, AE = 3 * kTMaxStages, CF = 4 * kTMaxStages,
@@ -141,10 +142,10 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.sr; s++) {
             mbar_init(bar(RF + s), p.raw_tma ? 1 : 32);
-            mbar_init(bar(RE + s), kTNDec);
+            mbar_init(bar(RE + s), 4);  // one group's warps
         }
         for (int s = 0; s < p.sa; s++) {
-            mbar_init(bar(AF + s), kTNDec);
+            mbar_init(bar(AF + s), 4);
             mbar_init(bar(AE + s), 1);
         }
         for (int s = 0; s < 2; s++) {
@@ -289,164 +290,217 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
             mbar_wait_bounded(bar(DR), 0, kTDrainNs);
         }
     } else if (warp < kTWEpi) {
-        // ------------- decode: raw unit -> A tile, B entries, corrections -------------
-        const int wd = warp - kTWDec;
-        const int dt = threadIdx.x - kTWDec * 32;  // 0..511
-        const int kl = 8 * (dt >> 6) + (dt & 7);  // k row within the stage
-        const int c8 = (dt >> 3) & 7;             // 32-value unit within the tile
-        const int h = c8 >> 2, q = c8 & 3;        // MMA half, unit within the half
-        uint32_t a_off[4];
-#pragma unroll
-        for (int c4 = 0; c4 < 4; c4++) {
-            const int nl = 32 * q + 8 * c4;
-            const int hh = nl >> 6, c = (nl & 63) >> 3, g8 = kl >> 3, kin = kl & 7;
-            a_off[c4] = (uint32_t)(h * kTHalf + (g8 * 2 + hh) * 1024 + kin * 128 + ((c ^ kin) << 4));
-        }
-        // byte offset of B entry (column c, this thread's k row) within a stage
+        // ------------- decode: raw half-block -> A tile rows, B entries, corrections -------------
+        // Four groups of four warps; group g takes the CTA's stages j = g, g+4, ...
+        // (so four stages are decoded at once and their latencies overlap).  A
+        // thread takes one k row of one MMA half: 128 values of one block half.
+        const int dw = warp - kTWDec;
+        const int grp = dw >> 2, wq = dw & 3;
+        const int h = wq >> 1;                 // MMA half of this thread's row piece
+        const int kl = 32 * (wq & 1) + lane;   // k row within the stage
+        const uint32_t a_base = (uint32_t)(h * kTHalf + (kl >> 3) * 2048 + (kl & 7) * 128);
+        const uint32_t kb2 = 2u * (uint32_t)kl;
         auto b_off = [&](int c) -> uint32_t {
-            const int kb = 2 * kl;
-            return (uint32_t)h * b_half + (uint32_t)((c >> 3) * 1024 + (c & 7) * 128 + ((((kb >> 4) ^ (c & 7)) << 4) |
-                                                                                          (kb & 15)));
+            return (uint32_t)h * b_half +
+                   (uint32_t)((c >> 3) * 1024 + (c & 7) * 128 + ((((kb2 >> 4) ^ (uint32_t)(c & 7)) << 4) | (kb2 & 15u)));
         };
-        RingPos pr, pa;
-        bool waited_x = false;
+        const uint32_t slot_row = r_ring + (uint32_t)(kl * p.raw_slot);
+        // ring positions of stage j = grp + 4i (sr, sa >= 4: at most one wrap per step)
+        uint32_t ridx = (uint32_t)grp, rph = 0, aidx = (uint32_t)grp, aph = 0;
+        int64_t j = grp;  // this group's next stage, counted from f0
+        pdl_wait();       // x may come from the preceding kernel
         uint32_t si = 0;
         for (int64_t fa = f0; fa < f1 && !*abort_flag; si++) {
             const int64_t t = fa / p.ksteps;
             const int64_t fb = (t + 1) * p.ksteps < f1 ? (t + 1) * p.ksteps : f1;
             const int64_t n0 = t * kTN;
-            const bool n_ok = n0 + 32 * c8 < p.N;
-            float corr[MR][GU];
+            const bool n_ok = n0 + 128 * h < p.N;
+            const uint32_t x0b = (uint32_t)(((n0 >> 8) * B) & ~int64_t(15));  // TMA box start within a row
+            float corr[MR][GH];
 #pragma unroll
             for (int m = 0; m < MR; m++)
 #pragma unroll
-                for (int gi = 0; gi < GU; gi++) corr[m][gi] = 0.f;
+                for (int g = 0; g < GH; g++) corr[m][g] = 0.f;
+            const int Ki = (int)p.K;
             bool ok = true;
-            for (int64_t f = fa; f < fb; f++, pr.next((uint32_t)p.sr), pa.next((uint32_t)p.sa)) {
-                const int ks = (int)(f - t * p.ksteps);
-                const int sr = (int)pr.idx, sa = (int)pa.idx;
-                const int64_t k = (int64_t)ks * kTK + kl;
-                const bool valid = n_ok && k < p.K;
-                if (!wait(bar(RF + sr), pr.phase, true)) {
+            // x of the group's next stage is loaded one group step ahead
+            float xn[MR];
+            auto load_x = [&](int64_t jj, float (&dst)[MR]) {
+                const int kx = (int)(f0 + jj - t * p.ksteps) * kTK + kl;
+                const bool in = f0 + jj < fb && n_ok && kx < Ki;
+#pragma unroll
+                for (int m = 0; m < MR; m++) dst[m] = (in && m < p.M) ? __ldg(p.x + (int64_t)m * p.K + kx) : 0.f;
+            };
+            load_x(j, xn);
+            for (; f0 + j < fb; j += kNGrp) {
+                const int ks = (int)(f0 + j - t * p.ksteps);
+                const int k = ks * kTK + kl;
+                const bool valid = n_ok && k < Ki;
+                float xv[MR];
+#pragma unroll
+                for (int m = 0; m < MR; m++) xv[m] = xn[m];
+                load_x(j + kNGrp, xn);
+                if (!wait(bar(RF + (int)ridx), rph, true)) {
                     ok = false;
                     break;
                 }
-                uint32_t blk = 0, within = 0;
+                // the block half under this row piece, in the raw stage
+                uint32_t blk = 0, hb = 0;
                 if (valid) {
-                    const int64_t V = row_v(k);
-                    const int64_t v = V + n0 + 32 * c8;
-                    const int64_t lo = p.raw_tma ? k * p.pitch + (((n0 >> 8) * B) & ~int64_t(15))
-                                                 : (((V + n0) >> 8) * B) & ~int64_t(15);
-                    blk = r_ring + (uint32_t)sr * raw_stage + (uint32_t)(kl * p.raw_slot) +
-                          (uint32_t)((v >> 8) * B - lo);
-                    within = (uint32_t)(v & 255);
+                    if (p.raw_tma) {
+                        const uint32_t u0 = (((uint32_t)k * (uint32_t)p.ld + (uint32_t)p.n_base) & 255u) +
+                                            (uint32_t)n0 + 128u * (uint32_t)h;
+                        blk = slot_row + ridx * raw_stage + (u0 >> 8) * (uint32_t)B - x0b;
+                        hb = (u0 >> 7) & 1u;
+                    } else {
+                        const int64_t V = row_v(k);
+                        const int64_t v = V + n0 + 128 * h;
+                        const int64_t lo = (((V + n0) >> 8) * B) & ~int64_t(15);
+                        blk = slot_row + ridx * raw_stage + (uint32_t)((v >> 8) * B - lo);
+                        hb = (uint32_t)((v >> 7) & 1);
+                    }
                 }
-                RawUnit u;
+                uint32_t qw[16], aux[8];  // quants (16 words); Q4_K/Q5_K header + Q5_K high bits, or Q6_K qh
+                uint32_t sw[2] = {0u, 0u};  // Q6_K: the 8 int8 group scales
+                float d = 0.f, dmin = 0.f;
+                if (valid) {
+                    if constexpr (QT == kQ4K || QT == kQ5K) {
+                        const uint4 hd = lds128(blk);
+                        aux[0] = hd.x; aux[1] = hd.y; aux[2] = hd.z; aux[3] = hd.w;
+                        const uint32_t qsa = blk + (QT == kQ4K ? 16u : 48u) + 64u * hb;
 #pragma unroll
-                for (int i = 0; i < 10; i++) u.v[i] = 0u;
-                u.shf = 0;
-                load_unit<QT>(blk, within, valid, u);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(RE + sr));
-                if (!waited_x) {
-                    pdl_wait();  // x may come from the preceding kernel
-                    waited_x = true;
-                }
-                float xv[MR];
-#pragma unroll
-                for (int m = 0; m < MR; m++) xv[m] = (valid && m < p.M) ? __ldg(p.x + (int64_t)m * p.K + k) : 0.f;
-                // A: 16 words of bf16 pairs (128 + q): pair j of chunk c4 = values (8c4 + j, 8c4 + j + 4)
-                uint32_t aw[16];
-                float sc[GU], mnv = 0.f;
-                if constexpr (QT == kQ4K || QT == kQ5K) {
-                    const float d = hw_f16_to_f32(u.v[0] & 0xFFFFu), dmin = hw_f16_to_f32(u.v[0] >> 16);
-                    const int sb = (int)(within >> 5);
-                    const uint32_t sc24 = sb < 4 ? u.v[1] : __funnelshift_r(u.v[1], u.v[2], 24);
-                    const uint32_t m24 = sb < 4 ? __funnelshift_r(u.v[2], u.v[3], 16) : (u.v[3] >> 8);
-                    const uint32_t sh = 6u * (sb & 3);
-                    sc[0] = d * (float)((sc24 >> sh) & 63u);
-                    mnv = dmin * (float)((m24 >> sh) & 63u);
-#pragma unroll
-                    for (int c4 = 0; c4 < 4; c4++) {
-                        const uint32_t W = u.v[4 + c4];
-                        uint32_t Y = 0;
-                        if constexpr (QT == kQ5K) Y = ((u.v[8] >> (8 * c4)) & 0xFFu) * 0x10010u;
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            uint32_t P = ((W >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
-                            if constexpr (QT == kQ5K) P |= (Y >> j) & 0x00100010u;
-                            aw[4 * c4 + j] = P;
+                        for (int i = 0; i < 4; i++) {
+                            const uint4 v4 = lds128(qsa + 16u * i);
+                            qw[4 * i] = v4.x; qw[4 * i + 1] = v4.y; qw[4 * i + 2] = v4.z; qw[4 * i + 3] = v4.w;
                         }
+                        if constexpr (QT == kQ5K) {
+                            const uint4 v4 = lds128(blk + 16u + 16u * hb);
+                            aux[4] = v4.x; aux[5] = v4.y; aux[6] = v4.z; aux[7] = v4.w;
+                        }
+                    } else {
+                        // 2-byte aligned block: aligned words and one funnel shift
+                        const uint32_t shf = (blk & 3u) * 8u, b4 = blk & ~3u;
+                        uint32_t prev = lds32(b4 + 64u * hb);
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            const uint32_t nx = lds32(b4 + 64u * hb + 4u * (i + 1));
+                            qw[i] = __funnelshift_r(prev, nx, shf);
+                            prev = nx;
+                        }
+                        prev = lds32(b4 + 128u + 32u * hb);
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const uint32_t nx = lds32(b4 + 128u + 32u * hb + 4u * (i + 1));
+                            aux[i] = __funnelshift_r(prev, nx, shf);
+                            prev = nx;
+                        }
+                        const uint32_t s0 = lds32(b4 + 192u + 8u * hb), s1 = lds32(b4 + 196u + 8u * hb),
+                                       s2 = lds32(b4 + 200u + 8u * hb);
+                        sw[0] = __funnelshift_r(s0, s1, shf);
+                        sw[1] = __funnelshift_r(s1, s2, shf);
+                        d = hw_f16_to_f32(lds16(blk + 208u));
                     }
                 } else {
-                    uint32_t ql[4], qh[2];
 #pragma unroll
-                    for (int i = 0; i < 4; i++) ql[i] = __funnelshift_r(u.v[i], u.v[i + 1], u.shf);
+                    for (int i = 0; i < 16; i++) qw[i] = 0u;
 #pragma unroll
-                    for (int i = 0; i < 2; i++) qh[i] = __funnelshift_r(u.v[5 + i], u.v[6 + i], u.shf);
-                    const float d = hw_f16_to_f32(u.v[8] >> 16);
-                    sc[0] = d * (float)(int)(int8_t)(u.v[8] & 0xFFu);
-                    sc[GU - 1] = d * (float)(int)(int8_t)((u.v[8] >> 8) & 0xFFu);
+                    for (int i = 0; i < 8; i++) aux[i] = 0u;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(RE + (int)ridx));
+                // per-group scales of this block half
+                float sg[GH], mg[GH];
+                if constexpr (QT == kQ4K || QT == kQ5K) {
+                    d = hw_f16_to_f32(aux[0] & 0xFFFFu);
+                    dmin = hw_f16_to_f32(aux[0] >> 16);
+                    const uint32_t sc24 = hb ? __funnelshift_r(aux[1], aux[2], 24) : aux[1];
+                    const uint32_t m24 = hb ? (aux[3] >> 8) : __funnelshift_r(aux[2], aux[3], 16);
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; c4++) {
-                        const uint32_t L = ql[c4];
-                        // the chunk's 16 high-bit pairs: value i at bits 2i of QH16; spread
-                        // bytes 0 and 1 of QH16 to bytes 0 and 2, then shift to bit 4
-                        const uint32_t b0 = 2u * (uint32_t)(c4 & 1);
-                        const uint32_t Z = prmt(qh[c4 >> 1], 0u, b0 | (4u << 4) | ((b0 + 1u) << 8) | (4u << 12)) << 4;
+                    for (int g = 0; g < GH; g++) {
+                        sg[g] = d * (float)((sc24 >> (6 * g)) & 63u);
+                        mg[g] = dmin * (float)((m24 >> (6 * g)) & 63u);
+                    }
+                } else {
 #pragma unroll
-                        for (int j = 0; j < 4; j++)
-                            aw[4 * c4 + j] = ((L >> (4 * j)) & 0x000F000Fu) | 0x43004300u | ((Z >> (2 * j)) & 0x00300030u);
+                    for (int g = 0; g < GH; g++) {
+                        sg[g] = d * (float)(int)(int8_t)((sw[g >> 2] >> (8 * (g & 3))) & 0xFFu);
+                        mg[g] = 0.f;
                     }
                 }
-                // B entries and corrections
-                uint32_t bb[MR][GU][3];
+                if (j >= p.sa && !wait(bar(AE + (int)aidx), aph ^ 1u, true)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t a_s = a_ring + aidx * (uint32_t)kTAStage;
+                // A: chunk cc holds values 8cc..8cc+7 of the half as bf16 pairs (v_j, v_j+4)
+#pragma unroll
+                for (int cc = 0; cc < 16; cc++) {
+                    const uint32_t W = qw[cc];
+                    uint32_t P[4];
+                    if constexpr (QT == kQ6K) {
+                        const uint32_t b0 = 2u * (uint32_t)(cc & 1);
+                        const uint32_t Z = prmt(aux[cc >> 1], 0u, b0 | (4u << 4) | ((b0 + 1u) << 8) | (4u << 12)) << 4;
+#pragma unroll
+                        for (int jq = 0; jq < 4; jq++)
+                            P[jq] = ((W >> (4 * jq)) & 0x000F000Fu) | 0x43004300u | ((Z >> (2 * jq)) & 0x00300030u);
+                    } else {
+                        uint32_t Y = 0;
+                        if constexpr (QT == kQ5K) Y = ((aux[4 + (cc >> 2)] >> (8 * (cc & 3))) & 0xFFu) * 0x10010u;
+#pragma unroll
+                        for (int jq = 0; jq < 4; jq++) {
+                            P[jq] = ((W >> (4 * jq)) & 0x000F000Fu) | 0x43004300u;
+                            if constexpr (QT == kQ5K) P[jq] |= (Y >> jq) & 0x00100010u;
+                        }
+                    }
+                    const uint32_t ao = a_base + (uint32_t)((cc >> 3) * 1024) + ((((uint32_t)cc & 7u) ^ ((uint32_t)kl & 7u)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a_s + ao), "r"(P[0]), "r"(P[1]),
+                                 "r"(P[2]), "r"(P[3])
+                                 : "memory");
+                }
+                // B: per group and m, the product x * s split into three bf16 parts
+                const uint32_t b_s = b_ring + aidx * b_stage;
 #pragma unroll
                 for (int m = 0; m < MR; m++) {
 #pragma unroll
-                    for (int gi = 0; gi < GU; gi++) {
+                    for (int g = 0; g < GH; g++) {
+                        uint32_t b1, b2, b3;
                         float ahat;
-                        split3(xv[m] * sc[gi], bb[m][gi][0], bb[m][gi][1], bb[m][gi][2], ahat);
-                        if constexpr (QT == kQ6K) corr[m][gi] = fmaf(160.f, ahat, corr[m][gi]);
-                        else corr[m][gi] = fmaf(128.f, ahat, fmaf(xv[m], mnv, corr[m][gi]));
+                        split3(xv[m] * sg[g], b1, b2, b3, ahat);
+                        if constexpr (QT == kQ6K) corr[m][g] = fmaf(160.f, ahat, corr[m][g]);
+                        else corr[m][g] = fmaf(128.f, ahat, fmaf(xv[m], mg[g], corr[m][g]));
+                        const int c = (m * G + g) * 3;
+                        sts16(b_s + b_off(c), b1);
+                        sts16(b_s + b_off(c + 1), b2);
+                        sts16(b_s + b_off(c + 2), b3);
                     }
                 }
-                if (pa.uses >= (uint32_t)p.sa && !wait(bar(AE + sa), pa.phase ^ 1u, true)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t a_s = a_ring + (uint32_t)(sa * kTAStage);
-#pragma unroll
-                for (int c4 = 0; c4 < 4; c4++)
-                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a_s + a_off[c4]), "r"(aw[4 * c4]),
-                                 "r"(aw[4 * c4 + 1]), "r"(aw[4 * c4 + 2]), "r"(aw[4 * c4 + 3])
-                                 : "memory");
-                const uint32_t b_s = b_ring + (uint32_t)sa * b_stage;
-#pragma unroll
-                for (int m = 0; m < MR; m++)
-#pragma unroll
-                    for (int gi = 0; gi < GU; gi++)
-#pragma unroll
-                        for (int tp = 0; tp < 3; tp++)
-                            sts16(b_s + b_off((m * G + GU * q + gi) * 3 + tp), bb[m][gi][tp]);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(bar(AF + sa));
+                if (lane == 0) mbar_arrive(bar(AF + (int)aidx));
+                ridx += kNGrp;
+                if (ridx >= (uint32_t)p.sr) {
+                    ridx -= (uint32_t)p.sr;
+                    rph ^= 1u;
+                }
+                aidx += kNGrp;
+                if (aidx >= (uint32_t)p.sa) {
+                    aidx -= (uint32_t)p.sa;
+                    aph ^= 1u;
+                }
             }
             if (!ok) break;
-            // the segment's corrections: the 8 lanes of a unit column (k rows) in
-            // a fixed shuffle order, then one slot per warp and unit
+            // the segment's corrections of this warp: all 32 lanes (k rows) in a
+            // fixed butterfly order, one slot per (group, warp)
             const uint32_t kb = si & 1u;
             if (si >= 2 && !wait(bar(KE + kb), ((si >> 1) - 1) & 1u)) break;
 #pragma unroll
             for (int m = 0; m < MR; m++) {
 #pragma unroll
-                for (int gi = 0; gi < GU; gi++) {
-                    float v = corr[m][gi];
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    v += __shfl_xor_sync(0xffffffffu, v, 4);
-                    if ((lane & 7) == 0) corr_f[kb * kCorrPerBuf + ((wd * 4 + q) * MR + m) * GU + gi] = v;
+                for (int g = 0; g < GH; g++) {
+                    float v = corr[m][g];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0) corr_f[kb * kCorrPerBuf + ((grp * 4 + wq) * GH + g) * MR + m] = v;
                 }
             }
             __syncwarp();
@@ -473,7 +527,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
 #pragma unroll
                 for (int hh = 0; hh < 2; hh++) {
                     const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + tb * (uint32_t)p.acc_stride +
-                                           (uint32_t)(hh * p.nc + (m * G + GU * q) * 3);
+                                           (uint32_t)(hh * p.nc + (m * G + (QT == kQ6K ? 2 : 1) * q) * 3);
                     uint32_t r[8];
                     if constexpr (QT == kQ6K) {
                         asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -498,15 +552,17 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
             const uint32_t kb = si & 1u;
             if (!wait(bar(KF + kb), (si >> 1) & 1u)) break;
             float cs[MR][2];
-            const int gi = (QT == kQ6K && lane >= 16) ? 1 : 0;
+            const int gq = QT == kQ6K ? 2 * q + (lane >= 16 ? 1 : 0) : q;  // scale group of this lane's row
 #pragma unroll
             for (int m = 0; m < MR; m++) {
 #pragma unroll
                 for (int hh = 0; hh < 2; hh++) {
                     float c = 0.f;
 #pragma unroll
-                    for (int i = 0; i < kTNDec / 2; i++)
-                        c += corr_f[kb * kCorrPerBuf + (((2 * i + hh) * 4 + q) * MR + m) * GU + gi];
+                    for (int gr = 0; gr < kNGrp; gr++)
+#pragma unroll
+                        for (int w2 = 0; w2 < 2; w2++)
+                            c += corr_f[kb * kCorrPerBuf + ((gr * 4 + 2 * hh + w2) * GH + gq) * MR + m];
                     cs[m][hh] = c;
                 }
             }
@@ -528,33 +584,54 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
                 }
             }
             if (!whole) {
-                // each epilogue warp counts itself in after its partial stores;
-                // the last of the tile's warps (4 per CTA) adds the partials in
-                // CTA order.  No CTA-wide barrier: every wait here stays bounded.
+                // split tile: each epilogue warp counts itself in for its row
+                // quarter (after its partial stores); the last CTA to arrive
+                // for a quarter adds that quarter's partials in CTA order.  No
+                // CTA-wide barrier: every wait here stays bounded.
                 const int64_t cf = (t * p.ksteps) / p.per;
                 const int64_t cl = ((t + 1) * p.ksteps - 1) / p.per;
                 __threadfence();  // this lane's partials, before the warp's arrival is counted
                 __syncwarp();
                 int last = 0;
-                if (lane == 0) {
-                    last = atomicAdd(p.counters + t, 1) == (int)(kTNEpi * (cl - cf + 1) - 1);
-                }
+                if (lane == 0) last = atomicAdd(p.counters + 4 * t + q, 1) == (int)(cl - cf);
                 last = __shfl_sync(0xffffffffu, last, 0);
                 if (last) {
                     __threadfence();
                     const bool cf_slot1 = cf * p.per < t * p.ksteps;
-                    for (int idx = lane; idx < MR * kTN; idx += 32) {
-                        const int m = idx / kTN, c = idx % kTN;
-                        if (m >= p.M || n0 + c >= p.N) continue;
-                        float acc = 0.f;
-                        for (int64_t cta = cf; cta <= cl; cta++) {
+                    float acc[MR][2];
+#pragma unroll
+                    for (int m = 0; m < MR; m++) acc[m][0] = acc[m][1] = 0.f;
+                    constexpr int kBatch = MR >= 4 ? 2 : 4;  // partial rows in flight
+                    for (int64_t c0 = cf; c0 <= cl; c0 += kBatch) {
+                        float v[kBatch][MR][2];
+#pragma unroll
+                        for (int u = 0; u < kBatch; u++) {
+                            const int64_t cta = c0 + u;
                             const int sl = (cta == cf && cf_slot1) ? 1 : 0;
-                            acc += __ldcg(p.partials + ((cta * 2 + sl) * MR + m) * kTN + c);
+                            const float *src = p.partials + (cta * 2 + sl) * MR * kTN + nl;
+#pragma unroll
+                            for (int m = 0; m < MR; m++)
+#pragma unroll
+                                for (int hh = 0; hh < 2; hh++)
+                                    v[u][m][hh] = cta <= cl ? __ldcg(src + m * kTN + 128 * hh) : 0.f;
                         }
-                        p.y[(int64_t)m * p.y_ld + n0 + c] = acc;
+#pragma unroll
+                        for (int u = 0; u < kBatch; u++)
+#pragma unroll
+                            for (int m = 0; m < MR; m++)
+#pragma unroll
+                                for (int hh = 0; hh < 2; hh++)
+                                    if (c0 + u <= cl) acc[m][hh] += v[u][m][hh];
                     }
+#pragma unroll
+                    for (int m = 0; m < MR; m++)
+#pragma unroll
+                        for (int hh = 0; hh < 2; hh++) {
+                            const int64_t n = n0 + 128 * hh + nl;
+                            if (m < p.M && n < p.N) p.y[(int64_t)m * p.y_ld + n] = acc[m][hh];
+                        }
                     __syncwarp();
-                    if (lane == 0) atomicExch(p.counters + t, 0);
+                    if (lane == 0) atomicExch(p.counters + 4 * t + q, 0);
                 }
             }
             fa = fb;
@@ -570,6 +647,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemv_tc_kernel(const __grid_cons
 
 // ------------------------------- host side -------------------------------
 struct TcPlan {
+    bool fits;
     int tiles, ksteps, per, grid;
     int sr, sa, raw_slot, raw_tma, nc, nbuf, tmem_cols;
     int64_t pitch;
@@ -582,7 +660,7 @@ static TcPlan tc_plan(const GemvShape &s, const TcLayout &L, int sms) {
     TcPlan g{};
     const int B = s.qtype == kQ4K ? 144 : s.qtype == kQ5K ? 176 : 210;
     const int MR = tc_mr(s.M);
-    const int G = s.qtype == kQ6K ? 8 : 4, GU = s.qtype == kQ6K ? 2 : 1;
+    const int G = s.qtype == kQ6K ? 8 : 4;
     g.tiles = (int)((s.N + kTN - 1) / kTN);
     g.ksteps = (int)((s.K + kTK - 1) / kTK);
     const int64_t total = (int64_t)g.tiles * g.ksteps;
@@ -604,21 +682,14 @@ static TcPlan tc_plan(const GemvShape &s, const TcLayout &L, int sms) {
         g.raw_slot = (2 * B + 15 + 15) & ~15;
     }
     const size_t a_st = kTAStage + 256 * (size_t)g.nc, r_st = (size_t)kTK * g.raw_slot;
-    const size_t fixed = 1024 + 2 * (size_t)kTNDec * 4 * MR * GU * 4 + 16 + 8 * (4 * kTMaxStages + 12) + 16;
+    const size_t fixed = 1024 + 2 * (size_t)kNGrp * 4 * G * MR * 4 + 16 + 8 * (4 * kTMaxStages + 12) + 16;
     const size_t budget = 227 * 1024 - fixed;
-    g.sa = 2;
-    g.sr = 2;
-    for (bool grown = true; grown;) {
-        grown = false;
-        if (g.sr < kTMaxStages && (g.sa + 0) * a_st + (g.sr + 1) * r_st <= budget) {
-            g.sr++;
-            grown = true;
-        }
-        if (g.sa < 4 && (g.sa + 1) * a_st + g.sr * r_st <= budget) {
-            g.sa++;
-            grown = true;
-        }
-    }
+    // four decode groups work on four stages at once: four A stages, and at
+    // least four raw stages, grown while they fit
+    g.sa = 4;
+    g.sr = 4;
+    while (g.sr < kTMaxStages && g.sa * a_st + (g.sr + 1) * r_st <= budget) g.sr++;
+    g.fits = g.sa * a_st + g.sr * r_st <= budget;
     g.smem = fixed + g.sa * a_st + g.sr * r_st;
     g.part_bytes = ((size_t)g.grid * 2 * MR * kTN * 4 + 255) & ~size_t(255);
     return g;
@@ -631,8 +702,13 @@ static TcPlan tc_plan(const GemvShape &s, const TcLayout &L, int sms) {
 // which forms each weight before the product with x.
 bool gemv_tc_supported(const GemvShape &s) {
     if (s.M < 1 || s.M > 4 || s.N % 32 != 0 || s.K < 256) return false;
+    if (s.qtype == kQ6K && s.M > 2) return false;  // Q6_K's 8 groups x 3 parts x M columns: shared memory
     const int64_t tiles = (s.N + kTN - 1) / kTN;
-    return tiles <= (int64_t)(kWorkspaceCounterHead / 4);
+    return 4 * tiles <= (int64_t)(kWorkspaceCounterHead / 4);  // a counter per tile quarter
+}
+
+bool gemv_tc_fits(const GemvShape &s, const TcLayout &L, int device) {
+    return gemv_tc_supported(s) && tc_plan(s, L, device_sm_count(device)).fits;
 }
 
 size_t gemv_tc_workspace_bytes(const GemvShape &s, const TcLayout &L, int device) {
@@ -663,7 +739,9 @@ static cudaError_t dispatch_tc(int mr, const CUtensorMap &tm, const TcParams &tp
     switch (mr) {
     case 1: return launch_tc<QT, 1>(tm, tp, g, st);
     case 2: return launch_tc<QT, 2>(tm, tp, g, st);
-    default: return launch_tc<QT, 4>(tm, tp, g, st);
+    default:
+        if constexpr (QT == kQ6K) return cudaErrorInvalidValue;  // Q6_K serves M <= 2 (gemv_tc_supported)
+        else return launch_tc<QT, 4>(tm, tp, g, st);
     }
 }
 
@@ -675,6 +753,10 @@ int gemv_tc_launch(const GemvShape &s, const TcLayout &L, const void *w, int64_t
     }
     const int sms = device_sm_count(device);
     const TcPlan g = tc_plan(s, L, sms);
+    if (!g.fits) {
+        set_error("the tensor-core GEMV's stages do not fit in shared memory for this shape");
+        return 2;
+    }
     const size_t need = kWorkspaceCounterHead + g.part_bytes;
     if (ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255u)) {
         set_error("the tensor-core GEMV needs a 256-byte aligned workspace of %zu bytes (got %zu)", need, ws_bytes);

@@ -65,6 +65,8 @@ struct TcLayout {
     int64_t rs, ld, n_base;
 };
 bool gemv_tc_supported(const GemvShape &s);
+// supported, and its pipeline stages fit in shared memory for this layout
+bool gemv_tc_fits(const GemvShape &s, const TcLayout &L, int device);
 size_t gemv_tc_workspace_bytes(const GemvShape &s, const TcLayout &L, int device);
 int gemv_tc_launch(const GemvShape &s, const TcLayout &L, const void *w, int64_t w_bytes, const float *x, float *y,
                    int64_t y_ld, void *ws, size_t ws_bytes, cudaStream_t stream, int device);
