@@ -707,6 +707,9 @@ def run_ours(args):
     rank, world, local = dist_env()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if world > 1 and (local >= torch.cuda.device_count() or world > torch.cuda.device_count()):
+        # ranks whose kernels wait on one another must never share a GPU
+        raise SystemExit(f"{world} ranks need {world} GPUs (one process per GPU); {torch.cuda.device_count()} visible")
     torch.cuda.set_device(local)
     pg = None
     if world > 1:
