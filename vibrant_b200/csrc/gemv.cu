@@ -839,9 +839,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             __threadfence_system();   // ... and, cumulatively, visible before the count
             const unsigned old = atomicAdd(&gq.sync[1], 1u);
             if (old == (unsigned)p.grid - 1u) {
+                // Every CTA fenced at system scope before counting itself in, so
+                // all stores of this call are visible to every GPU by now; an
+                // acquire at GPU scope orders that observation before the
+                // release stores of "done" (no second system fence).
+                __threadfence();
                 gq.sync[1] = 0u;
                 gq.sync[0] = seq;
-                __threadfence_system();
                 if (*reinterpret_cast<volatile unsigned *>(&gq.sync[2]) == 0u) {
                     for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, seq);
                     const int st = wait_flags_eq(gq.peer_flags[gq.rank] + gq.world, gq.world, seq, gq.wait_ns);
