@@ -420,7 +420,7 @@ def headline(ctx, args):
         "dt": dt, "e_dt": e_dt, "total": total, "shard_alg": shard_alg, "lo": lo, "hi": hi, "copies": nc,
         "copy_bytes": base.nbytes, "err": err, "clocks": sampler.summary(), "traffic": traffic,
         "kernel": kname or ("vkq::gemv_kernel<Q4_K,1,32,all-gather>" if gather is not None else
-                            "vkq::gemv_kernel<Q4_K,1,32>"),
+                            "vkq::gemv_tc_kernel<Q4_K,1>"),
         "h2d": 4 * K, "d2h": 4 * N,
     }
 
