@@ -55,8 +55,9 @@ def parse():
     ap.add_argument("--only", default=None, help="comma list of secondary workloads to run (default: all)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
     ap.add_argument("--probe", default=None, help="QTYPE,K,N,M[,COPIES]: time one workload (profiling)")
-    ap.add_argument("--gemv", default="auto", choices=["auto", "simt", "tc"],
-                    help="GEMV kernel for M <= 8 (vkq_set_gemv_path): automatic, CUDA cores or tensor cores")
+    ap.add_argument("--gemv", default="auto", choices=["auto", "simt", "tc", "strip"],
+                    help="GEMV kernel for M <= 8 (vkq_set_gemv_path): automatic, CUDA cores, tensor cores or "
+                         "Q4_K column strips")
     return ap.parse_args()
 
 
@@ -811,7 +812,7 @@ def main():
     args = parse()
     if args.gemv != "auto" and args.impl == "ours":
         from vibrant_b200 import vkq
-        vkq.set_gemv_path({"simt": vkq.GEMV_SIMT, "tc": vkq.GEMV_TC}[args.gemv])
+        vkq.set_gemv_path({"simt": vkq.GEMV_SIMT, "tc": vkq.GEMV_TC, "strip": vkq.GEMV_STRIP}[args.gemv])
     if args.probe:
         run_probe(args)
     elif args.impl == "reference":

@@ -133,7 +133,9 @@ VKQ_API int vkq_gemm(int device, int qtype, const void *w, int64_t w_bytes, int6
 
 /* Selects the kernel that serves vkq_gemv / vkq_matmul for 1 <= M <= 8,
  * process-wide: 0 automatic (the default), 1 the CUDA-core kernel, 2 the
- * tensor-core kernel (M <= 4; both in the 1e-5 tolerance class).  Returns
+ * tensor-core kernel (M <= 4), 3 the Q4_K column-strip kernel (M <= 4,
+ * N % 256 == 0); all in the 1e-5 tolerance class, and a kernel that does not
+ * serve a shape leaves it to the automatic choice.  Returns
  * the previous choice, or -1 for an invalid one.  No counterpart in the
  * reference (it has one fp32 kernel, internal/gpu/cuda/kernels.cu:61-77);
  * for tests and measurements. */

@@ -7,6 +7,8 @@ Q4_K, Q5_K, Q6_K = 12, 13, 14
 BLOCK_BYTES = {Q4_K: 144, Q5_K: 176, Q6_K: 210}
 GEMV_TOL = 1e-5    # max |y - y_ref| / sum_k |x_k W_kn|, fp32-accumulate GEMV
 GEMM_TOL = 2e-2    # same metric, bf16 tensor-core GEMM
+# vkq_set_gemv_path values of the three GEMV kernels
+GEMV_PATHS = {"simt": 1, "tc": 2, "strip": 3}
 
 
 def matmul_error(y: np.ndarray, x: np.ndarray, w: np.ndarray, y_ref: np.ndarray | None = None,

@@ -14,10 +14,12 @@ pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 
-@pytest.fixture(params=["simt", "tc"], autouse=True)
+@pytest.fixture(params=["simt", "tc", "strip"], autouse=True)
 def gemv_path(request):
+    """Every test on each GEMV kernel (a kernel that does not serve a shape
+    leaves it to the automatic choice)."""
     from vibrant_b200 import vkq
-    old = vkq.set_gemv_path(vkq.GEMV_SIMT if request.param == "simt" else vkq.GEMV_TC)
+    old = vkq.set_gemv_path(helpers.GEMV_PATHS[request.param])
     yield request.param
     vkq.set_gemv_path(old)
 
@@ -105,6 +107,9 @@ SHAPES = [
     (13, 512, 4096, 5),
     (12, 2048, 2048, 8),
     (14, 33, 96, 7),
+    (12, 5120, 1024, 2),    # 14B k/v projection, two rows
+    (12, 333, 4096, 4),     # K split over a cluster with a ragged last range
+    (12, 7, 256, 1),        # fewer rows than a cluster's CTAs would take
 ]
 
 
@@ -191,7 +196,7 @@ def test_side_stream_and_graph_capture(tvk):
     assert torch.equal(out2, ref)
 
 
-def test_error_paths(tvk):
+def test_error_paths(tvk, gemv_path):
     torch, vt = tvk
     from vibrant_b200 import vkq
     K, N = 256, 256
@@ -219,12 +224,15 @@ def test_error_paths(tvk):
     with pytest.raises(vkq.VkqError) as e:
         call(w=buf.data_ptr() + 8)
     assert e.value.status == vkq.ERR_MISALIGNED
-    with pytest.raises(vkq.VkqError) as e:
-        call(ws=None, wsb=0)
-    assert e.value.status == vkq.ERR_WORKSPACE
-    with pytest.raises(vkq.VkqError) as e:
-        call(wsb=1024)  # below either kernel's need
-    assert e.value.status == vkq.ERR_WORKSPACE
+    if gemv_path == "strip":
+        call(ws=None, wsb=0)  # the column-strip kernel needs no workspace
+    else:
+        with pytest.raises(vkq.VkqError) as e:
+            call(ws=None, wsb=0)
+        assert e.value.status == vkq.ERR_WORKSPACE
+        with pytest.raises(vkq.VkqError) as e:
+            call(wsb=1024)  # below either kernel's need
+        assert e.value.status == vkq.ERR_WORKSPACE
     with pytest.raises(vkq.VkqError) as e:
         call(x=0)
     assert e.value.status == vkq.ERR_INVALID_ARGUMENT

@@ -5,7 +5,7 @@ restated in the oracle).  Q6_K quants then cluster around the zero point
 q = 32 (the case where a GEMV that accumulates a*q and subtracts 32*sum(a)
 loses the most), and Q4_K blocks carry large negative mins.
 
-Both GEMV kernels (CUDA cores and tensor cores) at 1e-5 of sum_k |x w| for
+The three GEMV kernels (CUDA cores, tensor cores, Q4_K column strips) at 1e-5 of sum_k |x w| for
 M = 1..4, including row-straddling shapes (N % 256 == 128), and the
 tensor-core GEMM at 2e-2 on every output of a 512-row prefill; plus
 activations of extreme magnitude."""
@@ -25,10 +25,10 @@ def _weights(oracle, qt, K, N, seed, sigma=0.02):
     return wq, wd
 
 
-@pytest.fixture(params=["simt", "tc"])
+@pytest.fixture(params=["simt", "tc", "strip"])
 def path(request):
     from vibrant_b200 import vkq
-    old = vkq.set_gemv_path(vkq.GEMV_SIMT if request.param == "simt" else vkq.GEMV_TC)
+    old = vkq.set_gemv_path(helpers.GEMV_PATHS[request.param])
     yield request.param
     vkq.set_gemv_path(old)
 
@@ -76,7 +76,7 @@ def test_gemm_full_size_prefill_every_output(oracle, qt):
     assert helpers.matmul_error(y, x, wd) <= helpers.GEMM_TOL
 
 
-@pytest.mark.parametrize("kernel", ["simt", "tc", "gemm"])
+@pytest.mark.parametrize("kernel", ["simt", "tc", "strip", "gemm"])
 def test_extreme_activation_magnitudes(oracle, kernel):
     """Activations from 1e-30 to 1e20 (the GEMM scales x by 2^49 before its
     bf16 conversion, which stays finite below 2^79 ~ 6e23)."""
@@ -91,7 +91,7 @@ def test_extreme_activation_magnitudes(oracle, kernel):
     x[:, ::7] *= np.float32(1e20)
     x[:, 3::7] *= np.float32(1e-30)
     w = vt.QuantWeight(qt, K, N, wq)
-    old = vkq.set_gemv_path(vkq.GEMV_TC if kernel == "tc" else vkq.GEMV_SIMT)
+    old = vkq.set_gemv_path(helpers.GEMV_PATHS.get(kernel, vkq.GEMV_SIMT))
     try:
         y = vt.matmul(torch.from_numpy(x).cuda(), w, path="gemm" if kernel == "gemm" else "auto").cpu().numpy()
     finally:

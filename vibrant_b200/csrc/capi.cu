@@ -392,8 +392,8 @@ int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, in
 
 int vkq_set_gemv_path(int path) {
     t_err[0] = '\0';
-    if (path < 0 || path > 2) {
-        set_error("vkq_set_gemv_path: 0 (automatic), 1 (CUDA cores) or 2 (tensor cores)");
+    if (path < 0 || path > 3) {
+        set_error("vkq_set_gemv_path: 0 (automatic), 1 (CUDA cores), 2 (tensor cores) or 3 (column strips)");
         return -1;
     }
     return set_gemv_path(path);

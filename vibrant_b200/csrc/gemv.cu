@@ -974,7 +974,9 @@ static Plan make_plan(const GemvShape &s, int device) {
 }
 
 // Which kernel serves a plain GEMV (vkq_set_gemv_path): 0 chooses, 1 the
-// CUDA-core kernel of this file, 2 the tensor-core kernel (gemv_tc.cu).
+// CUDA-core kernel of this file, 2 the tensor-core kernel (gemv_tc.cu), 3 the
+// column-strip kernel (gemv_strip.cu); a kernel that does not serve the shape
+// leaves the choice to the automatic order.
 static int g_gemv_path = 0;
 
 int set_gemv_path(int path) {
@@ -992,6 +994,20 @@ static bool use_tensor_cores(const GemvShape &s, int device) {
     return gemv_tc_fits(s, TcLayout{s.N, 0, 0}, device);
 }
 
+// Single-row Q4_K GEMVs with N % 256 == 0 go to the column-strip kernel (no
+// workspace, no cross-CTA sums; as fast as the tensor-core kernel or faster
+// on every 3B and 14B layer shape measured), M = 2..4 to the tensor-core
+// kernel, unless a kernel is selected.  (Weight pointers are 16-byte
+// aligned: the entry points check it.)
+static bool use_strips(const GemvShape &s, int device) {
+    if (g_gemv_path == 1 || g_gemv_path == 2 || s.N % 256 != 0) return false;
+    if (g_gemv_path == 0 && s.M != 1) return false;
+    return gemv_strip_fits(s, StripLayout{s.N, 0}, device);
+}
+
+// Enough workspace for whichever kernel serves the shape (the CUDA-core
+// and tensor-core kernels check their own need; the column-strip kernel
+// needs none).
 size_t gemv_workspace_bytes(const GemvShape &s, int device) {
     Plan pl = make_plan(s, device);
     const size_t simt = pl.generic ? 0 : kWorkspaceCounterHead + pl.partial_bytes;
@@ -1036,6 +1052,8 @@ static cudaError_t dispatch_mr(const GemvParams &gp, const GatherParams &gq, con
 
 int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,
                 size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather) {
+    if (!gather && use_strips(s, device))
+        return gemv_strip_launch(s, StripLayout{s.N, 0}, w, w_bytes, x, y, s.N, 0, stream, device);
     if (!gather && use_tensor_cores(s, device))
         return gemv_tc_launch(s, TcLayout{s.N, 0, 0}, w, w_bytes, x, y, s.N, ws, ws_bytes, stream, device);
     Plan pl = make_plan(s, device);
@@ -1150,6 +1168,7 @@ static void *noalloc_scratch_address(int device) {
 
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
                         cudaStream_t stream, int device) {
+    if (use_strips(s, device)) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);
     Plan pl = make_plan(s, device);
     const bool tc = use_tensor_cores(s, device);
     if (pl.generic && !tc) return gemv_launch(s, w, w_bytes, x, y, nullptr, 0, stream, device);

@@ -1,0 +1,488 @@
+// gemv_strip.cu -- Q4_K dequantize + GEMV in column strips on sm_100a, for
+// weights whose stored rows start on a super-block boundary (the N % 256 == 0
+// layers of a transformer and their row-block shards).
+//
+// y[m][n] = sum_k x[m][k] * W[k][n], 1 <= M <= 4, fp32 accumulate, with the
+// per-value arithmetic of the CUDA-core GEMV in gemv.cu: the weight
+// w = (d*sc)*q - dmin*m is formed with one rounding, then x*w accumulated.
+// Q4_K layout (internal/tensor/quant_q4k.go:137-157, values as in
+// DequantizeQ4_K, quant_q4k.go:37-79): d, dmin (f16), 12 bytes of 6-bit
+// scales and mins in four little-endian 24-bit groups (sc[0..3], sc[4..7],
+// m[0..3], m[4..7]), then 128 bytes of quants, value v in byte v/2 (low
+// nibble for even v).  A 32-value sub-block is therefore 16 contiguous quant
+// bytes under one (scale, min) pair.
+//
+// Design (HBM-bound; algorithmic bytes per call = weight + x + y):
+//  * A lane-column is V consecutive output columns of the launch: one
+//    sub-block (V = 32, 16 quant bytes) or half of one (V = 16, 8 bytes).
+//    The lane-columns are dealt out in contiguous runs to column groups.  A
+//    group is one CTA, or a thread-block cluster of S CTAs that split K into
+//    S ranges and add their sums through distributed shared memory: no
+//    partial sum leaves the SM, so there is no global workspace, atomic or
+//    memory fence, and small matrices finish in one pass of the machine.
+//  * Thread t of a CTA owns lane-column t % nlc of its group and every R-th
+//    row (R = 512 / nlc) of the CTA's k range.  Per row it copies the
+//    16-byte block header, its quant bytes and x[m][k] into a ring of
+//    kStripDepth slots of its own in shared memory with cp.async (L2 256-byte
+//    prefetch), kStripDepth rows ahead of their use: the bytes in flight take
+//    no registers, and as each thread reads only its own slots, no barrier is
+//    needed (cp.async.wait_group per thread).  Lanes of one warp take
+//    adjacent lane-columns, so a warp's copies cover contiguous runs of each
+//    row.  The first rows' weight bytes are requested before
+//    griddepcontrol.wait (the weight does not depend on the preceding kernel;
+//    x and y do).
+//  * Per row: d and dmin, the sub-block's 6-bit scale and min (one funnel
+//    shift each out of the header words), then per pair of values one byte
+//    permute per value and two packed fp32x2 FMAs (w, then x*w; the quant is
+//    used as the subnormal float q * 2^-149 with the multipliers scaled by
+//    powers of two, exactly as in gemv.cu).
+//  * Sums: the CTA's threads add through shared memory in a fixed order
+//    (rows strided over threads, then the strides), the cluster's CTAs
+//    through DSMEM in CTA-rank order, so results are run-to-run identical.
+#include <cstdint>
+#include <mutex>
+
+#include "kq_device.cuh"
+#include "vkq_internal.h"
+
+namespace vkq {
+
+constexpr int kStripThreads = 512;  // one CTA per SM
+constexpr int kStripMaxCluster = 8;
+constexpr int kStripDepth = 8;      // rows in flight per thread
+constexpr int kStripSlot = 48;      // ring slot: header [0,16), quants [16,32), x[0..M) [32,48)
+
+// Multipliers of the subnormal-quant form (the values gemv.cu uses).
+constexpr float kStripScale = 0x1p100f;   // d*sc
+constexpr float kStripDown = 0x1p-49f;    // -dmin*m
+constexpr float kStripXScale = 0x1p49f;   // x
+
+struct StripParams {
+    const uint8_t *w;  // stored rows of row_blocks super-blocks each
+    const float *x;    // [M][K]
+    float *y;          // [M][y_ld], columns [col_off, col_off + N)
+    int64_t K, y_ld, col_off;
+    int64_t row_bytes;  // bytes per stored row
+    int64_t k_per;      // rows per cluster rank
+    int c0;             // in-block position of the launch's first column (multiple of V)
+    int lanes;          // lane-columns of the launch (N / V)
+    int groups;         // column groups
+    int S;              // CTAs per cluster
+};
+
+// cp.async global -> shared of 16, 8 or 4 bytes; the 16- and 8-byte copies
+// ask L2 to fetch the whole 256-byte sector group (the neighbouring
+// lane-columns of other CTAs read the rest of it).
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global.L2::256B [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem(const float *local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32addr(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// The quant words of one lane-column row (V / 8 words of 8 values), read
+// from a ring slot.
+template <int V> struct QWords;
+template <> struct QWords<32> {
+    uint4 v;
+    __device__ __forceinline__ void read(uint32_t a) { v = lds128(a); }
+    __device__ __forceinline__ uint32_t operator[](int i) const {
+        return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+    }
+};
+template <> struct QWords<16> {
+    uint2 v;
+    __device__ __forceinline__ void read(uint32_t a) { v = lds64(a); }
+    __device__ __forceinline__ uint32_t operator[](int i) const { return i == 0 ? v.x : v.y; }
+};
+
+template <int M, int V>
+__global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const StripParams p) {
+    constexpr int D = kStripDepth;
+    constexpr int MV = M * V;
+    constexpr int NP = V / 2;  // value pairs per lane-column
+    // ring[D][kStripThreads] slots during the main loop; afterwards the same
+    // bytes hold red[kStripThreads][M*V + 4] and red2[kStripThreads]
+    extern __shared__ __align__(16) uint8_t smem[];
+    float *red = reinterpret_cast<float *>(smem);
+    float *red2 = red + kStripThreads * (MV + 4);
+
+    const int t = threadIdx.x;
+    const int S = p.S;
+    const int crank = S > 1 ? (int)cluster_ctarank() : 0;
+    const int g = (int)(blockIdx.x / (unsigned)S);
+    const int lo = (int)((int64_t)g * p.lanes / p.groups);
+    const int nlc = (int)((int64_t)(g + 1) * p.lanes / p.groups) - lo;
+    const int R = kStripThreads / nlc;  // row groups (threads per lane-column)
+    const int lcl = t % nlc, rg = t / nlc;
+    const int64_t k0 = (int64_t)crank * p.k_per;
+    const int64_t span = (p.K - k0 < p.k_per ? p.K - k0 : p.k_per);
+    const int nr = (rg < R && span > rg) ? (int)((span - rg + R - 1) / R) : 0;
+
+    // this thread's lane-column: block b of the stored row, first value `within`
+    const int pos = p.c0 + (lo + lcl) * V;
+    const int64_t b = pos >> 8;
+    const int within = pos & 255;
+    const int j = within >> 5;  // sub-block
+    // 6-bit fields in header words 1..3: scale at bit 24*(j/4) + 6*(j%4), min 48 bits later
+    const int o_sc = 24 * (j >> 2) + 6 * (j & 3), o_m = o_sc + 48;
+    const bool sc_hi = o_sc >= 32, m_hi = o_m >= 64;
+    const uint32_t s_sc = (uint32_t)(o_sc & 31), s_m = (uint32_t)(o_m & 31);
+    const int qoff = 16 + (within >> 1);
+
+    const int64_t step = (int64_t)R * p.row_bytes;
+    const uint8_t *pw = p.w + (k0 + rg) * p.row_bytes + b * 144;  // header of the next row to request
+    const float *px = p.x + k0 + rg;                                // x[0][next row]
+    const uint32_t slot0 = smem_u32addr(smem) + (uint32_t)(t * kStripSlot);
+    constexpr uint32_t kSlotStride = kStripThreads * kStripSlot;
+
+    auto request_w = [&](int u) {
+        const uint32_t a = slot0 + (uint32_t)u * kSlotStride;
+        cp_async_16(a, pw);
+        if constexpr (V == 32) cp_async_16(a + 16, pw + qoff);
+        else cp_async_8(a + 16, pw + qoff);
+        pw += step;
+    };
+    auto request_x = [&](int u) {
+        const uint32_t a = slot0 + (uint32_t)u * kSlotStride + 32;
+#pragma unroll
+        for (int m = 0; m < M; m++) cp_async_4(a + 4 * m, px + (int64_t)m * p.K);
+        px += R;
+    };
+    // prologue: the weight bytes of the first D rows, then (once the
+    // preceding kernel is complete) their x; one commit group per row
+#pragma unroll
+    for (int u = 0; u < D; u++)
+        if (u < nr) request_w(u);
+    pdl_wait();  // x (and y) may belong to the preceding kernel
+    pdl_launch_dependents();
+#pragma unroll
+    for (int u = 0; u < D; u++) {
+        if (u < nr) request_x(u);
+        cp_async_commit();
+    }
+
+    float2 acc[M][NP];
+#pragma unroll
+    for (int m = 0; m < M; m++)
+#pragma unroll
+        for (int i = 0; i < NP; i++) acc[m][i] = make_float2(0.f, 0.f);
+
+    for (int i0 = 0; i0 < nr; i0 += D) {
+#pragma unroll
+        for (int u = 0; u < D; u++) {
+            if (i0 + u < nr) {
+                cp_async_wait<D - 1>();  // row i0 + u (commit group i0 + u) has landed
+                const uint32_t a = slot0 + (uint32_t)u * kSlotStride;
+                const uint4 h = lds128(a);
+                QWords<V> q;
+                q.read(a + 16);
+                float xr[M];
+                if constexpr (M == 1) {
+                    xr[0] = __uint_as_float(lds32(a + 32));
+                } else {
+                    const uint4 xq = lds128(a + 32);
+                    const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+#pragma unroll
+                    for (int m = 0; m < M; m++) xr[m] = __uint_as_float(xw[m]);
+                }
+                if (i0 + u + D < nr) {  // refill this slot with the row D ahead
+                    request_w(u);
+                    request_x(u);
+                }
+                cp_async_commit();
+                const float d = hw_f16_to_f32(h.x & 0xFFFFu), dmin = hw_f16_to_f32(h.x >> 16);
+                const uint32_t sa = sc_hi ? h.z : h.y, sb = sc_hi ? h.w : h.z;
+                const uint32_t ma = m_hi ? h.w : h.z, mb = m_hi ? 0u : h.w;
+                const float ds = (d * kStripScale) * (float)(__funnelshift_r(sa, sb, s_sc) & 63u);
+                const float ndm = (dmin * -kStripDown) * (float)(__funnelshift_r(ma, mb, s_m) & 63u);
+                const float2 s2 = make_float2(ds, ds), nm2 = make_float2(ndm, ndm);
+                float2 xs[M];
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    const float xm = xr[m] * kStripXScale;
+                    xs[m] = make_float2(xm, xm);
+                }
+#pragma unroll
+                for (int c = 0; c < V / 8; c++) {
+                    // byte lane i of E / O holds value 8c + 2i / 8c + 2i + 1
+                    const uint32_t E = q[c] & 0x0F0F0F0Fu, O = (q[c] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float2 q2 = make_float2(__uint_as_float(prmt(E, 0u, 0x4440u | i)),
+                                                      __uint_as_float(prmt(O, 0u, 0x4440u | i)));
+                        const float2 w2 = f2fma(s2, q2, nm2);
+#pragma unroll
+                        for (int m = 0; m < M; m++) acc[m][4 * c + i] = f2fma(xs[m], w2, acc[m][4 * c + i]);
+                    }
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // the ring's bytes become the sums' buffer
+
+    // ---- sums over the CTA's row groups ----
+    // red[t][m*V + v] with rows padded to RS = MV + 4 floats, so the 16-byte
+    // stores of 8 consecutive threads fall on distinct banks
+    constexpr int RS = MV + 4;
+    if (rg < R) {
+        float4 *mine = reinterpret_cast<float4 *>(red + t * RS);
+#pragma unroll
+        for (int m = 0; m < M; m++)
+#pragma unroll
+            for (int i = 0; i < NP; i += 2)
+                mine[(m * V + 2 * i) / 4] = make_float4(acc[m][i].x, acc[m][i].y, acc[m][i + 1].x, acc[m][i + 1].y);
+    }
+    __syncthreads();
+    // output e = lcl*MV + mv: the row group r of lane-column lcl wrote it at
+    // red[(r*nlc + lcl)*RS + mv]; the sum goes to row group 0's element
+    // (lcl*RS + mv), which no other output reads
+    const int E = nlc * MV;
+    const int rstride = nlc * RS;
+    const int P = E >= kStripThreads ? 1 : kStripThreads / E;  // threads per output
+    if (P == 1) {
+        for (int e = t; e < E; e += kStripThreads) {
+            const int at = (e / MV) * RS + e % MV;
+            float s = 0.f;
+            for (int r = 0; r < R; r++) s += red[r * rstride + at];
+            red[at] = s;
+        }
+    } else {
+        const int e = t % E, part = t / E;
+        const int at = (e / MV) * RS + e % MV;
+        if (part < P) {
+            float s = 0.f;
+            for (int r = part; r < R; r += P) s += red[r * rstride + at];
+            red2[part * E + e] = s;
+        }
+        __syncthreads();
+        if (t < E) {
+            float s = 0.f;
+            for (int q = 0; q < P; q++) s += red2[q * E + t];
+            red[at] = s;
+        }
+    }
+    __syncthreads();
+
+    // ---- the cluster's CTAs add their sums in rank order and store y ----
+    const int e_lo = S > 1 ? crank * E / S : 0, e_hi = S > 1 ? (crank + 1) * E / S : E;
+    if (S > 1) cluster_sync_all();
+    for (int e = e_lo + t; e < e_hi; e += kStripThreads) {
+        const int lc = e / MV, m = (e % MV) / V, v = e % V;
+        const float *src = red + lc * RS + e % MV;
+        float s;
+        if (S > 1) {
+            s = ld_dsmem(src, 0);
+            for (int r = 1; r < S; r++) s += ld_dsmem(src, (uint32_t)r);
+        } else {
+            s = *src;
+        }
+        p.y[(int64_t)m * p.y_ld + p.col_off + (int64_t)(lo + lc) * V + v] = s;
+    }
+    if (S > 1) cluster_sync_all();  // no CTA leaves while the others read its shared memory
+}
+
+// ------------------------------- host side -------------------------------
+struct StripPlan {
+    int V = 0, S = 1, groups = 0, lanes = 0;
+    int64_t k_per = 0;
+    size_t smem = 0;
+};
+
+static size_t strip_smem(int M, int V) {
+    const size_t ring = (size_t)kStripDepth * kStripThreads * kStripSlot;
+    const size_t sums = (size_t)kStripThreads * (M * V + 5) * sizeof(float);
+    return ring > sums ? ring : sums;
+}
+
+template <int M, int V> static const void *strip_fn() { return (const void *)gemv_strip_kernel<M, V>; }
+static const void *strip_kernel(int M, int V) {
+    switch (M) {
+    case 1: return V == 32 ? strip_fn<1, 32>() : strip_fn<1, 16>();
+    case 2: return V == 32 ? strip_fn<2, 32>() : strip_fn<2, 16>();
+    case 3: return strip_fn<3, 16>();
+    default: return strip_fn<4, 16>();
+    }
+}
+
+static cudaError_t strip_prepare(const void *fn, size_t smem) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    return e;
+}
+
+// CTAs of clusters of S that the device runs at once (max active clusters x S).
+static int strip_capacity(int M, int V, int S, int device) {
+    static std::mutex mu;
+    static int cache[16][5][2][kStripMaxCluster + 1];  // [device][M][V == 32][S], 0 = not asked
+    const int sms = device_sm_count(device);
+    if (S == 1) return sms;
+    if (device < 0 || device >= 16) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    int &c = cache[device][M][V == 32][S];
+    if (c == 0) {
+        const void *fn = strip_kernel(M, V);
+        const size_t smem = strip_smem(M, V);
+        int n = 0;
+        if (strip_prepare(fn, smem) == cudaSuccess) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3((unsigned)(S * (sms / S)));
+            cfg.blockDim = dim3(kStripThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute a[1];
+            a[0].id = cudaLaunchAttributeClusterDimension;
+            a[0].val.clusterDim.x = (unsigned)S;
+            a[0].val.clusterDim.y = 1;
+            a[0].val.clusterDim.z = 1;
+            cfg.attrs = a;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) n = 0;
+        }
+        cudaGetLastError();
+        c = n > 0 ? n * S : -1;
+    }
+    return c > 0 ? c : 0;
+}
+
+// Estimated cycles of one launch: the busiest CTA's issue time (thread
+// instructions per lane-column row, 32 threads per warp instruction, four
+// schedulers at ~2/3 issue), or its longest thread's chain of rows, plus
+// fixed costs (DRAM latency and the sums; the cluster barriers).
+static double strip_cost(int M, int V, int S, int nlc, int64_t rows) {
+    const double per_row = V * (2.4 + 0.5 * M) + 34 + 4 * M;
+    const double issue = (double)nlc * (double)rows * per_row / (32 * 4 * 0.67);
+    const int R = kStripThreads / nlc;
+    const double chain = (double)((rows + R - 1) / R) * (per_row + 40);
+    return (issue > chain ? issue : chain) + 2500 + (S > 1 ? 2000 + 600 * S : 0);
+}
+
+static bool strip_layout_ok(const GemvShape &s, const StripLayout &L, int V) {
+    return s.N % V == 0 && L.rs % 256 == 0 && L.c0 % V == 0 && L.c0 >= 0 && L.c0 < 256 &&
+           L.c0 + s.N <= L.rs && s.N / V < (int64_t(1) << 30);
+}
+
+static StripPlan strip_plan(const GemvShape &s, const StripLayout &L, int device) {
+    StripPlan best;
+    if (!gemv_strip_supported(s)) return best;
+    double best_cost = 0;
+    // 32-value lane-columns for M <= 2 (measured faster than 16 at every
+    // cluster size); 16 for M >= 3 (the accumulators of 32 would not fit)
+    for (int V : {32, 16}) {
+        if ((V == 32) != (s.M <= 2)) continue;
+        if (!strip_layout_ok(s, L, V)) continue;
+        const int64_t lanes = s.N / V;
+        for (int S = 1; S <= kStripMaxCluster; S++) {
+            if (S > 1 && (kStripMaxCluster % S != 0 && S != 3 && S != 6)) continue;
+            if ((int64_t)S > s.K) break;
+            const int cap = strip_capacity((int)s.M, V, S, device);
+            int64_t groups = cap / S;
+            if (groups <= 0) continue;
+            if (groups > lanes) groups = lanes;
+            const int64_t nlc = (lanes + groups - 1) / groups;
+            if (nlc > kStripThreads) continue;
+            const int64_t k_per = (s.K + S - 1) / S;
+            if ((int64_t)(S - 1) * k_per >= s.K) continue;  // every rank gets rows
+            const double c = strip_cost((int)s.M, V, S, (int)nlc, k_per);
+            if (best.V == 0 || c < best_cost) {
+                best_cost = c;
+                best.V = V;
+                best.S = S;
+                best.groups = (int)groups;
+                best.lanes = (int)lanes;
+                best.k_per = k_per;
+                best.smem = strip_smem((int)s.M, V);
+            }
+        }
+    }
+    return best;
+}
+
+bool gemv_strip_supported(const GemvShape &s) {
+    return s.qtype == kQ4K && s.M >= 1 && s.M <= 4 && s.K >= 1 && s.N >= 16;
+}
+
+bool gemv_strip_fits(const GemvShape &s, const StripLayout &L, int device) {
+    return strip_plan(s, L, device).V != 0;
+}
+
+int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, int64_t w_bytes, const float *x,
+                      float *y, int64_t y_ld, int64_t col_off, cudaStream_t stream, int device) {
+    const StripPlan pl = strip_plan(s, L, device);
+    if (pl.V == 0) {
+        set_error("the column-strip GEMV does not serve this shape or layout");
+        return 3;
+    }
+    const int64_t row_bytes = L.rs / 256 * 144;
+    if (w_bytes < s.K * row_bytes) {
+        set_error("weight buffer too small: %lld bytes for %lld rows of %lld", (long long)w_bytes, (long long)s.K,
+                  (long long)row_bytes);
+        return 2;
+    }
+    StripParams p{};
+    p.w = static_cast<const uint8_t *>(w);
+    p.x = x;
+    p.y = y;
+    p.K = s.K;
+    p.y_ld = y_ld;
+    p.col_off = col_off;
+    p.row_bytes = row_bytes;
+    p.k_per = pl.k_per;
+    p.c0 = (int)L.c0;
+    p.lanes = pl.lanes;
+    p.groups = pl.groups;
+    p.S = pl.S;
+    const void *fn = strip_kernel((int)s.M, pl.V);
+    cudaError_t e = strip_prepare(fn, pl.smem);
+    if (e == cudaSuccess) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3((unsigned)(pl.groups * pl.S));
+        cfg.blockDim = dim3(kStripThreads);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute a[2];
+        a[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        a[0].val.programmaticStreamSerializationAllowed = 1;
+        int na = 1;
+        if (pl.S > 1) {
+            a[1].id = cudaLaunchAttributeClusterDimension;
+            a[1].val.clusterDim.x = (unsigned)pl.S;
+            a[1].val.clusterDim.y = 1;
+            a[1].val.clusterDim.z = 1;
+            na = 2;
+        }
+        cfg.attrs = a;
+        cfg.numAttrs = (unsigned)na;
+        void *args[] = {&p};
+        e = cudaLaunchKernelExC(&cfg, fn, args);
+    }
+    if (e != cudaSuccess) {
+        set_error("column-strip gemv launch failed: %s", cudaGetErrorString(e));
+        return 5;
+    }
+    return 0;
+}
+
+}  // namespace vkq

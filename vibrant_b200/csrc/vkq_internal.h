@@ -54,7 +54,9 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
 int gemv_launch_noalloc(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y,
                         cudaStream_t stream, int device);
 int gemv_read_status();
-// Selects the kernel of plain GEMVs: 0 automatic, 1 CUDA cores, 2 tensor cores; returns the previous choice.
+// Selects the kernel of plain GEMVs: 0 automatic, 1 CUDA cores (gemv.cu), 2
+// tensor cores (gemv_tc.cu), 3 column strips (gemv_strip.cu); returns the
+// previous choice.
 int set_gemv_path(int path);
 
 // Tensor-core GEMV (gemv_tc.cu), fp32-class results, 1 <= M <= 4, N % 32 == 0.
@@ -71,6 +73,19 @@ size_t gemv_tc_workspace_bytes(const GemvShape &s, const TcLayout &L, int device
 int gemv_tc_launch(const GemvShape &s, const TcLayout &L, const void *w, int64_t w_bytes, const float *x, float *y,
                    int64_t y_ld, void *ws, size_t ws_bytes, cudaStream_t stream, int device);
 int gemv_tc_read_status();
+
+// Q4_K column-strip GEMV (gemv_strip.cu), 1 <= M <= 4, for stored rows that
+// start on a super-block boundary: row k of the weight is rs / 256 blocks,
+// and column n of the launch is value c0 + n of its stored row ({N, 0} for
+// a plain [K, N] weight with N % 256 == 0; {rb*256, lo & 255} for the
+// row-block shard of columns [lo, ...) of such a weight).  Needs no workspace.
+struct StripLayout {
+    int64_t rs, c0;
+};
+bool gemv_strip_supported(const GemvShape &s);
+bool gemv_strip_fits(const GemvShape &s, const StripLayout &L, int device);
+int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, int64_t w_bytes, const float *x,
+                      float *y, int64_t y_ld, int64_t col_off, cudaStream_t stream, int device);
 
 // bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
 size_t gemm_workspace_bytes(const GemvShape &s, int device);

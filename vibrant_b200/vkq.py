@@ -157,11 +157,12 @@ def gemv_noalloc(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: in
     _check(load().vkq_gemv_noalloc(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, _stream_ptr(stream)))
 
 
-GEMV_AUTO, GEMV_SIMT, GEMV_TC = 0, 1, 2
+GEMV_AUTO, GEMV_SIMT, GEMV_TC, GEMV_STRIP = 0, 1, 2, 3
 
 
 def set_gemv_path(path: int) -> int:
-    """vkq_set_gemv_path: 0 automatic, 1 CUDA cores, 2 tensor cores (process-wide); returns the previous."""
+    """vkq_set_gemv_path: 0 automatic, 1 CUDA cores, 2 tensor cores, 3 column strips (process-wide);
+    returns the previous choice."""
     old = load().vkq_set_gemv_path(path)
     if old < 0:
         raise VkqError(ERR_INVALID_ARGUMENT, last_error())
