@@ -421,7 +421,7 @@ def headline(ctx, args):
         "dt": dt, "e_dt": e_dt, "total": total, "shard_alg": shard_alg, "lo": lo, "hi": hi, "copies": nc,
         "copy_bytes": base.nbytes, "err": err, "clocks": sampler.summary(), "traffic": traffic,
         "kernel": kname or ("vkq::gemv_kernel<Q4_K,1,32,all-gather>" if gather is not None else
-                            "vkq::gemv_tc_kernel<Q4_K,1>"),
+                            "vkq::gemv_strip_kernel<1>"),
         "h2d": 4 * K, "d2h": 4 * N,
     }
 
@@ -553,6 +553,21 @@ def decode_3b(ctx, args):
     st = ctx.stream
     taps = {}
 
+    fused = ctx.world == 1  # one GPU: q|k|v and gate|up(+SiLU) in one launch each, RMSNorm folded in
+    qkv_out = [torch.empty(1, n, device=ctx.dev) for n in (m["q_out"], m["kv_out"], m["kv_out"])]
+
+    def token_fused(_i):
+        x = x0
+        for li, lay in enumerate(layers):
+            q = vt.linear_fused(x, [lay["q"].w, lay["k"].w, lay["v"].w], norm_w=norm_w[:m["hidden"]], eps=1e-6,
+                                outs=qkv_out, stream=st)[0]
+            o = lay["o"](q)
+            vt.linear_fused(o, [lay["gate"].w, lay["up"].w], norm_w=norm_w[:m["hidden"]], eps=1e-6, silu_mul=True,
+                            outs=[act], stream=st)
+            x = lay["down"](act)
+        vkq.rms_norm(x.data_ptr(), norm_w.data_ptr(), h.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
+        return head(h)
+
     def token(_i):
         x = x0
         for li, lay in enumerate(layers):
@@ -573,12 +588,16 @@ def decode_3b(ctx, args):
 
     align = (lambda: chans["q"].gemv(h, layers[0]["q"].w, ws=layers[0]["q"].ws, stream=st)) if chans else None
     steps = max(3, min(args.steps, 20))
-    dt = timed_graph(ctx, token, steps, 2, align=align)
+    dt = timed_graph(ctx, token_fused if fused else token, steps, 2, align=align)
     ctx.status("the 3B decode step")
     # parity of layer 0's q projection on every rank: the (h, q) pair of one token
     with torch.cuda.stream(st):
         vkq.rms_norm(x0.data_ptr(), norm_w.data_ptr(), h.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
-        q = layers[0]["q"](h)
+        if fused:
+            q = vt.linear_fused(x0, [layers[0]["q"].w, layers[0]["k"].w, layers[0]["v"].w],
+                                norm_w=norm_w[:m["hidden"]], eps=1e-6, stream=st)[0]
+        else:
+            q = layers[0]["q"](h)
     torch.cuda.synchronize(ctx.dev)
     hv = h.cpu().numpy().copy()
     qv = q.cpu().numpy().copy()
@@ -592,12 +611,14 @@ def decode_3b(ctx, args):
     for c in chans.values():
         c.close()
     nbytes = synth.model_bytes(m)
-    launches = m["layers"] * 10 + 2
+    launches = m["layers"] * (4 if fused else 10) + 2
     return {"workload": "decode_3b_q4k_q6k_36x2048", "value": round(1.0 / dt, 2), "unit": "tokens/s",
             "ms_per_token": round(dt * 1e3, 4), "weight_bytes_per_token": nbytes,
             "gbs": round(nbytes / dt / 1e9, 1),
             "hbm_frac_per_gpu": round(nbytes / dt / 1e9 / ctx.world / ctx.hbm, 4),
             "launches_per_token": launches, "parity_layer0_q_max_rel_err": err,
+            "fused": "rms_norm+q|k|v and rms_norm+gate|up+SiLU*up in one launch each (vkq_linear_fused)"
+            if fused else "none: every linear and elementwise step is its own launch",
             "parallelism": "single GPU" if ctx.world == 1 else
             f"every linear row-sharded over {ctx.world} GPUs with the all-gather fused into its GEMV "
             "(k, v replicated)",

@@ -167,6 +167,29 @@ VKQ_API int vkq_silu_mul(int device, const float *gate, const float *up, float *
 VKQ_API int vkq_rms_norm(int device, const float *x, const float *weight, float *out, int64_t rows, int64_t n,
                          float eps, void *stream);
 
+/* The fused linears of a decode step: one launch over `nweights` Q4_K
+ * weights [K, N_i] (N_i % 256 == 0, 16-byte aligned) that share the input
+ * x [M, K] (4-byte aligned):
+ *   h = x, or with norm_w != NULL h = x / sqrt(mean(x^2) + eps) * norm_w
+ *       row by row (the RMSNorm prologue, M <= 3);
+ *   VKQ_EPI_NONE:     y[i] = h . W_i for every weight (1..4: q, k and v);
+ *   VKQ_EPI_SILU_MUL: y[0] = SiLU(h . W_0) * (h . W_1) (two weights of one
+ *                     width: gate and up).
+ * w, w_bytes, N and y are host arrays of nweights entries; y[i] is a device
+ * buffer [M, N_i] (y[0] alone for VKQ_EPI_SILU_MUL).  fp32 accumulate, the
+ * GEMV's 1e-5 tolerance class; 1 <= M <= 4; no workspace.  Replaces, for one
+ * token, the RMSNorm of TransformerLayer.Forward (internal/transformer/
+ * layer.go:111, rms_norm_f32 of internal/gpu/cuda/kernels.cu:209-288) with the
+ * MatMul calls that follow it: q, k, v in Attention.Forward
+ * (internal/transformer/attention.go:120,124,128) and gate, up, SiLU, Mul in
+ * FeedForward.Forward (internal/transformer/feedforward.go:87-95).  Other
+ * qtypes give VKQ_ERR_UNSUPPORTED. */
+#define VKQ_EPI_NONE 0
+#define VKQ_EPI_SILU_MUL 1
+VKQ_API int vkq_linear_fused(int device, int qtype, int nweights, const void *const *w, const int64_t *w_bytes,
+                             int64_t K, const int64_t *N, const float *x, int64_t M, const float *norm_w, float eps,
+                             int epilogue, float *const *y, void *stream);
+
 /* ---- Row-sharded matmul across the GPUs of one node ----
  * The reference runs on a single device (internal/gpu/cuda/cuda.go:33-46);
  * these entry points implement the multi-GPU layout of the same MatMul.  The

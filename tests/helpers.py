@@ -69,6 +69,44 @@ def encode_q45k_exact(values: np.ndarray, qtype: int) -> np.ndarray:
     return out.reshape(-1)
 
 
+def quantize_q4k_subblocks(values: np.ndarray) -> np.ndarray:
+    """Test data that looks like a real Q4_K weight: every 32-value sub-block
+    gets its own 6-bit scale and min (the k-quant scheme: the sub-block's
+    range min(0, lo)..hi in 15 steps, d and dmin the largest sub-block step
+    and offset over 63), packed in the block layout of
+    internal/tensor/quant_q4k.go:137-157 with the 24-bit scale groups read by
+    extractScalesAndMins.  (The reference's own QuantizeQ4_K,
+    quant_q4k.go:215-282, is a test helper that fills sub-block 0's scale and
+    min only, so seven of its eight sub-blocks dequantize to zero.)  Written
+    for these tests; not part of the reference."""
+    v = np.asarray(values, dtype=np.float32).reshape(-1)
+    nb = (v.size + 255) // 256
+    x = np.zeros(nb * 256, np.float32)
+    x[:v.size] = v
+    x = x.reshape(nb, 8, 32).astype(np.float64)
+    lo = np.minimum(x.min(axis=2), 0.0)
+    hi = x.max(axis=2)
+    step = np.maximum((hi - lo) / 15.0, 1e-12)
+    d = np.maximum(step.max(axis=1) / 63.0, 1e-12)
+    dmin = np.maximum((-lo).max(axis=1) / 63.0, 1e-12)
+    d16, dmin16 = d.astype(np.float16), dmin.astype(np.float16)
+    dq, dminq = np.maximum(d16.astype(np.float64), 6e-8), np.maximum(dmin16.astype(np.float64), 6e-8)
+    sc = np.clip(np.rint(step / dq[:, None]), 1, 63).astype(np.int64)
+    mn = np.clip(np.rint(-lo / dminq[:, None]), 0, 63).astype(np.int64)
+    scale = dq[:, None] * sc
+    offs = dminq[:, None] * mn
+    q = np.clip(np.rint((x + offs[:, :, None]) / scale[:, :, None]), 0, 15).astype(np.int64).reshape(nb, 256)
+    out = np.zeros((nb, 144), np.uint8)
+    out[:, 0:2] = d16.view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = dmin16.view(np.uint8).reshape(nb, 2)
+    for g, f in enumerate((sc[:, 0:4], sc[:, 4:8], mn[:, 0:4], mn[:, 4:8])):
+        word = f[:, 0] | (f[:, 1] << 6) | (f[:, 2] << 12) | (f[:, 3] << 18)
+        for k in range(3):
+            out[:, 4 + 3 * g + k] = ((word >> (8 * k)) & 0xFF).astype(np.uint8)
+    out[:, 16:] = (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
+    return out.reshape(-1)
+
+
 def same_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """Bitwise equality with NaN as one class."""
     ab, bb = a.view(np.uint32), b.view(np.uint32)

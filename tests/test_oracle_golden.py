@@ -402,3 +402,35 @@ def test_sequential_fused_route_matches_fixture_products(oracle, qtype):
     import helpers
     assert helpers.matmul_error(seq, x, w) <= 1e-5
     assert np.max(np.abs(seq - disp) / (np.abs(disp) + 1e-4)) < 1e-3
+
+
+def test_reference_q4k_quantizer_fills_sub_block_zero_only(oracle):
+    """The reference's QuantizeQ4_K (internal/tensor/quant_q4k.go:215-282) is
+    a test helper: Scales[0] = Scales[6] = 32 and nothing else, so sub-blocks
+    1..7 have scale and min 0 and dequantize to zero.  The restatement keeps
+    that behaviour; realistic Q4_K test data comes from the per-sub-block
+    quantizer of the test helpers (next test)."""
+    rng = np.random.default_rng(4)
+    w = (rng.standard_normal(256 * 4) * 0.02).astype(np.float32)
+    wd = oracle.dequantize(12, oracle.quantize(12, w))[:w.size].reshape(4, 8, 32)
+    assert np.all(wd[:, 1:, :] == 0) and np.count_nonzero(wd[:, 0, :]) > 0
+
+
+def test_subblock_quantizer_round_trip(oracle):
+    import helpers
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal(256 * 64) * 0.02).astype(np.float32)
+    wq = helpers.quantize_q4k_subblocks(w)
+    wd = oracle.dequantize(12, wq)[:w.size]
+    assert np.all(np.abs(wd.reshape(-1, 32)).max(axis=1) > 0)            # every sub-block in use
+    assert np.sqrt(np.mean((wd - w) ** 2)) < 0.1 * np.sqrt(np.mean(w ** 2))  # 4-bit error, ~8 %
+    b = wq.reshape(-1, 144)
+    mins = np.array([[oracle_m for oracle_m in _mins(blk)] for blk in b[:8]])
+    assert (mins > 0).any()                                                 # negative offsets present
+
+
+def _mins(blk):
+    s = blk[4:16].astype(np.int64)
+    word = s[9] | (s[10] << 8) | (s[11] << 16)
+    lo = s[6] | (s[7] << 8) | (s[8] << 16)
+    return [(lo >> (6 * i)) & 63 for i in range(4)] + [(word >> (6 * i)) & 63 for i in range(4)]

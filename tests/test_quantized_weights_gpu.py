@@ -1,14 +1,16 @@
 """Parity on weights that look like real k-quant weights: Gaussian data
 quantized by the reference's own test quantizers (QuantizeQ4_K,
 internal/tensor/quant_q4k.go:215-282; QuantizeQ6_K, quant_q6k.go:214-294,
-restated in the oracle).  Q6_K quants then cluster around the zero point
-q = 32 (the case where a GEMV that accumulates a*q and subtracts 32*sum(a)
-loses the most), and Q4_K blocks carry large negative mins.
+restated in the oracle), and for Q4_K also by the per-sub-block quantizer of
+the test helpers (the reference's QuantizeQ4_K sets sub-block 0's scale and
+min only).  Q6_K quants then cluster around the zero point q = 32 (the case
+where a GEMV that accumulates a*q and subtracts 32*sum(a) loses the most),
+and Q4_K sub-blocks carry negative mins, so d*sc*q and dmin*m cancel.
 
-The three GEMV kernels (CUDA cores, tensor cores, Q4_K column strips) at 1e-5 of sum_k |x w| for
-M = 1..4, including row-straddling shapes (N % 256 == 128), and the
-tensor-core GEMM at 2e-2 on every output of a 512-row prefill; plus
-activations of extreme magnitude."""
+The three GEMV kernels (CUDA cores, tensor cores, Q4_K column strips) at
+1e-5 of sum_k |x w| for M = 1..4, including row-straddling shapes
+(N % 256 == 128), and the tensor-core GEMM at 2e-2 on every output of a
+512-row prefill; plus activations of extreme magnitude."""
 import numpy as np
 import pytest
 
@@ -17,10 +19,13 @@ import helpers
 pytestmark = pytest.mark.gpu
 
 
-def _weights(oracle, qt, K, N, seed, sigma=0.02):
+def _weights(oracle, qt, K, N, seed, sigma=0.02, quantizer="reference"):
+    """Gaussian data quantized by the reference's test quantizer (restated in
+    the oracle), or for Q4_K by the per-sub-block quantizer of the test
+    helpers."""
     rng = np.random.default_rng(seed)
     w = (rng.standard_normal(K * N) * sigma).astype(np.float32)
-    wq = oracle.quantize(qt, w)
+    wq = helpers.quantize_q4k_subblocks(w) if quantizer == "subblock" else oracle.quantize(qt, w)
     wd = oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
     return wq, wd
 
@@ -33,14 +38,16 @@ def path(request):
     vkq.set_gemv_path(old)
 
 
-@pytest.mark.parametrize("qt,K,N", [(14, 2048, 2048), (12, 2048, 11008), (14, 1024, 19072), (14, 11008, 2048),
-                                    (12, 512, 4352)])
+@pytest.mark.parametrize("qt,K,N,quantizer", [(14, 2048, 2048, "reference"), (12, 2048, 11008, "reference"),
+                                              (12, 2048, 11008, "subblock"), (12, 5120, 1024, "subblock"),
+                                              (14, 1024, 19072, "reference"), (14, 11008, 2048, "reference"),
+                                              (12, 512, 4352, "reference"), (12, 256, 4352, "subblock")])
 @pytest.mark.parametrize("M", [1, 2, 3, 4])
-def test_gemv_on_quantized_gaussian_weights(oracle, path, qt, K, N, M):
+def test_gemv_on_quantized_gaussian_weights(oracle, path, qt, K, N, quantizer, M):
     import torch
     from vibrant_b200 import synth
     from vibrant_b200 import tensor as vt
-    wq, wd = _weights(oracle, qt, K, N, seed=K + N + qt)
+    wq, wd = _weights(oracle, qt, K, N, seed=K + N + qt, quantizer=quantizer)
     x = synth.activations(M, K, seed=M + K)
     w = vt.QuantWeight(qt, K, N, wq)
     y = vt.matmul(torch.from_numpy(x).cuda(), w).cpu().numpy()

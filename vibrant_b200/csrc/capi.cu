@@ -430,6 +430,48 @@ int vkq_rms_norm(int device, const float *x, const float *weight, float *out, in
     return check_launch(rms_norm(x, weight, out, rows, n, eps, (cudaStream_t)stream), "rms_norm");
 }
 
+int vkq_linear_fused(int device, int qtype, int nweights, const void *const *w, const int64_t *w_bytes, int64_t K,
+                     const int64_t *N, const float *x, int64_t M, const float *norm_w, float eps, int epilogue,
+                     float *const *y, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (qtype != VKQ_Q4_K) {
+        set_error("vkq_linear_fused serves Q4_K weights (got qtype %d)", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if (!w || !w_bytes || !N || !y || !x || K <= 0 || M < 1 || M > 4 || nweights < 1 ||
+        nweights > kMaxStripSegs || (epilogue != VKQ_EPI_NONE && epilogue != VKQ_EPI_SILU_MUL) ||
+        (epilogue == VKQ_EPI_SILU_MUL && nweights != 2) || (norm_w && (M > 3 || !(eps >= 0.0f)))) {
+        set_error("invalid arguments to vkq_linear_fused");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(norm_w)) & 3u) {
+        set_error("x and norm_w must be 4-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    StripSeg segs[kMaxStripSegs];
+    for (int i = 0; i < nweights; i++) {
+        const bool out = i == 0 || epilogue == VKQ_EPI_NONE;
+        if (!w[i] || N[i] <= 0 || N[i] % 256 != 0 || (out && !y[i])) {
+            set_error("weight %d: null pointer or N=%lld not a positive multiple of 256", i, (long long)N[i]);
+            return VKQ_ERR_INVALID_ARGUMENT;
+        }
+        if (K > (int64_t(1) << 40) / N[i] || w_bytes[i] < K * N[i] / 256 * 144) {
+            set_error("weight %d: buffer of %lld bytes for a [%lld x %lld] Q4_K weight", i, (long long)w_bytes[i],
+                      (long long)K, (long long)N[i]);
+            return VKQ_ERR_INVALID_ARGUMENT;
+        }
+        if ((reinterpret_cast<uintptr_t>(w[i]) & 15u) || (out && (reinterpret_cast<uintptr_t>(y[i]) & 3u))) {
+            set_error("weight %d: weights must be 16-byte and outputs 4-byte aligned", i);
+            return VKQ_ERR_MISALIGNED;
+        }
+        segs[i] = StripSeg{w[i], w_bytes[i], N[i], N[i], 0, out ? y[i] : nullptr, N[i], 0};
+    }
+    const int r = gemv_strip_multi((int)M, K, segs, nweights, epilogue == VKQ_EPI_SILU_MUL, x, norm_w, eps,
+                                   (cudaStream_t)stream, device);
+    return r == 0 ? VKQ_OK : r == 2 ? VKQ_ERR_INVALID_ARGUMENT : r == 3 ? VKQ_ERR_UNSUPPORTED : VKQ_ERR_CUDA;
+}
+
 int vkq_device_status(int device, int *code) {
     int st = enter(device);
     if (st) return st;

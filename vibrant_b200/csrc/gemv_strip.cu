@@ -1,10 +1,18 @@
 // gemv_strip.cu -- Q4_K dequantize + GEMV in column strips on sm_100a, for
 // weights whose stored rows start on a super-block boundary (the N % 256 == 0
-// layers of a transformer and their row-block shards).
+// layers of a transformer and their row-block shards), with the fused forms
+// of a decode step's linears: several weights over one input (q, k and v),
+// gate and up with a SiLU(gate) * up epilogue, and an RMSNorm prologue.
 //
-// y[m][n] = sum_k x[m][k] * W[k][n], 1 <= M <= 4, fp32 accumulate, with the
+// y[m][n] = sum_k h[m][k] * W[k][n], 1 <= M <= 4, fp32 accumulate, with the
 // per-value arithmetic of the CUDA-core GEMV in gemv.cu: the weight
-// w = (d*sc)*q - dmin*m is formed with one rounding, then x*w accumulated.
+// w = (d*sc)*q - dmin*m is formed with one rounding, then h*w accumulated.
+// h = x, or with the prologue h = x / sqrt(mean(x^2) + eps) * g (the
+// reference's rms_norm_f32, internal/gpu/cuda/kernels.cu:209-288, applied by
+// internal/transformer/layer.go before attention and before the FFN): the
+// product is linear in h, so the kernel accumulates (x*g)*w and multiplies
+// each output by 1/rms, the sum of squares coming from the x values the
+// kernel reads anyway.
 // Q4_K layout (internal/tensor/quant_q4k.go:137-157, values as in
 // DequantizeQ4_K, quant_q4k.go:37-79): d, dmin (f16), 12 bytes of 6-bit
 // scales and mins in four little-endian 24-bit groups (sc[0..3], sc[4..7],
@@ -12,28 +20,30 @@
 // nibble for even v).  A 32-value sub-block is therefore 16 contiguous quant
 // bytes under one (scale, min) pair.
 //
-// Design (HBM-bound; algorithmic bytes per call = weight + x + y):
-//  * A lane-column is V consecutive output columns of the launch: one
-//    sub-block (V = 32, 16 quant bytes) or half of one (V = 16, 8 bytes).
-//    The lane-columns are dealt out in contiguous runs to column groups.  A
-//    group is one CTA, or a thread-block cluster of S CTAs that split K into
-//    S ranges and add their sums through distributed shared memory: no
-//    partial sum leaves the SM, so there is no global workspace, atomic or
-//    memory fence, and small matrices finish in one pass of the machine.
+// Design (HBM-bound; algorithmic bytes per call = weights + x + y):
+//  * A lane-column is V consecutive output columns of one weight: one
+//    sub-block (V = 32, 16 quant bytes; M <= 2) or half of one (V = 16,
+//    8 bytes; M >= 3).  The lane-columns of all the launch's weights, in
+//    order (or gate and up alternating, for the SiLU epilogue), are dealt out
+//    in contiguous runs to column groups.  A group is one CTA, or a
+//    thread-block cluster of S CTAs that split K into S ranges and add their
+//    sums through distributed shared memory: no partial sum leaves the SM, so
+//    there is no global workspace, atomic or memory fence, and small matrices
+//    finish in one pass of the machine.
 //  * Thread t of a CTA owns lane-column t % nlc of its group and every R-th
 //    row (R = 512 / nlc) of the CTA's k range.  Per row it copies the
-//    16-byte block header, its quant bytes and x[m][k] into a ring of
+//    16-byte block header, its quant bytes, x[m][k] (and g[k]) into a ring of
 //    kStripDepth slots of its own in shared memory with cp.async (L2 256-byte
 //    prefetch), kStripDepth rows ahead of their use: the bytes in flight take
 //    no registers, and as each thread reads only its own slots, no barrier is
 //    needed (cp.async.wait_group per thread).  Lanes of one warp take
 //    adjacent lane-columns, so a warp's copies cover contiguous runs of each
 //    row.  The first rows' weight bytes are requested before
-//    griddepcontrol.wait (the weight does not depend on the preceding kernel;
+//    griddepcontrol.wait (the weights do not depend on the preceding kernel;
 //    x and y do).
 //  * Per row: d and dmin, the sub-block's 6-bit scale and min (one funnel
 //    shift each out of the header words), then per pair of values one byte
-//    permute per value and two packed fp32x2 FMAs (w, then x*w; the quant is
+//    permute per value and two packed fp32x2 FMAs (w, then h*w; the quant is
 //    used as the subnormal float q * 2^-149 with the multipliers scaled by
 //    powers of two, exactly as in gemv.cu).
 //  * Sums: the CTA's threads add through shared memory in a fixed order
@@ -50,24 +60,33 @@ namespace vkq {
 constexpr int kStripThreads = 512;  // one CTA per SM
 constexpr int kStripMaxCluster = 8;
 constexpr int kStripDepth = 8;      // rows in flight per thread
-constexpr int kStripSlot = 48;      // ring slot: header [0,16), quants [16,32), x[0..M) [32,48)
+constexpr int kStripSlot = 48;      // ring slot: header [0,16), quants [16,32), x[0..M) then g [32,48)
 
 // Multipliers of the subnormal-quant form (the values gemv.cu uses).
 constexpr float kStripScale = 0x1p100f;   // d*sc
 constexpr float kStripDown = 0x1p-49f;    // -dmin*m
 constexpr float kStripXScale = 0x1p49f;   // x
 
+struct StripSegP {
+    const uint8_t *w;  // stored rows of row_bytes each
+    float *y;          // [M][y_ld], columns from col_off
+    int64_t row_bytes, y_ld, col_off;
+    int c0;            // in-block position of the weight's first column (multiple of V)
+    int lane_end;      // one past the weight's last lane-column in the launch's lane order
+};
+
 struct StripParams {
-    const uint8_t *w;  // stored rows of row_blocks super-blocks each
-    const float *x;    // [M][K]
-    float *y;          // [M][y_ld], columns [col_off, col_off + N)
-    int64_t K, y_ld, col_off;
-    int64_t row_bytes;  // bytes per stored row
-    int64_t k_per;      // rows per cluster rank
-    int c0;             // in-block position of the launch's first column (multiple of V)
-    int lanes;          // lane-columns of the launch (N / V)
-    int groups;         // column groups
-    int S;              // CTAs per cluster
+    StripSegP seg[kMaxStripSegs];
+    const float *x;       // [M][K]
+    const float *norm_w;  // RMSNorm weight g[K], or null
+    int64_t K, k_per;     // k_per: rows per cluster rank
+    float eps;
+    int nseg;
+    int silu;             // 1: lanes alternate gate (seg 0) and up (seg 1); y0 = SiLU(gate) * up
+    int lanes;            // lane-columns of the launch
+    int groups;           // column groups
+    int unit;             // lane-columns per indivisible unit (2 for the SiLU pairs)
+    int S;                // CTAs per cluster
 };
 
 // cp.async global -> shared of 16, 8 or 4 bytes; the 16- and 8-byte copies
@@ -101,6 +120,29 @@ __device__ __forceinline__ float ld_dsmem(const float *local, uint32_t rank) {
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
     return v;
 }
+// The cluster's sum of one shared-memory float, in CTA-rank order.
+__device__ __forceinline__ float cluster_sum(const float *local, int S) {
+    if (S == 1) return *local;
+    float s = ld_dsmem(local, 0);
+    for (int r = 1; r < S; r++) s += ld_dsmem(local, (uint32_t)r);
+    return s;
+}
+
+// Weight and in-weight lane-column of launch lane-column gl.
+__device__ __forceinline__ void strip_lane(const StripParams &p, int gl, int &si, int &ll) {
+    if (p.silu) {
+        si = gl & 1;
+        ll = gl >> 1;
+        return;
+    }
+    int start = 0;
+    si = 0;
+    while (si + 1 < p.nseg && gl >= p.seg[si].lane_end) {
+        start = p.seg[si].lane_end;
+        si++;
+    }
+    ll = gl - start;
+}
 
 // The quant words of one lane-column row (V / 8 words of 8 values), read
 // from a ring slot.
@@ -118,31 +160,42 @@ template <> struct QWords<16> {
     __device__ __forceinline__ uint32_t operator[](int i) const { return i == 0 ? v.x : v.y; }
 };
 
-template <int M, int V>
+template <int M> constexpr int strip_v() { return M <= 2 ? 32 : 16; }
+
+template <int M>
 __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const StripParams p) {
+    constexpr int V = strip_v<M>();
     constexpr int D = kStripDepth;
     constexpr int MV = M * V;
-    constexpr int NP = V / 2;  // value pairs per lane-column
+    constexpr int RS = MV + 4;  // padded row of the sums buffer (see below)
+    constexpr int NP = V / 2;   // value pairs per lane-column
     // ring[D][kStripThreads] slots during the main loop; afterwards the same
-    // bytes hold red[kStripThreads][M*V + 4] and red2[kStripThreads]
+    // bytes hold red[kStripThreads][RS] and red2[kStripThreads]
     extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float ssq_cta[4];  // this CTA's share of sum_k x[m][k]^2 (RMSNorm prologue)
     float *red = reinterpret_cast<float *>(smem);
-    float *red2 = red + kStripThreads * (MV + 4);
+    float *red2 = red + kStripThreads * RS;
 
     const int t = threadIdx.x;
     const int S = p.S;
+    const bool norm = p.norm_w != nullptr;
     const int crank = S > 1 ? (int)cluster_ctarank() : 0;
     const int g = (int)(blockIdx.x / (unsigned)S);
-    const int lo = (int)((int64_t)g * p.lanes / p.groups);
-    const int nlc = (int)((int64_t)(g + 1) * p.lanes / p.groups) - lo;
+    const int units = p.lanes / p.unit;
+    const int lo = (int)((int64_t)g * units / p.groups) * p.unit;
+    const int nlc = (int)((int64_t)(g + 1) * units / p.groups) * p.unit - lo;
     const int R = kStripThreads / nlc;  // row groups (threads per lane-column)
     const int lcl = t % nlc, rg = t / nlc;
     const int64_t k0 = (int64_t)crank * p.k_per;
     const int64_t span = (p.K - k0 < p.k_per ? p.K - k0 : p.k_per);
     const int nr = (rg < R && span > rg) ? (int)((span - rg + R - 1) / R) : 0;
+    const bool track_ssq = norm && lcl == 0;  // lane-column 0's threads see every row of the range once
 
-    // this thread's lane-column: block b of the stored row, first value `within`
-    const int pos = p.c0 + (lo + lcl) * V;
+    // this thread's lane-column: weight si, block b of its stored row, first value `within`
+    int si, ll;
+    strip_lane(p, lo + lcl, si, ll);
+    const int64_t row_bytes = p.seg[si].row_bytes;
+    const int pos = p.seg[si].c0 + ll * V;
     const int64_t b = pos >> 8;
     const int within = pos & 255;
     const int j = within >> 5;  // sub-block
@@ -152,9 +205,10 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     const uint32_t s_sc = (uint32_t)(o_sc & 31), s_m = (uint32_t)(o_m & 31);
     const int qoff = 16 + (within >> 1);
 
-    const int64_t step = (int64_t)R * p.row_bytes;
-    const uint8_t *pw = p.w + (k0 + rg) * p.row_bytes + b * 144;  // header of the next row to request
-    const float *px = p.x + k0 + rg;                                // x[0][next row]
+    const int64_t step = (int64_t)R * row_bytes;
+    const uint8_t *pw = p.seg[si].w + (k0 + rg) * row_bytes + b * 144;  // header of the next row to request
+    const float *px = p.x + k0 + rg;                                      // x[0][next row]
+    const float *pg = norm ? p.norm_w + k0 + rg : nullptr;                // g[next row]
     const uint32_t slot0 = smem_u32addr(smem) + (uint32_t)(t * kStripSlot);
     constexpr uint32_t kSlotStride = kStripThreads * kStripSlot;
 
@@ -170,6 +224,10 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
 #pragma unroll
         for (int m = 0; m < M; m++) cp_async_4(a + 4 * m, px + (int64_t)m * p.K);
         px += R;
+        if (norm) {
+            cp_async_4(a + 4 * M, pg);
+            pg += R;
+        }
     };
     // prologue: the weight bytes of the first D rows, then (once the
     // preceding kernel is complete) their x; one commit group per row
@@ -189,6 +247,9 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     for (int m = 0; m < M; m++)
 #pragma unroll
         for (int i = 0; i < NP; i++) acc[m][i] = make_float2(0.f, 0.f);
+    float ssq[M];
+#pragma unroll
+    for (int m = 0; m < M; m++) ssq[m] = 0.f;
 
     for (int i0 = 0; i0 < nr; i0 += D) {
 #pragma unroll
@@ -200,13 +261,17 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
                 QWords<V> q;
                 q.read(a + 16);
                 float xr[M];
-                if constexpr (M == 1) {
-                    xr[0] = __uint_as_float(lds32(a + 32));
-                } else {
-                    const uint4 xq = lds128(a + 32);
-                    const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
+                const uint4 xq = lds128(a + 32);
+                const uint32_t xw[4] = {xq.x, xq.y, xq.z, xq.w};
 #pragma unroll
-                    for (int m = 0; m < M; m++) xr[m] = __uint_as_float(xw[m]);
+                for (int m = 0; m < M; m++) xr[m] = __uint_as_float(xw[m]);
+                if (norm) {
+                    const float gk = __uint_as_float(M == 1 ? xq.y : M == 2 ? xq.z : xq.w);
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        if (track_ssq) ssq[m] = fmaf(xr[m], xr[m], ssq[m]);
+                        xr[m] *= gk;
+                    }
                 }
                 if (i0 + u + D < nr) {  // refill this slot with the row D ahead
                     request_w(u);
@@ -246,15 +311,20 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
 
     // ---- sums over the CTA's row groups ----
     // red[t][m*V + v] with rows padded to RS = MV + 4 floats, so the 16-byte
-    // stores of 8 consecutive threads fall on distinct banks
-    constexpr int RS = MV + 4;
+    // stores of 8 consecutive threads fall on distinct banks; the padding of
+    // lane-column 0's rows carries the sums of squares
     if (rg < R) {
-        float4 *mine = reinterpret_cast<float4 *>(red + t * RS);
+        float *row = red + t * RS;
+        float4 *mine = reinterpret_cast<float4 *>(row);
 #pragma unroll
         for (int m = 0; m < M; m++)
 #pragma unroll
             for (int i = 0; i < NP; i += 2)
                 mine[(m * V + 2 * i) / 4] = make_float4(acc[m][i].x, acc[m][i].y, acc[m][i + 1].x, acc[m][i + 1].y);
+        if (track_ssq) {
+#pragma unroll
+            for (int m = 0; m < M; m++) row[MV + m] = ssq[m];
+        }
     }
     __syncthreads();
     // output e = lcl*MV + mv: the row group r of lane-column lcl wrote it at
@@ -285,46 +355,66 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
             red[at] = s;
         }
     }
+    if (norm && t < M) {
+        float s = 0.f;
+        for (int r = 0; r < R; r++) s += red[r * rstride + MV + t];
+        ssq_cta[t] = s;
+    }
     __syncthreads();
 
     // ---- the cluster's CTAs add their sums in rank order and store y ----
-    const int e_lo = S > 1 ? crank * E / S : 0, e_hi = S > 1 ? (crank + 1) * E / S : E;
     if (S > 1) cluster_sync_all();
-    for (int e = e_lo + t; e < e_hi; e += kStripThreads) {
-        const int lc = e / MV, m = (e % MV) / V, v = e % V;
-        const float *src = red + lc * RS + e % MV;
-        float s;
-        if (S > 1) {
-            s = ld_dsmem(src, 0);
-            for (int r = 1; r < S; r++) s += ld_dsmem(src, (uint32_t)r);
-        } else {
-            s = *src;
+    float inv[M];  // 1 / rms of each row of x (1 without the prologue)
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+        inv[m] = 1.f;
+        if (norm) inv[m] = 1.f / sqrtf(cluster_sum(&ssq_cta[m], S) / (float)p.K + p.eps);
+    }
+    if (!p.silu) {
+        const int e_lo = crank * E / S, e_hi = (crank + 1) * E / S;
+        for (int e = e_lo + t; e < e_hi; e += kStripThreads) {
+            const int lc = e / MV, m = (e % MV) / V, v = e % V;
+            const float s = cluster_sum(red + lc * RS + e % MV, S);
+            int s_i, s_ll;
+            strip_lane(p, lo + lc, s_i, s_ll);
+            const StripSegP &sg = p.seg[s_i];
+            sg.y[(int64_t)m * sg.y_ld + sg.col_off + (int64_t)s_ll * V + v] = s * (M == 1 ? inv[0] : inv[m]);
         }
-        p.y[(int64_t)m * p.y_ld + p.col_off + (int64_t)(lo + lc) * V + v] = s;
+    } else {
+        // gate lane 2i, up lane 2i + 1 of the CTA hold pair i (lo is even)
+        const int E2 = (nlc / 2) * MV;
+        const int e_lo = crank * E2 / S, e_hi = (crank + 1) * E2 / S;
+        for (int e = e_lo + t; e < e_hi; e += kStripThreads) {
+            const int pl = e / MV, mv = e % MV, m = mv / V, v = mv % V;
+            const float sc = M == 1 ? inv[0] : inv[m];
+            const float gv = cluster_sum(red + (2 * pl) * RS + mv, S) * sc;
+            const float uv = cluster_sum(red + (2 * pl + 1) * RS + mv, S) * sc;
+            const StripSegP &sg = p.seg[0];
+            sg.y[(int64_t)m * sg.y_ld + sg.col_off + (int64_t)(lo / 2 + pl) * V + v] = gv / (1.0f + expf(-gv)) * uv;
+        }
     }
     if (S > 1) cluster_sync_all();  // no CTA leaves while the others read its shared memory
 }
 
 // ------------------------------- host side -------------------------------
 struct StripPlan {
-    int V = 0, S = 1, groups = 0, lanes = 0;
+    int V = 0, S = 1, groups = 0, lanes = 0, unit = 1;
     int64_t k_per = 0;
     size_t smem = 0;
 };
 
-static size_t strip_smem(int M, int V) {
+static size_t strip_smem(int M) {
     const size_t ring = (size_t)kStripDepth * kStripThreads * kStripSlot;
-    const size_t sums = (size_t)kStripThreads * (M * V + 5) * sizeof(float);
+    const size_t sums = (size_t)kStripThreads * (M * (M <= 2 ? 32 : 16) + 5) * sizeof(float);
     return ring > sums ? ring : sums;
 }
 
-template <int M, int V> static const void *strip_fn() { return (const void *)gemv_strip_kernel<M, V>; }
-static const void *strip_kernel(int M, int V) {
+static const void *strip_kernel(int M) {
     switch (M) {
-    case 1: return V == 32 ? strip_fn<1, 32>() : strip_fn<1, 16>();
-    case 2: return V == 32 ? strip_fn<2, 32>() : strip_fn<2, 16>();
-    case 3: return strip_fn<3, 16>();
-    default: return strip_fn<4, 16>();
+    case 1: return (const void *)gemv_strip_kernel<1>;
+    case 2: return (const void *)gemv_strip_kernel<2>;
+    case 3: return (const void *)gemv_strip_kernel<3>;
+    default: return (const void *)gemv_strip_kernel<4>;
     }
 }
 
@@ -335,17 +425,17 @@ static cudaError_t strip_prepare(const void *fn, size_t smem) {
 }
 
 // CTAs of clusters of S that the device runs at once (max active clusters x S).
-static int strip_capacity(int M, int V, int S, int device) {
+static int strip_capacity(int M, int S, int device) {
     static std::mutex mu;
-    static int cache[16][5][2][kStripMaxCluster + 1];  // [device][M][V == 32][S], 0 = not asked
+    static int cache[16][5][kStripMaxCluster + 1];  // [device][M][S], 0 = not asked
     const int sms = device_sm_count(device);
     if (S == 1) return sms;
     if (device < 0 || device >= 16) return 0;
     std::lock_guard<std::mutex> lock(mu);
-    int &c = cache[device][M][V == 32][S];
+    int &c = cache[device][M][S];
     if (c == 0) {
-        const void *fn = strip_kernel(M, V);
-        const size_t smem = strip_smem(M, V);
+        const void *fn = strip_kernel(M);
+        const size_t smem = strip_smem(M);
         int n = 0;
         if (strip_prepare(fn, smem) == cudaSuccess) {
             cudaLaunchConfig_t cfg{};
@@ -370,7 +460,8 @@ static int strip_capacity(int M, int V, int S, int device) {
 // Estimated cycles of one launch: the busiest CTA's issue time (thread
 // instructions per lane-column row, 32 threads per warp instruction, four
 // schedulers at ~2/3 issue), or its longest thread's chain of rows, plus
-// fixed costs (DRAM latency and the sums; the cluster barriers).
+// fixed costs (DRAM latency and the sums; the cluster barriers, which grow
+// with the cluster).
 static double strip_cost(int M, int V, int S, int nlc, int64_t rows) {
     const double per_row = V * (2.4 + 0.5 * M) + 34 + 4 * M;
     const double issue = (double)nlc * (double)rows * per_row / (32 * 4 * 0.67);
@@ -379,45 +470,43 @@ static double strip_cost(int M, int V, int S, int nlc, int64_t rows) {
     return (issue > chain ? issue : chain) + 2500 + (S > 1 ? 2000 + 600 * S : 0);
 }
 
-static bool strip_layout_ok(const GemvShape &s, const StripLayout &L, int V) {
-    return s.N % V == 0 && L.rs % 256 == 0 && L.c0 % V == 0 && L.c0 >= 0 && L.c0 < 256 &&
-           L.c0 + s.N <= L.rs && s.N / V < (int64_t(1) << 30);
-}
-
-static StripPlan strip_plan(const GemvShape &s, const StripLayout &L, int device) {
+static StripPlan strip_plan(int M, int64_t K, int64_t lanes, int unit, int device) {
     StripPlan best;
-    if (!gemv_strip_supported(s)) return best;
+    const int V = M <= 2 ? 32 : 16;
+    const int64_t units = lanes / unit;
     double best_cost = 0;
-    // 32-value lane-columns for M <= 2 (measured faster than 16 at every
-    // cluster size); 16 for M >= 3 (the accumulators of 32 would not fit)
-    for (int V : {32, 16}) {
-        if ((V == 32) != (s.M <= 2)) continue;
-        if (!strip_layout_ok(s, L, V)) continue;
-        const int64_t lanes = s.N / V;
-        for (int S = 1; S <= kStripMaxCluster; S++) {
-            if (S > 1 && (kStripMaxCluster % S != 0 && S != 3 && S != 6)) continue;
-            if ((int64_t)S > s.K) break;
-            const int cap = strip_capacity((int)s.M, V, S, device);
-            int64_t groups = cap / S;
-            if (groups <= 0) continue;
-            if (groups > lanes) groups = lanes;
-            const int64_t nlc = (lanes + groups - 1) / groups;
-            if (nlc > kStripThreads) continue;
-            const int64_t k_per = (s.K + S - 1) / S;
-            if ((int64_t)(S - 1) * k_per >= s.K) continue;  // every rank gets rows
-            const double c = strip_cost((int)s.M, V, S, (int)nlc, k_per);
-            if (best.V == 0 || c < best_cost) {
-                best_cost = c;
-                best.V = V;
-                best.S = S;
-                best.groups = (int)groups;
-                best.lanes = (int)lanes;
-                best.k_per = k_per;
-                best.smem = strip_smem((int)s.M, V);
-            }
+    for (int S = 1; S <= kStripMaxCluster; S++) {
+        if (S == 5 || S == 7) continue;
+        if ((int64_t)S > K) break;
+        const int cap = strip_capacity(M, S, device);
+        int64_t groups = cap / S;
+        if (groups <= 0) continue;
+        if (groups > units) groups = units;
+        const int64_t nlc = (units + groups - 1) / groups * unit;
+        if (nlc > kStripThreads) continue;
+        const int64_t k_per = (K + S - 1) / S;
+        if ((int64_t)(S - 1) * k_per >= K) continue;  // every rank gets rows
+        const double c = strip_cost(M, V, S, (int)nlc, k_per);
+        if (best.V == 0 || c < best_cost) {
+            best_cost = c;
+            best.V = V;
+            best.S = S;
+            best.groups = (int)groups;
+            best.lanes = (int)lanes;
+            best.unit = unit;
+            best.k_per = k_per;
+            best.smem = strip_smem(M);
         }
     }
     return best;
+}
+
+// Lane-columns of one weight, or 0 when the layout does not suit the kernel.
+static int64_t strip_lanes(const StripSeg &g, int V) {
+    if (g.N < V || g.N % V != 0 || g.rs % 256 != 0 || g.c0 < 0 || g.c0 >= 256 || g.c0 % V != 0 ||
+        g.c0 + g.N > g.rs || g.N / V >= (int64_t(1) << 28))
+        return 0;
+    return g.N / V;
 }
 
 bool gemv_strip_supported(const GemvShape &s) {
@@ -425,36 +514,67 @@ bool gemv_strip_supported(const GemvShape &s) {
 }
 
 bool gemv_strip_fits(const GemvShape &s, const StripLayout &L, int device) {
-    return strip_plan(s, L, device).V != 0;
+    if (!gemv_strip_supported(s)) return false;
+    const int64_t lanes = strip_lanes(StripSeg{nullptr, 0, s.N, L.rs, L.c0, nullptr, 0, 0}, s.M <= 2 ? 32 : 16);
+    return lanes > 0 && strip_plan((int)s.M, s.K, lanes, 1, device).V != 0;
 }
 
-int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, int64_t w_bytes, const float *x,
-                      float *y, int64_t y_ld, int64_t col_off, cudaStream_t stream, int device) {
-    const StripPlan pl = strip_plan(s, L, device);
-    if (pl.V == 0) {
-        set_error("the column-strip GEMV does not serve this shape or layout");
+int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu, const float *x,
+                     const float *norm_w, float eps, cudaStream_t stream, int device) {
+    const int V = M <= 2 ? 32 : 16;
+    if (M < 1 || M > 4 || nseg < 1 || nseg > kMaxStripSegs || K < 1 || (silu && nseg != 2) ||
+        (norm_w && M > 3)) {
+        set_error("the column-strip GEMV serves 1..%d weights, M <= 4 (M <= 3 with the RMSNorm prologue)",
+                  kMaxStripSegs);
         return 3;
     }
-    const int64_t row_bytes = L.rs / 256 * 144;
-    if (w_bytes < s.K * row_bytes) {
-        set_error("weight buffer too small: %lld bytes for %lld rows of %lld", (long long)w_bytes, (long long)s.K,
-                  (long long)row_bytes);
-        return 2;
-    }
     StripParams p{};
-    p.w = static_cast<const uint8_t *>(w);
+    int64_t lanes = 0;
+    for (int i = 0; i < nseg; i++) {
+        const int64_t n = strip_lanes(segs[i], V);
+        if (n == 0) {
+            set_error("weight %d (N=%lld, row stride %lld values, offset %lld) does not suit the column-strip GEMV", i,
+                      (long long)segs[i].N, (long long)segs[i].rs, (long long)segs[i].c0);
+            return 3;
+        }
+        const int64_t row_bytes = segs[i].rs / 256 * 144;
+        if (segs[i].w_bytes < K * row_bytes) {
+            set_error("weight %d: buffer of %lld bytes for %lld rows of %lld", i, (long long)segs[i].w_bytes,
+                      (long long)K, (long long)row_bytes);
+            return 2;
+        }
+        lanes += n;
+        StripSegP &q = p.seg[i];
+        q.w = static_cast<const uint8_t *>(segs[i].w);
+        q.y = segs[i].y;
+        q.row_bytes = row_bytes;
+        q.y_ld = segs[i].y_ld;
+        q.col_off = segs[i].col_off;
+        q.c0 = (int)segs[i].c0;
+        q.lane_end = (int)lanes;
+    }
+    if (silu && segs[0].N != segs[1].N) {
+        set_error("SiLU(gate) * up needs gate and up of one width (%lld, %lld)", (long long)segs[0].N,
+                  (long long)segs[1].N);
+        return 3;
+    }
+    const StripPlan pl = strip_plan(M, K, lanes, silu ? 2 : 1, device);
+    if (pl.V == 0) {
+        set_error("the column-strip GEMV has no plan for this shape");
+        return 3;
+    }
     p.x = x;
-    p.y = y;
-    p.K = s.K;
-    p.y_ld = y_ld;
-    p.col_off = col_off;
-    p.row_bytes = row_bytes;
+    p.norm_w = norm_w;
+    p.K = K;
     p.k_per = pl.k_per;
-    p.c0 = (int)L.c0;
+    p.eps = eps;
+    p.nseg = nseg;
+    p.silu = silu ? 1 : 0;
     p.lanes = pl.lanes;
     p.groups = pl.groups;
+    p.unit = pl.unit;
     p.S = pl.S;
-    const void *fn = strip_kernel((int)s.M, pl.V);
+    const void *fn = strip_kernel(M);
     cudaError_t e = strip_prepare(fn, pl.smem);
     if (e == cudaSuccess) {
         cudaLaunchConfig_t cfg{};
@@ -483,6 +603,16 @@ int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, i
         return 5;
     }
     return 0;
+}
+
+int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, int64_t w_bytes, const float *x,
+                      float *y, int64_t y_ld, int64_t col_off, cudaStream_t stream, int device) {
+    if (!gemv_strip_supported(s)) {
+        set_error("the column-strip GEMV serves Q4_K with 1 <= M <= 4");
+        return 3;
+    }
+    const StripSeg g{w, w_bytes, s.N, L.rs, L.c0, y, y_ld, col_off};
+    return gemv_strip_multi((int)s.M, s.K, &g, 1, false, x, nullptr, 0.f, stream, device);
 }
 
 }  // namespace vkq

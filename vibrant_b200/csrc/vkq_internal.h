@@ -86,6 +86,19 @@ bool gemv_strip_supported(const GemvShape &s);
 bool gemv_strip_fits(const GemvShape &s, const StripLayout &L, int device);
 int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, int64_t w_bytes, const float *x,
                       float *y, int64_t y_ld, int64_t col_off, cudaStream_t stream, int device);
+// One launch over several Q4_K weights [K, N_i] that share x [M, K]: weight
+// i (layout {rs, c0} as above) writes y_i[m][col_off + n]; with silu two
+// weights of one width (gate, up) write SiLU(gate) * up into y_0; with
+// norm_w the input is RMSNorm(x) * norm_w (row-wise, eps), M <= 3.
+constexpr int kMaxStripSegs = 4;
+struct StripSeg {
+    const void *w;
+    int64_t w_bytes, N, rs, c0;
+    float *y;
+    int64_t y_ld, col_off;
+};
+int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu, const float *x,
+                     const float *norm_w, float eps, cudaStream_t stream, int device);
 
 // bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
 size_t gemm_workspace_bytes(const GemvShape &s, int device);

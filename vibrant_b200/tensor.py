@@ -64,6 +64,26 @@ def workspace(nbytes: int, device: int) -> torch.Tensor | None:
     return ws
 
 
+def linear_fused(x: torch.Tensor, weights: list[QuantWeight], norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+                 silu_mul: bool = False, outs: list[torch.Tensor] | None = None,
+                 stream: torch.cuda.Stream | None = None) -> list[torch.Tensor]:
+    """One launch of vkq_linear_fused: [x @ W_i] (or [SiLU(x @ W_0) * (x @ W_1)]),
+    with x replaced by RMSNorm(x) * norm_w when norm_w is given."""
+    if x.dtype != torch.float32 or x.dim() != 2 or any(w.K != x.shape[1] for w in weights):
+        raise ValueError(f"x must be float32 [M, K] with K = every weight's K, got {tuple(x.shape)}")
+    x = x.contiguous()
+    M = x.shape[0]
+    n_out = 1 if silu_mul else len(weights)
+    if outs is None:
+        outs = [torch.empty((M, weights[i].N), dtype=torch.float32, device=x.device) for i in range(n_out)]
+    st = stream if stream is not None else torch.cuda.current_stream(x.device)
+    vkq.linear_fused(weights[0].qtype, [w.buf.data_ptr() for w in weights], [w.nbytes for w in weights], x.shape[1],
+                     [w.N for w in weights], x.data_ptr(), M, [o.data_ptr() for o in outs],
+                     norm_w.data_ptr() if norm_w is not None else None, eps,
+                     vkq.EPI_SILU_MUL if silu_mul else vkq.EPI_NONE, device=weights[0].device_index, stream=st)
+    return outs
+
+
 def matmul(x: torch.Tensor, w: QuantWeight, out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
            stream: torch.cuda.Stream | None = None, path: str = "auto") -> torch.Tensor:
     """y = x @ W for float32 x [M, K] on the weight's device (vkq_matmul)."""

@@ -47,6 +47,8 @@ SIGNATURES = {
     "vkq_set_gemv_path": (_int, [_int]),
     "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "vkq_linear_fused": (_int, [_int, _int, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64,
+                                ctypes.POINTER(_i64), _vp, _i64, _vp, ctypes.c_float, _int, ctypes.POINTER(_vp), _vp]),
     "vkq_gguf_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "vkq_gguf_close": (_int, [_vp]),
     "vkq_gguf_tensor_count": (_i64, [_vp]),
@@ -220,6 +222,20 @@ def gemv_allgather(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, col_lo:
     pf = (_vp * world)(*peer_flags)
     _check(load().vkq_gemv_allgather(device, qtype, w_ptr, w_bytes, K, N, col_lo, col_hi, x_ptr, M, po, pf, sync_ptr,
                                      world, rank, ws_ptr, ws_bytes, _stream_ptr(stream)))
+
+
+EPI_NONE, EPI_SILU_MUL = 0, 1
+
+
+def linear_fused(qtype: int, w_ptrs: list[int], w_bytes: list[int], K: int, Ns: list[int], x_ptr: int, M: int,
+                 y_ptrs: list[int], norm_w_ptr: int | None = None, eps: float = 1e-6, epilogue: int = EPI_NONE,
+                 device: int = -1, stream=None) -> None:
+    """vkq_linear_fused: several Q4_K weights over one input in one launch,
+    with an optional RMSNorm prologue and the SiLU(gate) * up epilogue."""
+    n = len(w_ptrs)
+    ys = list(y_ptrs) + [0] * (n - len(y_ptrs))
+    _check(load().vkq_linear_fused(device, qtype, n, (_vp * n)(*w_ptrs), (_i64 * n)(*w_bytes), K, (_i64 * n)(*Ns),
+                                   x_ptr, M, norm_w_ptr, eps, epilogue, (_vp * n)(*ys), _stream_ptr(stream)))
 
 
 def shard_columns(N: int, world: int, rank: int) -> tuple[int, int]:
