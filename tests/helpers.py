@@ -111,3 +111,46 @@ def same_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """Bitwise equality with NaN as one class."""
     ab, bb = a.view(np.uint32), b.view(np.uint32)
     return (ab == bb) | (np.isnan(a) & np.isnan(b))
+
+
+def write_gguf(path: str, tensors: list[tuple[str, int, list[int], bytes]], version: int = 3,
+               metadata: bool = True, alignment: int = 32) -> list[int]:
+    """A GGUF file for the loader tests (the container of
+    internal/gguf/parser.go:15-64): magic, version, counts, metadata of every
+    value kind (skipped by the loader), tensor infos (name, dims in file
+    order, GGML type, data offset relative to the data section) and the data
+    section at the end of the infos rounded up to `alignment`.  Returns the
+    relative offsets of the tensors."""
+    import struct
+
+    def s(x: str) -> bytes:
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    kv = []
+    if metadata:
+        kv = [s("general.architecture") + struct.pack("<I", 8) + s("llama"),
+              s("llama.block_count") + struct.pack("<II", 4, 36),
+              s("general.flag") + struct.pack("<IB", 7, 1),
+              s("llama.rope.freq_base") + struct.pack("<If", 6, 10000.0),
+              s("general.big") + struct.pack("<IQ", 10, 1 << 40),
+              s("general.ratio") + struct.pack("<Id", 12, 0.5),
+              s("tokenizer.ggml.tokens") + struct.pack("<IIQ", 9, 8, 3) + s("a") + s("bc") + s("<s>"),
+              s("tokenizer.ggml.scores") + struct.pack("<IIQ", 9, 6, 3) + struct.pack("<3f", 0.1, 0.2, 0.3),
+              s("nested") + struct.pack("<IIQ", 9, 9, 2) + struct.pack("<IQ", 4, 2) + struct.pack("<2I", 1, 2)
+              + struct.pack("<IQ", 8, 1) + s("x")]
+    head = b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(kv)) + b"".join(kv)
+    offsets, rel = [], 0
+    infos = b""
+    for name, ggml_type, dims, data in tensors:
+        offsets.append(rel)
+        infos += s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        infos += struct.pack("<IQ", ggml_type, rel)
+        rel += (len(data) + alignment - 1) // alignment * alignment
+    body = head + infos
+    body += b"\0" * ((-len(body)) % alignment)
+    for (_, _, _, data), off in zip(tensors, offsets):
+        body += data + b"\0" * ((-len(data)) % alignment)
+    with open(path, "wb") as f:
+        f.write(body)
+    return offsets

@@ -43,17 +43,25 @@ def _free_port() -> int:
     (14, 256, 151936, 2),  # wide shards: 64 values per lane; rows straddle blocks
     (14, 2048, 37984, 3),  # shards straddle super-blocks
     (12, 2048, 11008, 4),
+    (12, 2048, 11008, 8),  # column-strip all-gather, shard offsets of 32 .. 224 values into a block
+    (12, 5120, 1024, 2),
     (13, 512, 4160, 2),
     (14, 2048, 151936, 8),
 ])
-def test_allgather_kernel_single_rank(qt, K, N, world):
+@pytest.mark.parametrize("path", ["auto", "simt"])
+def test_allgather_kernel_single_rank(qt, K, N, world, path):
     """The all-gather kernel run as rank 0 of 1 on each rank's shard of a
     `world`-way split: the shard's columns land in the output at their
-    global offset and match the oracle; the other columns stay untouched."""
+    global offset and match the oracle; the other columns stay untouched.
+    (Automatic choice: the column-strip all-gather for Q4_K shards of
+    N % 256 == 0 weights, the CUDA-core one otherwise.)"""
     import torch
     from oracle import kq_oracle
     from vibrant_b200 import synth, vkq
     from vibrant_b200 import tensor as vt
+    if path == "simt" and qt != 12:
+        pytest.skip("the automatic choice is the CUDA-core kernel already")
+    old_path = vkq.set_gemv_path(vkq.GEMV_SIMT if path == "simt" else vkq.GEMV_AUTO)
     wq = synth.weights(qt, K, N, seed=K + N + world)
     wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
     m_max = 4
@@ -81,6 +89,7 @@ def test_allgather_kernel_single_rank(qt, K, N, world):
         assert vkq.device_status(0) == vkq.OK
     finally:
         torch.cuda.synchronize()
+        vkq.set_gemv_path(old_path)
         for p in (out, flags, sync):
             vkq.ipc_free(p)
 
@@ -89,9 +98,11 @@ _PROTOCOL_SCRIPT = textwrap.dedent("""
     import sys, time
     sys.path.insert(0, sys.argv[1])
     import numpy as np, torch
+    from oracle import kq_oracle
     from vibrant_b200 import synth, vkq
     from vibrant_b200 import tensor as vt
     torch.cuda.set_device(0)
+    vkq.set_gemv_path(int(sys.argv[2]))  # 1: the CUDA-core all-gather; 0: automatic (Q4_K: column strips)
     qt, K, N, M = 12, 1024, 4096, 1
     wq = synth.weights(qt, K, N, seed=9)
     world = 2
@@ -131,25 +142,27 @@ _PROTOCOL_SCRIPT = textwrap.dedent("""
     vkq.gemv_allgather(qt, sh1.buf.data_ptr(), sh1.nbytes, K, N, 0, N, x.data_ptr(), M, bufs[:1], flags[:1], sync,
                        1, 0, ws.data_ptr(), ws.numel(), device=0)
     assert vkq.device_status(0) == vkq.OK
-    ref = torch.empty(M, N, device="cuda")
-    w = vt.QuantWeight(qt, K, N, wq)
-    vkq.set_gemv_path(vkq.GEMV_SIMT)   # the CUDA-core kernel: the same plan as the all-gather's
-    vt.matmul(x, w, out=ref)
     torch.cuda.synchronize()
-    assert torch.equal(ref, Y[0]), "reset channel gives a different result"
+    wd = kq_oracle.dequantize(qt, wq)[:K * N].reshape(K, N).astype(np.float64)
+    xv = x.cpu().numpy().astype(np.float64)
+    err = np.max(np.abs(Y[0].cpu().numpy() - xv @ wd) / (np.abs(xv) @ np.abs(wd)))
+    assert err <= 1e-5, ("reset channel", err)
     for p in bufs + flags + [sync]:
         vkq.ipc_free(p)
     print("protocol ok")
 """)
 
 
-def test_absent_peer_times_out_and_the_channel_fails_closed():
-    """A second rank that never arrives (one GPU, a flag nothing sets)."""
+@pytest.mark.parametrize("path", ["simt", "strip"])
+def test_absent_peer_times_out_and_the_channel_fails_closed(path):
+    """A second rank that never arrives (one GPU, a flag nothing sets), on
+    the CUDA-core all-gather and on the column-strip one (the automatic
+    choice for Q4_K shards with block-aligned rows)."""
     import torch
     assert torch.cuda.is_available()
     env = dict(os.environ, VKQ_PEER_WAIT_MS="300")
-    r = subprocess.run([sys.executable, "-c", _PROTOCOL_SCRIPT, ROOT], env=env, capture_output=True, text=True,
-                       timeout=300)
+    r = subprocess.run([sys.executable, "-c", _PROTOCOL_SCRIPT, ROOT, "1" if path == "simt" else "0"], env=env,
+                       capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "protocol ok" in r.stdout, r.stdout + r.stderr
 
 

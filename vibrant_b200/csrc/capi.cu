@@ -484,9 +484,11 @@ int vkq_device_status(int device, int *code) {
     int g = gemv_read_status();
     const int g2 = gemm_read_status();
     const int g3 = gemv_tc_read_status();
+    const int g4 = gemv_strip_read_status();
     if (g == 0) g = g2;
     if (g == 0) g = g3;
-    if (g < 0 || g2 < 0 || g3 < 0) {
+    if (g == 0) g = g4;
+    if (g < 0 || g2 < 0 || g3 < 0 || g4 < 0) {
         set_error("cannot read the device status word");
         return VKQ_ERR_CUDA;
     }

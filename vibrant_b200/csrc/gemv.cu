@@ -42,6 +42,7 @@
 #include <mutex>
 
 #include "kq_device.cuh"
+#include "peer.cuh"
 #include "vkq_internal.h"
 
 namespace vkq {
@@ -142,31 +143,6 @@ __device__ __forceinline__ void store_peers4(const GatherParams &g, bool peers, 
     }
 #pragma unroll 1
     for (int r = 0; r < g.world; r++) *reinterpret_cast<float4 *>(g.peer_y[r] + off) = v;
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *a) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned *a, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
-}
-// Bounded wait until flags f[0..count) all equal seq.  Returns 0 on success,
-// kStatusPeer at once when a flag is beyond seq (a rank is out of step), and
-// kStatusTimeout when the budget runs out.
-__device__ __forceinline__ int wait_flags_eq(const unsigned *f, int count, unsigned seq, uint64_t budget_ns) {
-    const uint64_t t0 = globaltimer_ns();
-    for (;;) {
-        bool all = true;
-        for (int r = 0; r < count; r++) {
-            const int d = (int)(ld_acquire_sys(f + r) - seq);
-            if (d > 0) return kStatusPeer;
-            all = all && d == 0;
-        }
-        if (all) return 0;
-        if (globaltimer_ns() - t0 > budget_ns) return kStatusTimeout;
-        __nanosleep(200);
-    }
 }
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -1054,6 +1030,10 @@ int gemv_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
                 size_t ws_bytes, cudaStream_t stream, int device, const GatherArgs *gather) {
     if (!gather && use_strips(s, device))
         return gemv_strip_launch(s, StripLayout{s.N, 0}, w, w_bytes, x, y, s.N, 0, stream, device);
+    // the all-gather of a Q4_K shard with block-aligned rows: column strips
+    if (gather && g_gemv_path != 1 && g_gemv_path != 2 && s.qtype == kQ4K && s.M <= 4 &&
+        gemv_strip_gather_fits(s, *gather, device))
+        return gemv_strip_gather(s, w, w_bytes, x, *gather, stream, device);
     if (!gather && use_tensor_cores(s, device))
         return gemv_tc_launch(s, TcLayout{s.N, 0, 0}, w, w_bytes, x, y, s.N, ws, ws_bytes, stream, device);
     Plan pl = make_plan(s, device);

@@ -49,13 +49,27 @@
 //  * Sums: the CTA's threads add through shared memory in a fixed order
 //    (rows strided over threads, then the strides), the cluster's CTAs
 //    through DSMEM in CTA-rank order, so results are run-to-run identical.
+//  * Row-sharded all-gather (one weight): the launch computes this rank's
+//    columns from its row-block shard and stores each result into every
+//    rank's output buffer through peer memory, with the channel protocol of
+//    the CUDA-core GEMV (peer.cuh, gemv.cu): CTA 0 posts "started" once the
+//    preceding work is complete, a CTA's stores into other ranks' buffers
+//    wait until every rank has started the call (here only at the end of
+//    the launch, when they have), and the last CTA to finish posts "done"
+//    and waits for every rank's; a wait that runs out or a rank out of step
+//    marks the channel failed, and from then on the launch keeps to its own
+//    buffer.
 #include <cstdint>
 #include <mutex>
 
 #include "kq_device.cuh"
+#include "peer.cuh"
 #include "vkq_internal.h"
 
 namespace vkq {
+
+static __device__ int g_strip_status;
+__device__ __forceinline__ void strip_status(int code) { atomicExch(&g_strip_status, code); }
 
 constexpr int kStripThreads = 512;  // one CTA per SM
 constexpr int kStripMaxCluster = 8;
@@ -73,6 +87,15 @@ struct StripSegP {
     int64_t row_bytes, y_ld, col_off;
     int c0;            // in-block position of the weight's first column (multiple of V)
     int lane_end;      // one past the weight's last lane-column in the launch's lane order
+};
+
+// The all-gather channel of a launch (world == 0: plain stores into seg[].y).
+struct StripGatherP {
+    float *peer_y[kMaxRanks];         // every rank's output buffer (addresses valid on this device)
+    unsigned *peer_flags[kMaxRanks];  // every rank's flag array
+    unsigned *sync;                   // this rank's channel words
+    int world, rank;
+    uint64_t wait_ns;
 };
 
 struct StripParams {
@@ -163,7 +186,7 @@ template <> struct QWords<16> {
 template <int M> constexpr int strip_v() { return M <= 2 ? 32 : 16; }
 
 template <int M>
-__global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const StripParams p) {
+__global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const StripParams p, const StripGatherP gq) {
     constexpr int V = strip_v<M>();
     constexpr int D = kStripDepth;
     constexpr int MV = M * V;
@@ -173,6 +196,7 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     // bytes hold red[kStripThreads][RS] and red2[kStripThreads]
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float ssq_cta[4];  // this CTA's share of sum_k x[m][k]^2 (RMSNorm prologue)
+    __shared__ unsigned chan[2];  // all-gather: this call's number; 2 unchecked, 1 peers ok, 0 own buffer only
     float *red = reinterpret_cast<float *>(smem);
     float *red2 = red + kStripThreads * RS;
 
@@ -240,6 +264,16 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     for (int u = 0; u < D; u++) {
         if (u < nr) request_x(u);
         cp_async_commit();
+    }
+    const bool gather = gq.world > 1;
+    if (gather && t == 0) {
+        const unsigned seq = *reinterpret_cast<volatile unsigned *>(&gq.sync[0]) + 1u;
+        const bool failed = *reinterpret_cast<volatile unsigned *>(&gq.sync[2]) != 0u;
+        if (blockIdx.x == 0 && !failed)
+            for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.rank, seq);
+        if (failed) strip_status(kStatusPeer);
+        chan[0] = seq;
+        chan[1] = failed ? 0u : 2u;
     }
 
     float2 acc[M][NP];
@@ -363,6 +397,30 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     __syncthreads();
 
     // ---- the cluster's CTAs add their sums in rank order and store y ----
+    if (gather) {  // every rank has started this call (it has finished with its buffer's old contents)
+        if (t == 0 && chan[1] == 2u) {
+            const int st = wait_flags_eq(gq.peer_flags[gq.rank], gq.world, chan[0], gq.wait_ns);
+            if (st != 0) {
+                strip_status(st);
+                atomicExch(&gq.sync[2], 1u);
+            }
+            chan[1] = st == 0 ? 1u : 0u;
+        }
+        __syncthreads();
+    }
+    const bool peers = gather && chan[1] == 1u;
+    // an output value into its place: y, or every rank's buffer (only this
+    // rank's when the channel has failed)
+    auto put = [&](const StripSegP &sg, int64_t off, float v) {
+        if (gq.world == 0) {
+            sg.y[off] = v;
+        } else if (!peers) {
+            gq.peer_y[gq.rank][off] = v;
+        } else {
+#pragma unroll 1
+            for (int r = 0; r < gq.world; r++) gq.peer_y[r][off] = v;
+        }
+    };
     if (S > 1) cluster_sync_all();
     float inv[M];  // 1 / rms of each row of x (1 without the prologue)
 #pragma unroll
@@ -378,7 +436,7 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
             int s_i, s_ll;
             strip_lane(p, lo + lc, s_i, s_ll);
             const StripSegP &sg = p.seg[s_i];
-            sg.y[(int64_t)m * sg.y_ld + sg.col_off + (int64_t)s_ll * V + v] = s * (M == 1 ? inv[0] : inv[m]);
+            put(sg, (int64_t)m * sg.y_ld + sg.col_off + (int64_t)s_ll * V + v, s * (M == 1 ? inv[0] : inv[m]));
         }
     } else {
         // gate lane 2i, up lane 2i + 1 of the CTA hold pair i (lo is even)
@@ -390,10 +448,36 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
             const float gv = cluster_sum(red + (2 * pl) * RS + mv, S) * sc;
             const float uv = cluster_sum(red + (2 * pl + 1) * RS + mv, S) * sc;
             const StripSegP &sg = p.seg[0];
-            sg.y[(int64_t)m * sg.y_ld + sg.col_off + (int64_t)(lo / 2 + pl) * V + v] = gv / (1.0f + expf(-gv)) * uv;
+            put(sg, (int64_t)m * sg.y_ld + sg.col_off + (int64_t)(lo / 2 + pl) * V + v, gv / (1.0f + expf(-gv)) * uv);
         }
     }
     if (S > 1) cluster_sync_all();  // no CTA leaves while the others read its shared memory
+    // All-gather: the last CTA to finish tells every rank this rank's shard
+    // is in place (unless the call failed), then waits until every rank's
+    // shard is in its own buffer.
+    if (gather) {
+        __syncthreads();  // every store of this CTA is issued
+        if (t == 0) {
+            __threadfence_system();  // ... and, cumulatively, visible before the count
+            const unsigned old = atomicAdd(&gq.sync[1], 1u);
+            if (old == gridDim.x - 1u) {
+                // every CTA fenced at system scope before counting itself in;
+                // an acquire at GPU scope orders that before the "done" posts
+                __threadfence();
+                gq.sync[1] = 0u;
+                gq.sync[0] = chan[0];
+                if (*reinterpret_cast<volatile unsigned *>(&gq.sync[2]) == 0u) {
+                    for (int r = 0; r < gq.world; r++)
+                        st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, chan[0]);
+                    const int st = wait_flags_eq(gq.peer_flags[gq.rank] + gq.world, gq.world, chan[0], gq.wait_ns);
+                    if (st != 0) {
+                        strip_status(st);
+                        atomicExch(&gq.sync[2], 1u);
+                    }
+                }
+            }
+        }
+    }
 }
 
 // ------------------------------- host side -------------------------------
@@ -520,7 +604,7 @@ bool gemv_strip_fits(const GemvShape &s, const StripLayout &L, int device) {
 }
 
 int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu, const float *x,
-                     const float *norm_w, float eps, cudaStream_t stream, int device) {
+                     const float *norm_w, float eps, cudaStream_t stream, int device, const GatherArgs *gather) {
     const int V = M <= 2 ? 32 : 16;
     if (M < 1 || M > 4 || nseg < 1 || nseg > kMaxStripSegs || K < 1 || (silu && nseg != 2) ||
         (norm_w && M > 3)) {
@@ -574,6 +658,21 @@ int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu
     p.groups = pl.groups;
     p.unit = pl.unit;
     p.S = pl.S;
+    StripGatherP gq{};
+    if (gather) {
+        if (nseg != 1 || silu || gather->world < 1 || gather->world > kMaxRanks) {
+            set_error("the column-strip all-gather serves one weight over 1 to %d ranks", kMaxRanks);
+            return 3;
+        }
+        for (int r = 0; r < gather->world; r++) {
+            gq.peer_y[r] = gather->peer_y[r];
+            gq.peer_flags[r] = gather->peer_flags[r];
+        }
+        gq.sync = gather->sync;
+        gq.world = gather->world;
+        gq.rank = gather->rank;
+        gq.wait_ns = gather->wait_ns;
+    }
     const void *fn = strip_kernel(M);
     cudaError_t e = strip_prepare(fn, pl.smem);
     if (e == cudaSuccess) {
@@ -595,7 +694,7 @@ int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu
         }
         cfg.attrs = a;
         cfg.numAttrs = (unsigned)na;
-        void *args[] = {&p};
+        void *args[] = {&p, &gq};
         e = cudaLaunchKernelExC(&cfg, fn, args);
     }
     if (e != cudaSuccess) {
@@ -612,7 +711,27 @@ int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, i
         return 3;
     }
     const StripSeg g{w, w_bytes, s.N, L.rs, L.c0, y, y_ld, col_off};
-    return gemv_strip_multi((int)s.M, s.K, &g, 1, false, x, nullptr, 0.f, stream, device);
+    return gemv_strip_multi((int)s.M, s.K, &g, 1, false, x, nullptr, 0.f, stream, device, nullptr);
+}
+
+bool gemv_strip_gather_fits(const GemvShape &s, const GatherArgs &g, int device) {
+    // the shard's rows start at one in-block position: every row of the full
+    // weight starts on a block boundary (ld % 256 == 0), or there is one row
+    if ((g.ld & 255) != 0 && s.K != 1) return false;
+    return gemv_strip_fits(s, StripLayout{g.rs, g.n_base & 255}, device);
+}
+
+int gemv_strip_gather(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, const GatherArgs &g,
+                      cudaStream_t stream, int device) {
+    const StripSeg seg{w, w_bytes, s.N, g.rs, g.n_base & 255, g.peer_y[g.rank], g.y_ld, g.col_off};
+    return gemv_strip_multi((int)s.M, s.K, &seg, 1, false, x, nullptr, 0.f, stream, device, &g);
+}
+
+int gemv_strip_read_status() {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_strip_status, sizeof(int)) != cudaSuccess) return -1;
+    cudaMemcpyToSymbol(g_strip_status, &zero, sizeof(int));
+    return v;
 }
 
 }  // namespace vkq

@@ -98,7 +98,14 @@ struct StripSeg {
     int64_t y_ld, col_off;
 };
 int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu, const float *x,
-                     const float *norm_w, float eps, cudaStream_t stream, int device);
+                     const float *norm_w, float eps, cudaStream_t stream, int device,
+                     const GatherArgs *gather = nullptr);
+// The row-sharded all-gather of one Q4_K weight through the column-strip
+// kernel (a row-block shard of an N % 256 == 0 weight; see GatherArgs).
+bool gemv_strip_gather_fits(const GemvShape &s, const GatherArgs &g, int device);
+int gemv_strip_gather(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, const GatherArgs &g,
+                      cudaStream_t stream, int device);
+int gemv_strip_read_status();  // reads and clears the column-strip kernel's device status word
 
 // bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
 size_t gemm_workspace_bytes(const GemvShape &s, int device);
