@@ -41,3 +41,29 @@ def test_noalloc_matches_gemv_twice(qt, K, N, M):
         assert helpers.matmul_error(a, x.cpu().numpy(), wd, y_ref=b.astype(np.float64)) <= helpers.GEMV_TOL
         assert helpers.matmul_error(a, x.cpu().numpy(), wd) <= helpers.GEMV_TOL
     assert vkq.device_status(0) == vkq.OK
+
+
+@pytest.mark.parametrize("qt", [12, 13, 14])
+def test_noalloc_scratch_covers_every_plan(qt):
+    """The fixed 8 MiB scratch holds every GEMV plan on this device: the
+    split-K partials are bounded by the grid (two CTAs per SM x 2 x M x the
+    tile width, plus the 64 KiB counter head), whatever K and N are, so on a
+    148-SM B200 the largest need (M = 8) is about 5.2 MB and the rejection
+    path (VKQ_ERR_WORKSPACE, nothing launched) cannot be reached here.  The
+    extreme shapes below check the bound and run through vkq_gemv_noalloc."""
+    import torch
+    from vibrant_b200 import synth, vkq
+    limit = 8 << 20
+    worst = 0
+    for M in (1, 2, 4, 5, 8):
+        for K, N in ((1, 1 << 20), (64, 262144), (65536, 256), (2048, 151936), (11008, 2048)):
+            worst = max(worst, vkq.matmul_workspace_bytes(qt, M, K, N, device=0))
+    assert 0 < worst <= limit, worst
+    K, N, M = 64, 262144, 8
+    w = torch.from_numpy(synth.weights(qt, K, N, seed=2)).cuda()
+    x = torch.from_numpy(synth.activations(M, K, seed=3)).cuda()
+    y = torch.full((M, N), float("nan"), device="cuda")
+    vkq.gemv_noalloc(qt, w.data_ptr(), w.numel(), K, N, x.data_ptr(), M, y.data_ptr(), device=0)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all().item()
+    assert vkq.device_status(0) == vkq.OK
