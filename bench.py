@@ -420,7 +420,7 @@ def headline(ctx, args):
     return {
         "dt": dt, "e_dt": e_dt, "total": total, "shard_alg": shard_alg, "lo": lo, "hi": hi, "copies": nc,
         "copy_bytes": base.nbytes, "err": err, "clocks": sampler.summary(), "traffic": traffic,
-        "kernel": kname or ("vkq::gemv_kernel<Q4_K,1,32,all-gather>" if gather is not None else
+        "kernel": kname or ("vkq::gemv_strip_kernel<1> (all-gather)" if gather is not None else
                             "vkq::gemv_strip_kernel<1>"),
         "h2d": 4 * K, "d2h": 4 * N,
     }
@@ -553,18 +553,35 @@ def decode_3b(ctx, args):
     st = ctx.stream
     taps = {}
 
-    fused = ctx.world == 1  # one GPU: q|k|v and gate|up(+SiLU) in one launch each, RMSNorm folded in
+    # q|k|v and gate|up(+SiLU) in one launch each, RMSNorm folded in; on
+    # several GPUs q and gate|up are this rank's shards, gathered in the
+    # launch, and k, v whole on every rank
+    fused = True
     qkv_out = [torch.empty(1, n, device=ctx.dev) for n in (m["q_out"], m["kv_out"], m["kv_out"])]
+    g_hidden = norm_w[:m["hidden"]]
+
+    def qkv(x, lay):
+        if chans:
+            return chans["q"].linear_fused(x, [lay["q"].w, lay["k"].w, lay["v"].w], norm_w=g_hidden, eps=1e-6,
+                                           outs=qkv_out[1:], stream=st)
+        return vt.linear_fused(x, [lay["q"].w, lay["k"].w, lay["v"].w], norm_w=g_hidden, eps=1e-6,
+                               outs=qkv_out, stream=st)[0]
+
+    def gate_up(o, lay):
+        if chans:
+            return chans["gate"].linear_fused(o, [lay["gate"].w, lay["up"].w], norm_w=g_hidden, eps=1e-6,
+                                              silu_mul=True, stream=st)
+        vt.linear_fused(o, [lay["gate"].w, lay["up"].w], norm_w=g_hidden, eps=1e-6, silu_mul=True, outs=[act],
+                        stream=st)
+        return act
 
     def token_fused(_i):
         x = x0
         for li, lay in enumerate(layers):
-            q = vt.linear_fused(x, [lay["q"].w, lay["k"].w, lay["v"].w], norm_w=norm_w[:m["hidden"]], eps=1e-6,
-                                outs=qkv_out, stream=st)[0]
+            q = qkv(x, lay)
             o = lay["o"](q)
-            vt.linear_fused(o, [lay["gate"].w, lay["up"].w], norm_w=norm_w[:m["hidden"]], eps=1e-6, silu_mul=True,
-                            outs=[act], stream=st)
-            x = lay["down"](act)
+            a = gate_up(o, lay)
+            x = lay["down"](a)
         vkq.rms_norm(x.data_ptr(), norm_w.data_ptr(), h.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
         return head(h)
 
@@ -594,8 +611,7 @@ def decode_3b(ctx, args):
     with torch.cuda.stream(st):
         vkq.rms_norm(x0.data_ptr(), norm_w.data_ptr(), h.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
         if fused:
-            q = vt.linear_fused(x0, [layers[0]["q"].w, layers[0]["k"].w, layers[0]["v"].w],
-                                norm_w=norm_w[:m["hidden"]], eps=1e-6, stream=st)[0]
+            q = qkv(x0, layers[0])
         else:
             q = layers[0]["q"](h)
     torch.cuda.synchronize(ctx.dev)
@@ -617,11 +633,13 @@ def decode_3b(ctx, args):
             "gbs": round(nbytes / dt / 1e9, 1),
             "hbm_frac_per_gpu": round(nbytes / dt / 1e9 / ctx.world / ctx.hbm, 4),
             "launches_per_token": launches, "parity_layer0_q_max_rel_err": err,
-            "fused": "rms_norm+q|k|v and rms_norm+gate|up+SiLU*up in one launch each (vkq_linear_fused)"
+            "fused": ("rms_norm+q|k|v and rms_norm+gate|up+SiLU*up in one launch each "
+                      + ("(vkq_linear_fused_allgather: q and gate|up sharded and gathered in the launch)"
+                         if chans else "(vkq_linear_fused)"))
             if fused else "none: every linear and elementwise step is its own launch",
             "parallelism": "single GPU" if ctx.world == 1 else
-            f"every linear row-sharded over {ctx.world} GPUs with the all-gather fused into its GEMV "
-            "(k, v replicated)",
+            f"q, o, gate|up, down and the LM head row-sharded over {ctx.world} GPUs with the all-gather fused "
+            "into their launches (k, v replicated)",
             "steps": steps}
 
 
@@ -766,7 +784,7 @@ def run_ours(args):
                    "columns_per_rank": hl["hi"] - hl["lo"],
                    "parallelism": "single GPU" if world == 1 else
                    f"row-sharded output columns over {world} GPUs (each holds its row-block shard only), "
-                   "all-gather fused into the GEMV (stores into every rank's output over NVLink)",
+                   "all-gather fused into the GEMV (flagged-word stores into every other rank's channel over NVLink)",
                    "l2": f"{hl['copies']} rotated weight copies ({hl['copies'] * hl['copy_bytes'] / 1e6:.0f} MB per "
                          "GPU) and the L2 flushed before the timed region"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": ctx.hbm, "unit": "GB/s",

@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define VKQ_ABI_VERSION 2
+#define VKQ_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define VKQ_API __attribute__((visibility("default")))
@@ -243,7 +243,9 @@ VKQ_API int vkq_comm_size(const vkq_comm *comm);
  * float32 [M, N], 16-byte aligned).  Arrays are HOST arrays of `world`
  * entries; workspaces[r] holds vkq_matmul_workspace_bytes(M, K, hi - lo) on
  * device r; streams[r] is a stream of device r.  Launches on every device
- * and returns; 1 <= M <= 8. */
+ * and returns; 1 <= M <= 8.  The first call with a larger M * N grows the
+ * communicator's channel buffers (it synchronizes every device and
+ * allocates: make it before any stream capture). */
 VKQ_API int vkq_gemv_sharded(vkq_comm *comm, int qtype, const void *const *w_shards, const int64_t *w_bytes,
                              int64_t K, int64_t N, const float *const *x, int64_t M, float *const *y,
                              void *const *workspaces, const size_t *workspace_bytes, void *const *streams);
@@ -264,15 +266,37 @@ VKQ_API int vkq_ipc_free(int device, void *ptr);
  * from the rank's row-block shard w (vkq_shard_weight for the same columns,
  * w_bytes >= vkq_shard_bytes) and stored into every rank's output y[M][N].
  * peer_out and peer_flags are HOST arrays of `world` device pointers usable
- * on this device: every rank's output buffer and channel flag array (own
- * entry included); a flag array holds 2 * world uint32 and starts at zero;
- * sync points to this rank's 4 uint32 channel words (zero at first; zero them
- * on every rank, with the flags, to reset a failed channel).
+ * on this device: every rank's output buffer and channel buffer (own entry
+ * included); a channel buffer holds vkq_gather_channel_bytes(M, N) bytes or
+ * more (flag words, then the flagged-word slots through which the Q4_K
+ * column-strip kernel exchanges values) and starts at zero; sync points to
+ * this rank's 4 uint32 channel words (zero at first; zero them on every rank,
+ * with the channel buffers, to reset a failed channel).
  * 1 <= M <= 8; the workspace is vkq_matmul_workspace_bytes(M, K, col_hi - col_lo). */
 VKQ_API int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                                int64_t col_lo, int64_t col_hi, const float *x, int64_t M, void *const *peer_out,
                                void *const *peer_flags, void *sync, int world, int rank, void *workspace,
                                size_t workspace_bytes, void *stream);
+/* Bytes of a channel buffer for outputs of up to m_max rows of N columns:
+ * 256 bytes of flag words, then two 8-byte slots per output element. */
+VKQ_API size_t vkq_gather_channel_bytes(int64_t m_max, int64_t N);
+
+/* vkq_linear_fused on a row-sharded model (Q4_K, N % 256 == 0): w[0] is this
+ * rank's row-block shard of columns [col_lo, col_hi) of a [K, N] weight
+ * (vkq_shard_columns), and its output is all-gathered like
+ * vkq_gemv_allgather's into every rank's peer_out[rank] [M][N];
+ *   VKQ_EPI_NONE:     w[1..] are whole weights [K, N_local[i]] computed on
+ *                     every rank into y_local[i] (k and v beside a sharded q);
+ *   VKQ_EPI_SILU_MUL: nweights == 2, w[1] the shard of the same columns of
+ *                     the up weight; the gathered output is SiLU(gate) * up.
+ * norm_w / eps as in vkq_linear_fused; channel buffers of
+ * vkq_gather_channel_bytes(M, N); 1 <= M <= 4; every rank makes the same
+ * sequence of calls on a channel (vkq_gemv_allgather's protocol). */
+VKQ_API int vkq_linear_fused_allgather(int device, int qtype, int nweights, const void *const *w,
+                                       const int64_t *w_bytes, int64_t K, int64_t N, int64_t col_lo, int64_t col_hi,
+                                       const int64_t *N_local, const float *x, int64_t M, const float *norm_w,
+                                       float eps, int epilogue, float *const *y_local, void *const *peer_out,
+                                       void *const *peer_flags, void *sync, int world, int rank, void *stream);
 
 /* ---- GGUF weights to the device, still quantized ----
  * Replaces the GPU upload route of the reference: ParseGGUF

@@ -386,6 +386,7 @@ int vkq_gemv_allgather(int device, int qtype, const void *w, int64_t w_bytes, in
     g.ld = N;
     g.n_base = col_lo;
     g.wait_ns = peer_wait_ns();
+    g.slot_elems = M * N;  // the channel buffers hold vkq_gather_channel_bytes(M, N) (the contract)
     GemvShape s{qtype, K, col_hi - col_lo, M};
     return gemv_launch(s, w, w_bytes, x, nullptr, workspace, workspace_bytes, (cudaStream_t)stream, device, &g);
 }
@@ -430,6 +431,10 @@ int vkq_rms_norm(int device, const float *x, const float *weight, float *out, in
     return check_launch(rms_norm(x, weight, out, rows, n, eps, (cudaStream_t)stream), "rms_norm");
 }
 
+size_t vkq_gather_channel_bytes(int64_t m_max, int64_t N) {
+    return m_max > 0 && N > 0 ? gather_channel_bytes(m_max, N) : 0;
+}
+
 int vkq_linear_fused(int device, int qtype, int nweights, const void *const *w, const int64_t *w_bytes, int64_t K,
                      const int64_t *N, const float *x, int64_t M, const float *norm_w, float eps, int epilogue,
                      float *const *y, void *stream) {
@@ -469,6 +474,76 @@ int vkq_linear_fused(int device, int qtype, int nweights, const void *const *w, 
     }
     const int r = gemv_strip_multi((int)M, K, segs, nweights, epilogue == VKQ_EPI_SILU_MUL, x, norm_w, eps,
                                    (cudaStream_t)stream, device);
+    return r == 0 ? VKQ_OK : r == 2 ? VKQ_ERR_INVALID_ARGUMENT : r == 3 ? VKQ_ERR_UNSUPPORTED : VKQ_ERR_CUDA;
+}
+
+int vkq_linear_fused_allgather(int device, int qtype, int nweights, const void *const *w, const int64_t *w_bytes,
+                               int64_t K, int64_t N, int64_t col_lo, int64_t col_hi, const int64_t *N_local,
+                               const float *x, int64_t M, const float *norm_w, float eps, int epilogue,
+                               float *const *y_local, void *const *peer_out, void *const *peer_flags, void *sync,
+                               int world, int rank, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (qtype != VKQ_Q4_K) {
+        set_error("vkq_linear_fused_allgather serves Q4_K weights (got qtype %d)", qtype);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    const bool silu = epilogue == VKQ_EPI_SILU_MUL;
+    if (!w || !w_bytes || !x || !sync || !peer_out || !peer_flags || K <= 0 || M < 1 || M > 4 || nweights < 1 ||
+        nweights > kMaxStripSegs || (epilogue != VKQ_EPI_NONE && !silu) || (silu && nweights != 2) ||
+        (!silu && nweights > 1 && (!N_local || !y_local)) || (norm_w && (M > 3 || !(eps >= 0.0f)))) {
+        set_error("invalid arguments to vkq_linear_fused_allgather");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || N <= 0 || N % 256 != 0 || col_lo < 0 ||
+        col_hi > N || col_hi <= col_lo || col_lo % 32 != 0 || col_hi % 32 != 0) {
+        set_error("vkq_linear_fused_allgather: invalid world/rank (%d/%d) or columns [%lld, %lld) of N=%lld "
+                  "(N a multiple of 256, columns of 32)",
+                  world, rank, (long long)col_lo, (long long)col_hi, (long long)N);
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(norm_w)) & 3u) {
+        set_error("x and norm_w must be 4-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    GatherArgs g{};
+    for (int r = 0; r < world; r++) {
+        if (!peer_out[r] || !peer_flags[r]) {
+            set_error("vkq_linear_fused_allgather: null peer buffer for rank %d", r);
+            return VKQ_ERR_INVALID_ARGUMENT;
+        }
+        g.peer_y[r] = static_cast<float *>(peer_out[r]);
+        g.peer_flags[r] = static_cast<unsigned *>(peer_flags[r]);
+    }
+    const int64_t rb = shard_row_blocks(K, N, col_lo, col_hi);
+    StripSeg segs[kMaxStripSegs];
+    for (int i = 0; i < nweights; i++) {
+        const bool shard = i == 0 || silu;
+        const int64_t n_i = shard ? N : N_local[i];
+        const int64_t need = shard ? K * rb * 144 : (n_i > 0 ? K * n_i / 256 * 144 : 0);
+        if (!w[i] || n_i <= 0 || n_i % 256 != 0 || (!shard && !y_local[i]) || w_bytes[i] < need) {
+            set_error("weight %d: null pointer, N not a multiple of 256, or a buffer of %lld bytes (needs %lld)", i,
+                      (long long)w_bytes[i], (long long)need);
+            return VKQ_ERR_INVALID_ARGUMENT;
+        }
+        if ((reinterpret_cast<uintptr_t>(w[i]) & 15u) || (!shard && (reinterpret_cast<uintptr_t>(y_local[i]) & 3u))) {
+            set_error("weight %d: weights must be 16-byte and outputs 4-byte aligned", i);
+            return VKQ_ERR_MISALIGNED;
+        }
+        segs[i] = shard ? StripSeg{w[i], w_bytes[i], col_hi - col_lo, rb * 256, col_lo & 255, g.peer_y[rank], N, col_lo}
+                        : StripSeg{w[i], w_bytes[i], n_i, n_i, 0, y_local[i], n_i, 0};
+    }
+    g.sync = static_cast<unsigned *>(sync);
+    g.world = world;
+    g.rank = rank;
+    g.y_ld = N;
+    g.col_off = col_lo;
+    g.rs = rb * 256;
+    g.ld = N;
+    g.n_base = col_lo;
+    g.wait_ns = peer_wait_ns();
+    g.slot_elems = M * N;  // the channel buffers hold vkq_gather_channel_bytes(M, N) (the contract)
+    const int r = gemv_strip_multi((int)M, K, segs, nweights, silu, x, norm_w, eps, (cudaStream_t)stream, device, &g);
     return r == 0 ? VKQ_OK : r == 2 ? VKQ_ERR_INVALID_ARGUMENT : r == 3 ? VKQ_ERR_UNSUPPORTED : VKQ_ERR_CUDA;
 }
 

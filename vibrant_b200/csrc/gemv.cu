@@ -97,19 +97,21 @@ struct GemvParams {
 // block that straddles two rows or two shards is copied whole and the values
 // outside the row's columns are never read).
 //
-// Protocol (every rank makes the same sequence of calls on one channel):
-//  * seq = sync[0] + 1 is this call's number; CTA 0 posts "started seq" into
-//    every rank's flag array (slot `rank`) once the preceding work on this
-//    rank's stream has completed (after griddepcontrol.wait);
-//  * a CTA stores into other ranks' buffers only after every rank has posted
-//    "started seq" (so each target has finished with the previous contents);
-//    a flag beyond seq, or a wait that runs out, marks the call failed
-//    (sync[2], sticky) and the CTA then stores into its own buffer only;
-//  * the last CTA to finish posts "done seq" to every rank (after a system
-//    fence) unless the call failed, and waits until every rank's "done seq"
-//    is in its own flag array: the kernel's completion means the whole result
-//    is in place.  A failed channel posts nothing more and fails every later
-//    call at once (no waits) until the host resets it.
+// Protocol (every rank makes the same sequence of calls on one channel; the
+// flagged-word exchange of peer.cuh):
+//  * seq = sync[0] + 1 is this call's number (read after
+//    griddepcontrol.wait, once the preceding work is complete);
+//  * every finished output value goes into this rank's output and, as one
+//    64-bit store of (seq, value bits), into its slot in every other rank's
+//    channel buffer;
+//  * at the end every thread of the grid polls a share of this rank's slots
+//    for the other ranks' columns of call seq and copies them into the
+//    output, so the kernel's completion means the whole result is in place;
+//    the last CTA to finish records seq in sync[0];
+//  * a slot of a later call (a rank out of step) or a wait that runs out
+//    marks the channel failed (sync[2], sticky): a failed channel sends and
+//    waits no more, every later call keeps to its own columns and reports
+//    VKQ_ERR_PEER until the host resets it.
 constexpr int kMaxPeers = 8;
 struct GatherParams {
     float *peer_y[kMaxPeers];         // every rank's output buffer (addresses valid on this device)
@@ -123,26 +125,32 @@ struct GatherParams {
 
 __device__ __forceinline__ void set_status(int code) { atomicExch(&g_gemv_status, code); }
 
-// Output stores: the local y, or (all-gather) the same position of every
-// rank's output buffer through peer memory (plain stores over NVLink); only
-// this rank's own buffer when the call has failed (peers == false).
-__device__ __forceinline__ void store_peers(const GatherParams &g, bool peers, int64_t m, int64_t c, float v) {
-    const int64_t off = m * g.y_ld + g.col_off + c;
-    if (!peers) {
-        g.peer_y[g.rank][off] = v;
-        return;
-    }
+// Output stores of the all-gather: this rank's output buffer and, unless
+// the channel has failed (peers == false), the value's slot in every other
+// rank's channel buffer.
+__device__ __forceinline__ void store_peers(const GatherParams &g, bool peers, unsigned seq, int64_t m, int64_t c,
+                                            float v) {
+    g.peer_y[g.rank][m * g.y_ld + g.col_off + c] = v;
+    if (!peers) return;
+    const uint64_t word = ((uint64_t)seq << 32) | __float_as_uint(v);
 #pragma unroll 1
-    for (int r = 0; r < g.world; r++) g.peer_y[r][off] = v;
+    for (int r = 0; r < g.world; r++)
+        if (r != g.rank) st_relaxed_sys_u64(channel_slot(g.peer_flags[r], g.y_ld, m, g.col_off + c, seq), word);
 }
-__device__ __forceinline__ void store_peers4(const GatherParams &g, bool peers, int64_t m, int64_t c, float4 v) {
-    const int64_t off = m * g.y_ld + g.col_off + c;  // 16-byte aligned: widths and offsets are multiples of 32
-    if (!peers) {
-        *reinterpret_cast<float4 *>(g.peer_y[g.rank] + off) = v;
-        return;
-    }
+__device__ __forceinline__ void store_peers4(const GatherParams &g, bool peers, unsigned seq, int64_t m, int64_t c,
+                                             float4 v) {
+    // 16-byte aligned: widths and offsets are multiples of 32
+    *reinterpret_cast<float4 *>(g.peer_y[g.rank] + m * g.y_ld + g.col_off + c) = v;
+    if (!peers) return;
+    const float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll 1
-    for (int r = 0; r < g.world; r++) *reinterpret_cast<float4 *>(g.peer_y[r] + off) = v;
+    for (int r = 0; r < g.world; r++) {
+        if (r == g.rank) continue;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            st_relaxed_sys_u64(channel_slot(g.peer_flags[r], g.y_ld, m, g.col_off + c + i, seq),
+                               ((uint64_t)seq << 32) | __float_as_uint(e[i]));
+    }
 }
 __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -468,50 +476,25 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         }
     }
 
-    // All-gather: this call's number, and (CTA 0) the "started" flag on every
-    // rank.  A CTA's first store into other ranks' buffers waits until every
-    // rank has started this call (so it has finished with the previous
-    // contents).  flag[1] carries seq, flag[2] whether peer stores are allowed.
+    // All-gather: this call's number, and whether the channel failed
+    // earlier (then this rank keeps to its own columns and waits for none).
+    // flag[1] carries seq, flag[2] whether values go to the other ranks.
     unsigned seq = 0;
-    bool peers_checked = !(G && gq.world > 1);
     bool peers_ok = true;
     if (G && gq.world > 1) {
         if (tid == 0) {
-            seq = *reinterpret_cast<volatile unsigned *>(&gq.sync[0]) + 1u;
+            const unsigned sq = *reinterpret_cast<volatile unsigned *>(&gq.sync[0]) + 1u;
             const bool failed = *reinterpret_cast<volatile unsigned *>(&gq.sync[2]) != 0u;
-            if (blockIdx.x == 0 && !failed)
-                for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.rank, seq);
             if (failed) set_status(kStatusPeer);
-            flag[1] = (int)seq;
+            flag[1] = (int)sq;
             flag[2] = failed ? 0 : 1;
         }
         named_bar_sync(1, kNW * 32);
         seq = (unsigned)flag[1];
-        if (!flag[2]) {  // the channel failed earlier: no waits, own buffer only
-            peers_checked = true;
-            peers_ok = false;
-        }
+        peers_ok = flag[2] != 0;
+    } else if (G) {
+        peers_ok = false;  // one rank: its own buffer only
     }
-    // Before this CTA's first store into peers' buffers: every rank has
-    // started this call, or the call is marked failed (sticky) and the CTA
-    // keeps to its own buffer.  Called by every thread of the CTA.
-    auto check_peers = [&]() {
-        if constexpr (G) {
-            if (!peers_checked) {
-                if (tid == 0) {
-                    const int st = wait_flags_eq(gq.peer_flags[gq.rank], gq.world, seq, gq.wait_ns);
-                    if (st != 0) {
-                        set_status(st);
-                        atomicExch(&gq.sync[2], 1u);
-                    }
-                    flag[2] = st == 0 ? 1 : 0;
-                }
-                named_bar_sync(1, kNW * 32);
-                peers_ok = flag[2] != 0;
-                peers_checked = true;
-            }
-        }
-    };
 
     const int64_t first_tile = f0 / K;
     const int64_t last_tile = (f1 - 1) / K;
@@ -597,7 +580,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
             }
         }
         const bool whole = (tile * K >= f0) && ((tile + 1) * K <= f1);
-        if (whole) check_peers();  // first store of this CTA into the ranks' outputs
         named_bar_sync(1, kNW * 32);
         // 3. the slots added in order, stored coalesced
         const int64_t n0 = tile * TN;
@@ -614,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
                 for (int w = 2; w < kNW; w++) sum += red[(w * MR + m) * TN + phys];
             }
             if (whole) {
-                if constexpr (G) store_peers(gq, peers_ok, m, n0 + c, sum);
+                if constexpr (G) store_peers(gq, peers_ok, seq, m, n0 + c, sum);
                 else p.y[(int64_t)m * N + n0 + c] = sum;
             }
             else p.partials[(((int64_t)blockIdx.x * 2 + slot) * MR + m) * TN + c] = sum;
@@ -672,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         const bool peers = peers_ok;
         return [=, &gq, &p](int m, int c, float4 v) {
             if constexpr (G) {
-                store_peers4(gq, peers, m, n0 + c, v);
+                store_peers4(gq, peers, seq, m, n0 + c, v);
             } else {
                 float *yo = p.y + (int64_t)m * N + n0 + c;
                 yo[0] = v.x; yo[1] = v.y; yo[2] = v.z; yo[3] = v.w;
@@ -701,7 +683,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         };
         const int n1 = (int)(c_hi - c_lo + 1);
         if (gl == gh) {
-            check_peers();
             sum_rows(tile, part, n1, to_output(tile));
             named_bar_sync(1, kNW * 32);
             if (tid == 0) atomicExch(cnt1, 0);
@@ -721,7 +702,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
         if (!flag[0]) return;
         __threadfence();
         auto gpart = [&](int j) { return p.gpartials + (size_t)(tile + gl + j) * MR * TN; };
-        check_peers();
         sum_rows(tile, gpart, (int)(gh - gl + 1), to_output(tile));
         named_bar_sync(1, kNW * 32);
         if (tid == 0) atomicExch(&p.counters[tile], 0);
@@ -806,30 +786,32 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvParams p, c
     }
     if (pend_first) combine(first_tile, old_first);
     if (pend_last) combine(last_tile, old_last);
-    // All-gather: the last CTA to finish tells every rank this rank's shard
-    // is in place (unless the call failed), then waits until every rank's
-    // shard is in its own buffer.
+    // All-gather: the other ranks' columns from this rank's slots into its
+    // output (every thread of the grid takes a share), then the last CTA to
+    // finish records the call number.
     if (G && gq.world > 1) {
-        named_bar_sync(1, kNW * 32);  // every store of this CTA is issued
+        if (peers_ok) {
+            const int64_t n_all = gq.y_ld, rest = n_all - N;
+            const int64_t total = (int64_t)p.M * rest;
+            int bad = 0;
+            for (int64_t e = (int64_t)blockIdx.x * kThreads + tid; e < total && bad == 0;
+                 e += (int64_t)p.grid * kThreads) {
+                const int64_t m = e / rest, j = e % rest, n = j < gq.col_off ? j : j + N;
+                float v;
+                bad = wait_slot(channel_slot(gq.peer_flags[gq.rank], n_all, m, n, seq), seq, gq.wait_ns,
+                                &gq.sync[2], &v);
+                if (bad == 0) gq.peer_y[gq.rank][m * n_all + n] = v;
+            }
+            // the first thread to find a fault reports it and marks the
+            // channel failed, which stops every other waiting thread
+            if (bad > 0 && atomicExch(&gq.sync[2], 1u) == 0u) set_status(bad);
+        }
+        named_bar_sync(1, kNW * 32);
         if (tid == 0) {
-            __threadfence_system();   // ... and, cumulatively, visible before the count
             const unsigned old = atomicAdd(&gq.sync[1], 1u);
-            if (old == (unsigned)p.grid - 1u) {
-                // Every CTA fenced at system scope before counting itself in, so
-                // all stores of this call are visible to every GPU by now; an
-                // acquire at GPU scope orders that observation before the
-                // release stores of "done" (no second system fence).
-                __threadfence();
+            if (old == (unsigned)p.grid - 1u) {  // every CTA has read this call's number
                 gq.sync[1] = 0u;
                 gq.sync[0] = seq;
-                if (*reinterpret_cast<volatile unsigned *>(&gq.sync[2]) == 0u) {
-                    for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, seq);
-                    const int st = wait_flags_eq(gq.peer_flags[gq.rank] + gq.world, gq.world, seq, gq.wait_ns);
-                    if (st != 0) {
-                        set_status(st);
-                        atomicExch(&gq.sync[2], 1u);
-                    }
-                }
             }
         }
     }

@@ -49,16 +49,17 @@
 //  * Sums: the CTA's threads add through shared memory in a fixed order
 //    (rows strided over threads, then the strides), the cluster's CTAs
 //    through DSMEM in CTA-rank order, so results are run-to-run identical.
-//  * Row-sharded all-gather (one weight): the launch computes this rank's
-//    columns from its row-block shard and stores each result into every
-//    rank's output buffer through peer memory, with the channel protocol of
-//    the CUDA-core GEMV (peer.cuh, gemv.cu): CTA 0 posts "started" once the
-//    preceding work is complete, a CTA's stores into other ranks' buffers
-//    wait until every rank has started the call (here only at the end of
-//    the launch, when they have), and the last CTA to finish posts "done"
-//    and waits for every rank's; a wait that runs out or a rank out of step
-//    marks the channel failed, and from then on the launch keeps to its own
-//    buffer.
+//  * Row-sharded all-gather (weight 0, or the gate|up pair; further weights
+//    stay whole and local, as k and v of a sharded q): the launch computes
+//    this rank's columns from its row-block shard and sends each value to
+//    every other rank as one 64-bit store of (call number, value bits) into
+//    that rank's channel slots (peer.cuh); then every thread of the grid
+//    polls a share of this rank's slots for the other ranks' columns of this
+//    call and copies them into the output.  No fence, no "started" or
+//    "done" flag: the slot carries its own call number, and two parities per
+//    element suffice because no rank can be two calls ahead of another.  A wait that runs out
+//    or a slot of a later call marks the channel failed (sticky); a failed
+//    channel sends and waits no more and keeps the launch to its own columns.
 #include <cstdint>
 #include <mutex>
 
@@ -89,10 +90,9 @@ struct StripSegP {
     int lane_end;      // one past the weight's last lane-column in the launch's lane order
 };
 
-// The all-gather channel of a launch (world == 0: plain stores into seg[].y).
+// The all-gather channel of a launch (world == 0: none).
 struct StripGatherP {
-    float *peer_y[kMaxRanks];         // every rank's output buffer (addresses valid on this device)
-    unsigned *peer_flags[kMaxRanks];  // every rank's flag array
+    unsigned *peer_flags[kMaxRanks];  // every rank's channel buffer (addresses valid on this device)
     unsigned *sync;                   // this rank's channel words
     int world, rank;
     uint64_t wait_ns;
@@ -266,14 +266,12 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
         cp_async_commit();
     }
     const bool gather = gq.world > 1;
-    if (gather && t == 0) {
+    if (gather && t == 0) {  // this call's number, and whether the channel failed earlier
         const unsigned seq = *reinterpret_cast<volatile unsigned *>(&gq.sync[0]) + 1u;
         const bool failed = *reinterpret_cast<volatile unsigned *>(&gq.sync[2]) != 0u;
-        if (blockIdx.x == 0 && !failed)
-            for (int r = 0; r < gq.world; r++) st_release_sys(gq.peer_flags[r] + gq.rank, seq);
         if (failed) strip_status(kStatusPeer);
         chan[0] = seq;
-        chan[1] = failed ? 0u : 2u;
+        chan[1] = failed ? 0u : 1u;
     }
 
     float2 acc[M][NP];
@@ -397,28 +395,19 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     __syncthreads();
 
     // ---- the cluster's CTAs add their sums in rank order and store y ----
-    if (gather) {  // every rank has started this call (it has finished with its buffer's old contents)
-        if (t == 0 && chan[1] == 2u) {
-            const int st = wait_flags_eq(gq.peer_flags[gq.rank], gq.world, chan[0], gq.wait_ns);
-            if (st != 0) {
-                strip_status(st);
-                atomicExch(&gq.sync[2], 1u);
-            }
-            chan[1] = st == 0 ? 1u : 0u;
-        }
-        __syncthreads();
-    }
     const bool peers = gather && chan[1] == 1u;
-    // an output value into its place: y, or every rank's buffer (only this
-    // rank's when the channel has failed)
-    auto put = [&](const StripSegP &sg, int64_t off, float v) {
-        if (gq.world == 0) {
-            sg.y[off] = v;
-        } else if (!peers) {
-            gq.peer_y[gq.rank][off] = v;
-        } else {
+    const unsigned seq = gather ? chan[0] : 0u;
+    // an output value into its place in y (for the all-gather, weight 0's y
+    // is this rank's output buffer) and, for the gathered weight unless the
+    // channel has failed, into its slot in every other rank's channel buffer
+    auto put = [&](const StripSegP &sg, int m, int64_t col, float v, bool gathered) {
+        const int64_t off = (int64_t)m * sg.y_ld + sg.col_off + col;
+        sg.y[off] = v;
+        if (gathered && peers) {
+            const uint64_t word = ((uint64_t)seq << 32) | __float_as_uint(v);
 #pragma unroll 1
-            for (int r = 0; r < gq.world; r++) gq.peer_y[r][off] = v;
+            for (int r = 0; r < gq.world; r++)
+                if (r != gq.rank) st_relaxed_sys_u64(channel_slot(gq.peer_flags[r], sg.y_ld, m, sg.col_off + col, seq), word);
         }
     };
     if (S > 1) cluster_sync_all();
@@ -436,7 +425,7 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
             int s_i, s_ll;
             strip_lane(p, lo + lc, s_i, s_ll);
             const StripSegP &sg = p.seg[s_i];
-            put(sg, (int64_t)m * sg.y_ld + sg.col_off + (int64_t)s_ll * V + v, s * (M == 1 ? inv[0] : inv[m]));
+            put(sg, m, (int64_t)s_ll * V + v, s * (M == 1 ? inv[0] : inv[m]), s_i == 0);
         }
     } else {
         // gate lane 2i, up lane 2i + 1 of the CTA hold pair i (lo is even)
@@ -448,33 +437,40 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
             const float gv = cluster_sum(red + (2 * pl) * RS + mv, S) * sc;
             const float uv = cluster_sum(red + (2 * pl + 1) * RS + mv, S) * sc;
             const StripSegP &sg = p.seg[0];
-            put(sg, (int64_t)m * sg.y_ld + sg.col_off + (int64_t)(lo / 2 + pl) * V + v, gv / (1.0f + expf(-gv)) * uv);
+            put(sg, m, (int64_t)(lo / 2 + pl) * V + v, gv / (1.0f + expf(-gv)) * uv, true);
         }
     }
     if (S > 1) cluster_sync_all();  // no CTA leaves while the others read its shared memory
-    // All-gather: the last CTA to finish tells every rank this rank's shard
-    // is in place (unless the call failed), then waits until every rank's
-    // shard is in its own buffer.
+    // All-gather: the other ranks' columns from this rank's slots into its
+    // output (every thread of the grid takes a share), then the last CTA to
+    // finish records the call number.
     if (gather) {
-        __syncthreads();  // every store of this CTA is issued
+        if (peers) {
+            // weight 0 (with the SiLU epilogue: the gate|up pair) is the sharded one
+            const StripSegP &sg = p.seg[0];
+            const int64_t width = (int64_t)(p.silu ? p.lanes / 2 : p.seg[0].lane_end) * V;
+            const int64_t n_all = sg.y_ld, rest = n_all - width;
+            const int64_t total = (int64_t)M * rest;
+            int bad = 0;
+            for (int64_t e = (int64_t)blockIdx.x * kStripThreads + t; e < total && bad == 0;
+                 e += (int64_t)gridDim.x * kStripThreads) {
+                const int m = (int)(e / rest);
+                const int64_t j = e % rest, n = j < sg.col_off ? j : j + width;
+                float v;
+                bad = wait_slot(channel_slot(gq.peer_flags[gq.rank], n_all, m, n, seq), seq, gq.wait_ns,
+                                &gq.sync[2], &v);
+                if (bad == 0) sg.y[m * n_all + n] = v;
+            }
+            // the first thread to find a fault reports it and marks the
+            // channel failed, which stops every other waiting thread
+            if (bad > 0 && atomicExch(&gq.sync[2], 1u) == 0u) strip_status(bad);
+        }
+        __syncthreads();
         if (t == 0) {
-            __threadfence_system();  // ... and, cumulatively, visible before the count
             const unsigned old = atomicAdd(&gq.sync[1], 1u);
-            if (old == gridDim.x - 1u) {
-                // every CTA fenced at system scope before counting itself in;
-                // an acquire at GPU scope orders that before the "done" posts
-                __threadfence();
+            if (old == gridDim.x - 1u) {  // every CTA has read this call's number
                 gq.sync[1] = 0u;
                 gq.sync[0] = chan[0];
-                if (*reinterpret_cast<volatile unsigned *>(&gq.sync[2]) == 0u) {
-                    for (int r = 0; r < gq.world; r++)
-                        st_release_sys(gq.peer_flags[r] + gq.world + gq.rank, chan[0]);
-                    const int st = wait_flags_eq(gq.peer_flags[gq.rank] + gq.world, gq.world, chan[0], gq.wait_ns);
-                    if (st != 0) {
-                        strip_status(st);
-                        atomicExch(&gq.sync[2], 1u);
-                    }
-                }
             }
         }
     }
@@ -660,12 +656,14 @@ int gemv_strip_multi(int M, int64_t K, const StripSeg *segs, int nseg, bool silu
     p.S = pl.S;
     StripGatherP gq{};
     if (gather) {
-        if (nseg != 1 || silu || gather->world < 1 || gather->world > kMaxRanks) {
-            set_error("the column-strip all-gather serves one weight over 1 to %d ranks", kMaxRanks);
+        // weight 0 (and for SiLU weight 1) is this rank's shard, gathered;
+        // the other weights are whole and stay local
+        if (gather->world < 1 || gather->world > kMaxRanks ||
+            (gather->world > 1 && gather->slot_elems < (int64_t)M * segs[0].y_ld)) {
+            set_error("the column-strip all-gather serves 1 to %d ranks with channel slots for every output", kMaxRanks);
             return 3;
         }
         for (int r = 0; r < gather->world; r++) {
-            gq.peer_y[r] = gather->peer_y[r];
             gq.peer_flags[r] = gather->peer_flags[r];
         }
         gq.sync = gather->sync;
@@ -715,6 +713,8 @@ int gemv_strip_launch(const GemvShape &s, const StripLayout &L, const void *w, i
 }
 
 bool gemv_strip_gather_fits(const GemvShape &s, const GatherArgs &g, int device) {
+    // the channel buffers hold a slot pair for every output element
+    if (g.world > 1 && g.slot_elems < s.M * g.y_ld) return false;
     // the shard's rows start at one in-block position: every row of the full
     // weight starts on a block boundary (ld % 256 == 0), or there is one row
     if ((g.ld & 255) != 0 && s.K != 1) return false;

@@ -65,9 +65,34 @@ using namespace vkq;
 struct vkq_comm {
     int world;
     int dev[kMaxRanks];
-    unsigned *flags[kMaxRanks];  // per device: 2 * world words (started, done)
+    unsigned *flags[kMaxRanks];  // per device: channel buffer (flag words, then flagged-word slots)
     unsigned *sync[kMaxRanks];   // per device: channel words (last call, finished CTAs, failed)
+    size_t chan_bytes;           // bytes of each channel buffer
 };
+
+// Grows every device's channel buffer to hold the slots of an [M][N]
+// output (zero-filled; between calls, never inside a stream capture).
+static int comm_reserve(vkq_comm *c, int64_t M, int64_t N) {
+    const size_t need = gather_channel_bytes(M, N);
+    if (need <= c->chan_bytes) return VKQ_OK;
+    for (int i = 0; i < c->world; i++) {
+        cudaError_t e = cudaSetDevice(c->dev[i]);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaFree(c->flags[i]);
+        if (e == cudaSuccess) {
+            c->flags[i] = nullptr;
+            e = cudaMalloc(&c->flags[i], need);
+        }
+        if (e == cudaSuccess) e = cudaMemset(c->flags[i], 0, need);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) {
+            set_error("growing the channel buffer on device %d: %s", c->dev[i], cudaGetErrorString(e));
+            return VKQ_ERR_CUDA;
+        }
+    }
+    c->chan_bytes = need;
+    return VKQ_OK;
+}
 
 extern "C" {
 
@@ -152,6 +177,7 @@ int vkq_comm_init(int world, const int *devices, vkq_comm **comm) {
             }
     vkq_comm *c = new vkq_comm();
     c->world = world;
+    c->chan_bytes = 256 + 8 * (size_t)world;
     cudaError_t e = cudaSuccess;
     for (int i = 0; i < world && e == cudaSuccess; i++) {
         c->dev[i] = devices[i];
@@ -214,7 +240,7 @@ int vkq_comm_reset(vkq_comm *comm) {
     for (int i = 0; i < comm->world; i++) {
         cudaError_t e = cudaSetDevice(comm->dev[i]);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
-        if (e == cudaSuccess) e = cudaMemset(comm->flags[i], 0, 256 + 8 * (size_t)comm->world);
+        if (e == cudaSuccess) e = cudaMemset(comm->flags[i], 0, comm->chan_bytes);
         if (e == cudaSuccess) e = cudaMemset(comm->sync[i], 0, 256);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) {
@@ -275,6 +301,8 @@ int vkq_gemv_sharded(vkq_comm *comm, int qtype, const void *const *w_shards, con
             return VKQ_ERR_INVALID_ARGUMENT;
         }
     }
+    const int rs = comm_reserve(comm, M, N);
+    if (rs) return rs;
     for (int r = 0; r < world; r++) {
         int64_t lo, hi;
         plan_columns(N, world, r, lo, hi);
@@ -303,6 +331,7 @@ int vkq_gemv_sharded(vkq_comm *comm, int qtype, const void *const *w_shards, con
         g.ld = N;
         g.n_base = lo;
         g.wait_ns = peer_wait_ns();
+        g.slot_elems = (int64_t)((comm->chan_bytes - 256) / 16);
         GemvShape s{qtype, K, hi - lo, M};
         const int st = gemv_launch(s, w_shards[r], w_bytes[r], x[r], nullptr, workspaces[r], workspace_bytes[r],
                                    (cudaStream_t)streams[r], comm->dev[r], &g);

@@ -41,7 +41,13 @@ struct GatherArgs {
     int64_t y_ld, col_off;
     int64_t rs, ld, n_base;
     uint64_t wait_ns;
+    // output elements (m, n) the channel buffers' flagged-word slots hold
+    // (0: none; the column-strip all-gather needs M * y_ld)
+    int64_t slot_elems;
 };
+// Bytes of a channel buffer (flag words, then two 8-byte slots per output
+// element of an [m_max][N] output).
+inline size_t gather_channel_bytes(int64_t m_max, int64_t N) { return 256 + (size_t)m_max * (size_t)N * 16; }
 // Budget of each wait on peer ranks (ns): VKQ_PEER_WAIT_MS, default 2000 ms.
 uint64_t peer_wait_ns();
 // Block slots per row of the row-block shard of columns [lo, hi).

@@ -208,11 +208,14 @@ class PeerGather:
 
     Rank r holds ShardedWeight(..., world, r) and computes output columns
     vkq_shard_columns(N, world, r); the kernel stores them into every rank's
-    output [m_max, N].  Each rank allocates its output and a flag array with
-    vkq_ipc_alloc, the 64-byte handles are exchanged over the group and every
-    rank maps every other rank's buffers (vkq_ipc_open).  `gemv` then leaves
-    the whole x @ W in `out` on every rank, with no collective library call on
-    the data path.  Every rank must make the same sequence of calls."""
+    output [m_max, N] (the CUDA-core kernel), or sends them into every rank's
+    channel buffer as flagged words that each rank copies into its own output
+    (the Q4_K column-strip kernel).  Each rank allocates its output and its
+    channel buffer (vkq_gather_channel_bytes(m_max, N)) with vkq_ipc_alloc,
+    the 64-byte handles are exchanged over the group and every rank maps
+    every other rank's buffers (vkq_ipc_open).  `gemv` then leaves the whole
+    x @ W in `out` on every rank, with no collective library call on the data
+    path.  Every rank must make the same sequence of calls."""
 
     def __init__(self, group, rank: int, world: int, device: int, N: int, m_max: int = 8):
         import torch.distributed as dist
@@ -223,7 +226,8 @@ class PeerGather:
             raise ValueError(f"N={N} leaves a rank of {world} without columns")
         self.group, self.rank, self.world, self.device, self.N, self.m_max = group, rank, world, device, N, m_max
         self.out_ptr, h_out = vkq.ipc_alloc(m_max * N * 4, device)
-        self.flags_ptr, h_flags = vkq.ipc_alloc(max(256, 8 * world), device)
+        self.chan_bytes = vkq.gather_channel_bytes(m_max, N)
+        self.flags_ptr, h_flags = vkq.ipc_alloc(self.chan_bytes, device)
         self.sync_ptr, _ = vkq.ipc_alloc(256, device)
         handles: list = [None] * world
         dist.all_gather_object(handles, (h_out, h_flags), group=group)
@@ -239,7 +243,7 @@ class PeerGather:
             self.peer_out.append(po)
             self.peer_flags.append(pf)
         self.out = torch.as_tensor(_DeviceArray(self.out_ptr, (m_max, N)), device=f"cuda:{device}")
-        self.flag_words = torch.as_tensor(_DeviceArray(self.flags_ptr, (2 * world,), "<u4"),
+        self.flag_words = torch.as_tensor(_DeviceArray(self.flags_ptr, (self.chan_bytes // 4,), "<u4"),
                                           device=f"cuda:{device}")
         self.sync_words = torch.as_tensor(_DeviceArray(self.sync_ptr, (4,), "<u4"), device=f"cuda:{device}")
 
@@ -261,6 +265,33 @@ class PeerGather:
                            self.peer_out, self.peer_flags, self.sync_ptr, self.world, self.rank,
                            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
                            device=self.device, stream=st)
+        return self.out[:M]
+
+    def linear_fused(self, x: torch.Tensor, weights: list, norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+                     silu_mul: bool = False, outs: list[torch.Tensor] | None = None,
+                     stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """vkq_linear_fused_allgather: weights[0] (and weights[1] with
+        silu_mul) is this rank's ShardedWeight of the group's N columns,
+        gathered into `out`; further weights are whole QuantWeights computed
+        here into outs[i - 1].  Returns out[:M] (SiLU(gate) * up with
+        silu_mul)."""
+        w0 = weights[0]
+        if w0.N != self.N or (w0.world, w0.rank) != (self.world, self.rank):
+            raise ValueError("weights[0] is not this rank's shard of the group's columns")
+        M = x.shape[0]
+        if M > self.m_max or x.dtype != torch.float32:
+            raise ValueError("x does not match the group")
+        x = x.contiguous()
+        local = [] if silu_mul else weights[1:]
+        if outs is None:
+            outs = [torch.empty((M, w.N), dtype=torch.float32, device=x.device) for w in local]
+        st = stream if stream is not None else torch.cuda.current_stream(x.device)
+        vkq.linear_fused_allgather(
+            w0.qtype, [w.buf.data_ptr() for w in weights], [w.nbytes for w in weights], w0.K, self.N, w0.lo, w0.hi,
+            [0] + [w.N for w in local], x.data_ptr(), M, [0] + [o.data_ptr() for o in outs],
+            self.peer_out, self.peer_flags, self.sync_ptr, self.world, self.rank,
+            norm_w.data_ptr() if norm_w is not None else None, eps,
+            vkq.EPI_SILU_MUL if silu_mul else vkq.EPI_NONE, device=self.device, stream=st)
         return self.out[:M]
 
     def reset(self) -> None:

@@ -45,6 +45,11 @@ SIGNATURES = {
     "vkq_gemv_allgather": (_int, [_int, _int, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _int,
                                   _int, _vp, _sz, _vp]),
     "vkq_set_gemv_path": (_int, [_int]),
+    "vkq_gather_channel_bytes": (_sz, [_i64, _i64]),
+    "vkq_linear_fused_allgather": (_int, [_int, _int, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64, _i64,
+                                          _i64, _i64, ctypes.POINTER(_i64), _vp, _i64, _vp, ctypes.c_float, _int,
+                                          ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_vp), _vp, _int,
+                                          _int, _vp]),
     "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "vkq_linear_fused": (_int, [_int, _int, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64,
@@ -236,6 +241,29 @@ def linear_fused(qtype: int, w_ptrs: list[int], w_bytes: list[int], K: int, Ns: 
     ys = list(y_ptrs) + [0] * (n - len(y_ptrs))
     _check(load().vkq_linear_fused(device, qtype, n, (_vp * n)(*w_ptrs), (_i64 * n)(*w_bytes), K, (_i64 * n)(*Ns),
                                    x_ptr, M, norm_w_ptr, eps, epilogue, (_vp * n)(*ys), _stream_ptr(stream)))
+
+
+def linear_fused_allgather(qtype: int, w_ptrs: list[int], w_bytes: list[int], K: int, N: int, col_lo: int,
+                           col_hi: int, n_local: list[int], x_ptr: int, M: int, y_local: list[int],
+                           peer_out: list[int], peer_flags: list[int], sync_ptr: int, world: int, rank: int,
+                           norm_w_ptr: int | None = None, eps: float = 1e-6, epilogue: int = EPI_NONE,
+                           device: int = -1, stream=None) -> None:
+    """vkq_linear_fused_allgather: weight 0 (or the gate|up pair) is this
+    rank's shard of columns [col_lo, col_hi), gathered into every rank's
+    output; further weights are whole and local (n_local / y_local, entry 0
+    unused)."""
+    n = len(w_ptrs)
+    nl = list(n_local) + [0] * (n - len(n_local))
+    yl = list(y_local) + [0] * (n - len(y_local))
+    _check(load().vkq_linear_fused_allgather(device, qtype, n, (_vp * n)(*w_ptrs), (_i64 * n)(*w_bytes), K, N,
+                                             col_lo, col_hi, (_i64 * n)(*nl), x_ptr, M, norm_w_ptr, eps, epilogue,
+                                             (_vp * n)(*yl), (_vp * world)(*peer_out), (_vp * world)(*peer_flags),
+                                             sync_ptr, world, rank, _stream_ptr(stream)))
+
+
+def gather_channel_bytes(m_max: int, N: int) -> int:
+    """vkq_gather_channel_bytes: size of an all-gather channel buffer."""
+    return int(load().vkq_gather_channel_bytes(m_max, N))
 
 
 def shard_columns(N: int, world: int, rank: int) -> tuple[int, int]:
