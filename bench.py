@@ -678,15 +678,37 @@ def sweep_14b(ctx, args):
                     lin = Linear(ctx, qt, K, N, seed=7000 * li + j, M=M, channel="gemm", bounds=block_bounds(N))
                 else:
                     lin = Linear(ctx, qt, K, N, seed=7000 * li + j, M=M, channel=chans.get(N), replicate=rep)
-                lay.append((K, lin))
+                lay.append((K, lin, role))
             layers.append(lay)
         xs = {K: torch.from_numpy(synth.activations(M, K, seed=K + M)).to(ctx.dev)
               for K in (m["hidden"], m["q_out"], m["ffn"])}
         gathered = {}
+        # M == 1: the decode step's fused launches (q|k|v in one, gate|up with
+        # SiLU * up in one; sharded and gathered in the launch at N > 1)
+        fused = M == 1
+        kv_outs = [torch.empty(M, m["kv_out"], device=ctx.dev) for _ in range(2)]
+        act = torch.empty(M, m["ffn"], device=ctx.dev)
+
+        def fused_layer(lay):
+            r = {role: lin for _, lin, role in lay}
+            h, f = m["hidden"], m["ffn"]
+            if chans:
+                chans[m["q_out"]].linear_fused(xs[h], [r["q"].w, r["k"].w, r["v"].w], outs=kv_outs, stream=ctx.stream)
+                r["o"](xs[m["q_out"]])
+                chans[f].linear_fused(xs[h], [r["gate"].w, r["up"].w], silu_mul=True, stream=ctx.stream)
+            else:
+                vt.linear_fused(xs[h], [r["q"].w, r["k"].w, r["v"].w], outs=[r["q"].out] + kv_outs,
+                                stream=ctx.stream)
+                r["o"](xs[m["q_out"]])
+                vt.linear_fused(xs[h], [r["gate"].w, r["up"].w], silu_mul=True, outs=[act], stream=ctx.stream)
+            r["down"](xs[f])
 
         def step(_i):
             for lay in layers:
-                for K, lin in lay:
+                if fused:
+                    fused_layer(lay)
+                    continue
+                for K, lin, _ in lay:
                     y = lin(xs[K])
                     if lin.channel == "gemm":
                         maxw = -(-lin.N // 256 // ctx.world) * 256
@@ -723,7 +745,8 @@ def sweep_14b(ctx, args):
             "ms_per_step": round(dt * 1e3, 4), "tokens_per_s": round(M / dt, 1), "gbs": round(gbs, 1),
             "tflops": round(tf, 2), "hbm_frac_per_gpu": round(gbs / ctx.world / ctx.hbm, 4),
             "tensor_frac_per_gpu": round(tf / ctx.world / ctx.bf16, 4),
-            "path": ("fp32 GEMV" + (" + fused peer all-gather" if ctx.world > 1 else "")) if M <= 8 else
+            "path": ("fp32 GEMV" + (" + fused peer all-gather" if ctx.world > 1 else "")
+                     + (", q|k|v and gate|up+SiLU*up fused (4 launches per layer)" if fused else "")) if M <= 8 else
             ("tcgen05 GEMM" + (" + NCCL all-gather" if ctx.world > 1 else ""))}
         for c in chans.values():
             c.close()
