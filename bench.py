@@ -55,6 +55,8 @@ def parse():
     ap.add_argument("--only", default=None, help="comma list of secondary workloads to run (default: all)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="CPU baseline sample budget")
     ap.add_argument("--probe", default=None, help="QTYPE,K,N,M[,COPIES]: time one workload (profiling)")
+    ap.add_argument("--probe-fused", default=None, choices=["qkv", "gate_up"],
+                    help="time one fused launch of the 3B layer (RMSNorm + q|k|v, or RMSNorm + gate|up + SiLU*up)")
     ap.add_argument("--gemv", default="auto", choices=["auto", "simt", "tc", "strip"],
                     help="GEMV kernel for M <= 8 (vkq_set_gemv_path): automatic, CUDA cores, tensor cores or "
                          "Q4_K column strips")
@@ -870,6 +872,53 @@ def run_probe(args):
           f"{2 * M * K * N / dt / 1e12:.1f} TFLOP/s  status={vkq.device_status(0)}", flush=True)
 
 
+def run_probe_fused(args):
+    """One fused launch of the 3B layer (vkq_linear_fused, RMSNorm prologue)
+    over rotated weight copies, CUDA-event time per launch of a graph
+    replay of --steps launches."""
+    import torch
+    from vibrant_b200 import synth, vkq
+    from vibrant_b200 import tensor as vt
+    m = synth.MODEL_3B
+    K = m["hidden"]
+    widths = (m["q_out"], m["kv_out"], m["kv_out"]) if args.probe_fused == "qkv" else (m["ffn"], m["ffn"])
+    silu = args.probe_fused == "gate_up"
+    torch.cuda.set_device(0)
+    one = sum(synth.n_blocks(K, n) * synth.BLOCK_BYTES[vkq.Q4_K] for n in widths)
+    copies = max(2, -(-(512 << 20) // one))
+    sets = [[vt.QuantWeight(vkq.Q4_K, K, n, synth.weights_device(vkq.Q4_K, K, n, 100 * c + i, 0))
+             for i, n in enumerate(widths)] for c in range(copies)]
+    x = torch.from_numpy(synth.activations(1, K, seed=2)).cuda()
+    g = torch.ones(K, device="cuda")
+    outs = [torch.empty(1, widths[0], device="cuda")] if silu else [torch.empty(1, n, device="cuda") for n in widths]
+    st = torch.cuda.Stream()
+
+    def launch(i):
+        vt.linear_fused(x, sets[i % copies], norm_w=g, eps=1e-6, silu_mul=silu, outs=outs, stream=st)
+
+    with torch.cuda.stream(st):
+        for i in range(3):
+            launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
+        for i in range(args.steps):
+            launch(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        graph.replay()
+        st.synchronize()
+        e0.record(st)
+        graph.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3 / args.steps
+    b = one + 4 * K + 4 * (widths[0] if silu else sum(widths)) + 4 * K
+    print(f"fused {args.probe_fused} 2048 -> {'+'.join(map(str, widths))}: {dt * 1e6:.2f} us/launch  "
+          f"{b / dt / 1e9:.1f} GB/s ({copies} weight sets)  status={vkq.device_status(0)}", flush=True)
+
+
 def main():
     args = parse()
     if args.gemv != "auto" and args.impl == "ours":
@@ -877,6 +926,8 @@ def main():
         vkq.set_gemv_path({"simt": vkq.GEMV_SIMT, "tc": vkq.GEMV_TC, "strip": vkq.GEMV_STRIP}[args.gemv])
     if args.probe:
         run_probe(args)
+    elif args.probe_fused:
+        run_probe_fused(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
