@@ -74,7 +74,12 @@ __device__ __forceinline__ void strip_status(int code) { atomicExch(&g_strip_sta
 
 constexpr int kStripThreads = 512;  // one CTA per SM
 constexpr int kStripMaxCluster = 8;
-constexpr int kStripDepth = 8;      // rows in flight per thread
+// Rows in flight per thread.  Measured on the 3B/14B shapes with 8, 6, 4, 3
+// and 2: the shallowest ring was fastest nearly everywhere (2048 -> 11008:
+// 13.6 -> 10.7 us; 3B decode step 496 -> 529 tokens/s) -- a smaller prologue
+// on the critical path of CTAs that start late, and more of the SM's memory
+// left to L1.
+constexpr int kStripDepth = 2;
 constexpr int kStripSlot = 48;      // ring slot: header [0,16), quants [16,32), x[0..M) then g [32,48)
 
 // Multipliers of the subnormal-quant form (the values gemv.cu uses).
@@ -149,6 +154,22 @@ __device__ __forceinline__ float cluster_sum(const float *local, int S) {
     float s = ld_dsmem(local, 0);
     for (int r = 1; r < S; r++) s += ld_dsmem(local, (uint32_t)r);
     return s;
+}
+
+// Sum of n floats a[0], a[stride], ... in four interleaved partial sums (the
+// loads of one pass are independent, so they overlap instead of waiting on
+// each other); a fixed order for a given n.
+__device__ __forceinline__ float strided_sum(const float *a, int n, int stride) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+        s0 += a[(i + 0) * stride];
+        s1 += a[(i + 1) * stride];
+        s2 += a[(i + 2) * stride];
+        s3 += a[(i + 3) * stride];
+    }
+    for (; i < n; i++) s0 += a[i * stride];
+    return (s0 + s1) + (s2 + s3);
 }
 
 // Weight and in-weight lane-column of launch lane-column gl.
@@ -368,30 +389,16 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     if (P == 1) {
         for (int e = t; e < E; e += kStripThreads) {
             const int at = (e / MV) * RS + e % MV;
-            float s = 0.f;
-            for (int r = 0; r < R; r++) s += red[r * rstride + at];
-            red[at] = s;
+            red[at] = strided_sum(red + at, R, rstride);
         }
     } else {
         const int e = t % E, part = t / E;
         const int at = (e / MV) * RS + e % MV;
-        if (part < P) {
-            float s = 0.f;
-            for (int r = part; r < R; r += P) s += red[r * rstride + at];
-            red2[part * E + e] = s;
-        }
+        if (part < P) red2[part * E + e] = strided_sum(red + part * rstride + at, (R - part + P - 1) / P, P * rstride);
         __syncthreads();
-        if (t < E) {
-            float s = 0.f;
-            for (int q = 0; q < P; q++) s += red2[q * E + t];
-            red[at] = s;
-        }
+        if (t < E) red[at] = strided_sum(red2 + t, P, E);
     }
-    if (norm && t < M) {
-        float s = 0.f;
-        for (int r = 0; r < R; r++) s += red[r * rstride + MV + t];
-        ssq_cta[t] = s;
-    }
+    if (norm && t < M) ssq_cta[t] = strided_sum(red + MV + t, R, rstride);
     __syncthreads();
 
     // ---- the cluster's CTAs add their sums in rank order and store y ----
