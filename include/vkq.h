@@ -114,10 +114,24 @@ VKQ_API int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, in
                const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
                void *stream);
 
+/* vkq_matmul for a caller whose activations live in host memory (the
+ * reference's MatMul on a CPU activation and a device weight: the upload of
+ * x, the product, the download of y, as Tensor.ToDevice / EnsureCPUData do
+ * around matmulGPU, internal/tensor/tensor_cuda_api.go and
+ * internal/tensor/tensor.go:482-524): copies x_host [M, K] into the device
+ * buffer x_dev, runs vkq_matmul into the device buffer y_dev and copies it
+ * to y_host [M, N], all enqueued on `stream` (one cudaMemcpyAsync per copy;
+ * pinned host buffers make the call asynchronous).  Same arguments and
+ * errors as vkq_matmul otherwise. */
+VKQ_API int vkq_matmul_host(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+                            const float *x_host, int64_t M, float *y_host, float *x_dev, float *y_dev,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
 /* The fp32-class GEMV path of vkq_matmul, for 1 <= M <= 8 (decode): the
- * tensor-core kernel for M <= 4 (dequantized quants and per-sub-block scaled
- * x split into three bf16 parts, fp32 accumulate) or the CUDA-core kernel;
- * both within max relative error 1e-5 of sum_k |x w|. */
+ * Q4_K column-strip kernel (M == 1, N % 256 == 0), the tensor-core kernel
+ * (M <= 4; dequantized quants and per-sub-block scaled x split into three
+ * bf16 parts, fp32 accumulate) or the CUDA-core kernel; all within max
+ * relative error 1e-5 of sum_k |x w|. */
 VKQ_API int vkq_gemv(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
              const float *x, int64_t M, float *y, void *workspace, size_t workspace_bytes,
              void *stream);

@@ -274,3 +274,28 @@ def test_gemv_matches_sequential_fused_route(tvk, oracle, qt, K, N, M):
     ref = oracle.matmul_quant_sequential(qt, x, wq, K, N)
     w = oracle.dequantize(qt, wq)[:K * N].reshape(K, N)
     assert helpers.matmul_error(y, x, w, y_ref=ref.astype(np.float64)) <= 2 * helpers.GEMV_TOL
+
+
+@pytest.mark.parametrize("qt,K,N,M", [(12, 2048, 11008, 1), (14, 1024, 4096, 3), (13, 512, 768, 16)])
+def test_matmul_host_matches_matmul(tvk, qt, K, N, M):
+    """vkq_matmul_host (x from pinned host memory, y back to it, one call)
+    gives the bits vkq_matmul gives on device buffers."""
+    torch, vt = tvk
+    from vibrant_b200 import synth, vkq
+    w = vt.QuantWeight(qt, K, N, synth.weights(qt, K, N, seed=K + N))
+    x_host = torch.from_numpy(synth.activations(M, K, seed=M + 7)).pin_memory()
+    ref = vt.matmul(x_host.cuda(), w).cpu()
+    y_host = torch.full((M, N), float("nan")).pin_memory()
+    x_dev = torch.empty(M, K, device="cuda")
+    y_dev = torch.empty(M, N, device="cuda")
+    need = vkq.matmul_workspace_bytes(qt, M, K, N, device=0)
+    ws = torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    vkq.matmul_host(qt, w.buf.data_ptr(), w.nbytes, K, N, x_host.data_ptr(), M, y_host.data_ptr(),
+                    x_dev.data_ptr(), y_dev.data_ptr(), ws.data_ptr(), ws.numel(), device=0, stream=s)
+    s.synchronize()
+    assert torch.equal(y_host.view(torch.int32), ref.view(torch.int32))
+    with pytest.raises(vkq.VkqError):
+        vkq.matmul_host(qt, w.buf.data_ptr(), w.nbytes, K, N, 0, M, y_host.data_ptr(), x_dev.data_ptr(),
+                        y_dev.data_ptr(), ws.data_ptr(), ws.numel(), device=0, stream=s)
+    assert vkq.device_status(0) == vkq.OK

@@ -281,6 +281,27 @@ int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K,
     return VKQ_OK;
 }
 
+int vkq_matmul_host(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+                    const float *x_host, int64_t M, float *y_host, float *x_dev, float *y_dev, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (!x_host || !y_host) {
+        set_error("vkq_matmul_host: null host buffer");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x_dev, M, y_dev);
+    if (st) return st;
+    cudaStream_t s = (cudaStream_t)stream;
+    st = check_launch(cudaMemcpyAsync(x_dev, x_host, (size_t)(M * K) * sizeof(float), cudaMemcpyHostToDevice, s),
+                      "copying x to the device");
+    if (st) return st;
+    st = vkq_matmul(device, qtype, w, w_bytes, K, N, x_dev, M, y_dev, workspace, workspace_bytes, stream);
+    if (st) return st;
+    return check_launch(cudaMemcpyAsync(y_host, y_dev, (size_t)(M * N) * sizeof(float), cudaMemcpyDeviceToHost, s),
+                        "copying y to the host");
+}
+
 int vkq_ipc_alloc(int device, size_t bytes, void **ptr, unsigned char handle[64]) {
     int st = enter(device);
     if (st) return st;
