@@ -385,15 +385,18 @@ def headline(ctx, args):
     ctx.barrier()
     from vibrant_b200 import vkq
     ws_ptr, ws_n = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    # raw pointers, as a host program holds them
+    w_ptrs, w_bytes = [c.buf.data_ptr() for c in copies], base.nbytes
+    xh_ptr, yh_ptr, xd_ptr, yd_ptr = x_host.data_ptr(), y_host.data_ptr(), x.data_ptr(), y.data_ptr()
+    s_ptr = ctx.stream.cuda_stream
     with torch.cuda.stream(ctx.stream):
         if align is not None:
             align()
         e0.record(ctx.stream)
         if gather is None:  # one call per step: x up, the product, y down (vkq_matmul_host)
             for i in range(e_steps):
-                w = copies[i % nc]
-                vkq.matmul_host(qt, w.buf.data_ptr(), w.nbytes, K, N, x_host.data_ptr(), 1, y_host.data_ptr(),
-                                x.data_ptr(), y.data_ptr(), ws_ptr, ws_n, device=ctx.local, stream=ctx.stream)
+                vkq.matmul_host(qt, w_ptrs[i % nc], w_bytes, K, N, xh_ptr, 1, yh_ptr, xd_ptr, yd_ptr, ws_ptr, ws_n,
+                                device=ctx.local, stream=s_ptr)
         else:
             for i in range(e_steps):
                 x.copy_(x_host, non_blocking=True)

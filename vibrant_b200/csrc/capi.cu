@@ -43,6 +43,30 @@ int device_sm_count(int device) {
 
 bool vkq_last_error_empty() { return t_err[0] == '\0'; }
 
+cudaError_t kernel_smem(const void *fn, size_t smem, bool carveout) {
+    struct Entry {
+        const void *fn;
+        int dev;
+        size_t smem;
+    };
+    static std::mutex mu;
+    static Entry table[512];
+    static int used = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> g(mu);
+    int i = 0;
+    while (i < used && (table[i].fn != fn || table[i].dev != dev)) i++;
+    if (i < used && table[i].smem >= smem) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && carveout) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    if (i == used && used < 512) table[used++] = Entry{fn, dev, smem};
+    else if (i < used) table[i].smem = smem;
+    return cudaSuccess;
+}
+
 static int block_bytes(int qt) {
     switch (qt) {
     case VKQ_Q4_K: return 144;
@@ -57,7 +81,8 @@ static int block_bytes(int qt) {
 static int enter(int device) {
     t_err[0] = '\0';
     int dev = device;
-    if (device >= 0) {
+    int cur = -1;
+    if (device >= 0 && (cudaGetDevice(&cur) != cudaSuccess || cur != device)) {
         cudaError_t e = cudaSetDevice(device);
         if (e != cudaSuccess) {
             set_error("cudaSetDevice(%d): %s", device, cudaGetErrorString(e));

@@ -696,7 +696,7 @@ template <int QT>
 static cudaError_t launch_gemm(const CUtensorMap &tm, const CUtensorMap &tw, const GemmParams &gp, const GemmPlan &g,
                                cudaStream_t st) {
     auto kern = gemm_kernel<QT>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+    cudaError_t e = kernel_smem((const void *)kern, g.smem, false);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)g.grid);

@@ -979,10 +979,8 @@ size_t gemv_workspace_bytes(const GemvShape &s, int device) {
 template <int QT, int MR, int VPT, bool G>
 static cudaError_t launch_fast(const GemvParams &gp, const GatherParams &gq, const Plan &pl, cudaStream_t stream) {
     auto kern = gemv_kernel<QT, MR, VPT, G>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
-    if (e != cudaSuccess) return e;
     // two CTAs per SM need the largest shared-memory carveout
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaError_t e = kernel_smem((const void *)kern, pl.smem, true);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(pl.grid);

@@ -226,9 +226,13 @@ __global__ void __launch_bounds__(kStripThreads, 1) gemv_strip_kernel(const Stri
     const bool norm = p.norm_w != nullptr;
     const int crank = S > 1 ? (int)cluster_ctarank() : 0;
     const int g = (int)(blockIdx.x / (unsigned)S);
+    // groups of q + 1 units first, then groups of q: the larger groups start
+    // on the SMs that the previous launch frees first, the smaller ones on the
+    // SMs its slowest CTAs hold longest
     const int units = p.lanes / p.unit;
-    const int lo = (int)((int64_t)g * units / p.groups) * p.unit;
-    const int nlc = (int)((int64_t)(g + 1) * units / p.groups) * p.unit - lo;
+    const int uq = units / p.groups, ur = units % p.groups;
+    const int lo = (g * uq + (g < ur ? g : ur)) * p.unit;
+    const int nlc = (uq + (g < ur ? 1 : 0)) * p.unit;
     const int R = kStripThreads / nlc;  // row groups (threads per lane-column)
     const int lcl = t % nlc, rg = t / nlc;
     const int64_t k0 = (int64_t)crank * p.k_per;
@@ -505,11 +509,7 @@ static const void *strip_kernel(int M) {
     }
 }
 
-static cudaError_t strip_prepare(const void *fn, size_t smem) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    return e;
-}
+static cudaError_t strip_prepare(const void *fn, size_t smem) { return kernel_smem(fn, smem, true); }
 
 // CTAs of clusters of S that the device runs at once (max active clusters x S).
 static int strip_capacity(int M, int S, int device) {

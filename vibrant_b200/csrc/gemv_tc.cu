@@ -719,7 +719,7 @@ size_t gemv_tc_workspace_bytes(const GemvShape &s, const TcLayout &L, int device
 template <int QT, int MR>
 static cudaError_t launch_tc(const CUtensorMap &tm, const TcParams &tp, const TcPlan &g, cudaStream_t st) {
     auto kern = gemv_tc_kernel<QT, MR>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+    cudaError_t e = kernel_smem((const void *)kern, g.smem, false);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)g.grid);

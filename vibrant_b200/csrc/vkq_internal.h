@@ -9,6 +9,11 @@
 namespace vkq {
 
 int device_sm_count(int device);
+// Raises a kernel's dynamic shared-memory limit on the current device to at
+// least `smem` bytes (with `carveout`, also its preferred carveout to the
+// maximum); the driver is asked only when a launch needs more than the last
+// limit set for that kernel and device.
+cudaError_t kernel_smem(const void *fn, size_t smem, bool carveout);
 
 cudaError_t dequantize_f32(int qtype, const void *w, int64_t nblocks, float *out, cudaStream_t s, int device);
 cudaError_t dequant_transpose_f32(int qtype, const void *w, int64_t K, int64_t N, float *out, cudaStream_t s,
