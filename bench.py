@@ -831,7 +831,7 @@ def run_ours(args):
         "e2e": {"value": round(hl["total"] / hl["e_dt"] / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": hl["h2d"], "d2h_bytes_per_step": hl["d2h"],
                 "ms_per_step": round(hl["e_dt"] * 1e3, 5),
-                "path": "vkq_matmul_host (N=1: x up, product, y down in one call) / copies around vkq_gemv_allgather (N>1); ctypes, eager launches"},
+                "path": "vkq_matmul_host (N=1: one call per step; pinned buffers reached through the host mapping: a staging kernel reads x, the GEMV stores y into host memory) / copies around vkq_gemv_allgather (N>1); ctypes, eager launches"},
         "parity": {"max_rel_err": hl["err"], "tolerance": 1e-5, "checked": "all columns on every rank vs the oracle"},
         "gpu_launches": args.steps,
         "clocks": hl["clocks"],

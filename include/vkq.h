@@ -118,11 +118,14 @@ VKQ_API int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, in
  * reference's MatMul on a CPU activation and a device weight: the upload of
  * x, the product, the download of y, as Tensor.ToDevice / EnsureCPUData do
  * around matmulGPU, internal/tensor/tensor_cuda_api.go and
- * internal/tensor/tensor.go:482-524): copies x_host [M, K] into the device
- * buffer x_dev, runs vkq_matmul into the device buffer y_dev and copies it
- * to y_host [M, N], all enqueued on `stream` (one cudaMemcpyAsync per copy;
- * pinned host buffers make the call asynchronous).  Same arguments and
- * errors as vkq_matmul otherwise. */
+ * internal/tensor/tensor.go:482-524): moves x_host [M, K] into the device
+ * buffer x_dev, runs vkq_matmul and delivers y [M, N] to y_host, all
+ * enqueued on `stream`.  Pinned host buffers (cudaHostAlloc, mapped into the
+ * device's address space) up to 1 MiB are reached through the mapping: a
+ * small kernel reads x, and for M <= 8 the GEMV stores y straight into
+ * y_host (y_dev is then unused); other host memory, and larger buffers, are
+ * copied with cudaMemcpyAsync (synchronously for pageable memory).  Same
+ * arguments and errors as vkq_matmul otherwise. */
 VKQ_API int vkq_matmul_host(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                             const float *x_host, int64_t M, float *y_host, float *x_dev, float *y_dev,
                             void *workspace, size_t workspace_bytes, void *stream);

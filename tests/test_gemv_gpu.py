@@ -276,16 +276,23 @@ def test_gemv_matches_sequential_fused_route(tvk, oracle, qt, K, N, M):
     assert helpers.matmul_error(y, x, w, y_ref=ref.astype(np.float64)) <= 2 * helpers.GEMV_TOL
 
 
-@pytest.mark.parametrize("qt,K,N,M", [(12, 2048, 11008, 1), (14, 1024, 4096, 3), (13, 512, 768, 16)])
-def test_matmul_host_matches_matmul(tvk, qt, K, N, M):
-    """vkq_matmul_host (x from pinned host memory, y back to it, one call)
-    gives the bits vkq_matmul gives on device buffers."""
+@pytest.mark.parametrize("pinned", [True, False], ids=["pinned", "pageable"])
+@pytest.mark.parametrize("qt,K,N,M", [(12, 2048, 11008, 1), (14, 1024, 4096, 3), (13, 512, 768, 16),
+                                      (12, 4, 256, 1), (14, 999, 1000, 2), (12, 600, 28672, 8)])
+def test_matmul_host_matches_matmul(tvk, qt, K, N, M, pinned):
+    """vkq_matmul_host (x from host memory, y back to it, one call) gives the
+    bits vkq_matmul gives on device buffers: through the host mapping for
+    pinned buffers (x read by a staging kernel, y stored by the GEMV; the
+    28672-column case is above the 1 MiB limit for y at M = 8 and copies it),
+    by cudaMemcpyAsync for pageable ones."""
     torch, vt = tvk
     from vibrant_b200 import synth, vkq
     w = vt.QuantWeight(qt, K, N, synth.weights(qt, K, N, seed=K + N))
-    x_host = torch.from_numpy(synth.activations(M, K, seed=M + 7)).pin_memory()
+    x_host = torch.from_numpy(synth.activations(M, K, seed=M + 7))
     ref = vt.matmul(x_host.cuda(), w).cpu()
-    y_host = torch.full((M, N), float("nan")).pin_memory()
+    y_host = torch.full((M, N), float("nan"))
+    if pinned:
+        x_host, y_host = x_host.pin_memory(), y_host.pin_memory()
     x_dev = torch.empty(M, K, device="cuda")
     y_dev = torch.empty(M, N, device="cuda")
     need = vkq.matmul_workspace_bytes(qt, M, K, N, device=0)

@@ -117,6 +117,20 @@ static int check_launch(cudaError_t e, const char *what) {
     return VKQ_OK;
 }
 
+// Largest x or y that vkq_matmul_host moves through the host mapping.
+constexpr size_t kStageBytes = 1 << 20;
+
+// The device address of pinned host memory mapped into the current device's
+// address space, or null for any other memory.
+static void *mapped_host(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
 static int check_matmul_args(int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
                              int64_t M, float *y) {
     int bb = block_bytes(qtype);
@@ -318,13 +332,22 @@ int vkq_matmul_host(int device, int qtype, const void *w, int64_t w_bytes, int64
     st = check_matmul_args(qtype, w, w_bytes, K, N, x_dev, M, y_dev);
     if (st) return st;
     cudaStream_t s = (cudaStream_t)stream;
-    st = check_launch(cudaMemcpyAsync(x_dev, x_host, (size_t)(M * K) * sizeof(float), cudaMemcpyHostToDevice, s),
-                      "copying x to the device");
+    const size_t xb = (size_t)(M * K) * sizeof(float), yb = (size_t)(M * N) * sizeof(float);
+    // Pinned host buffers are reached through their device mapping: a small
+    // kernel reads x (before the preceding kernel ends) and the GEMV stores y
+    // straight into host memory, with no copy-engine round trips; other host
+    // memory, and larger prefill inputs and outputs, go by cudaMemcpyAsync.
+    const float *x_map = xb <= kStageBytes ? static_cast<const float *>(mapped_host(x_host)) : nullptr;
+    float *y_map = (M <= 8 && yb <= kStageBytes) ? static_cast<float *>(mapped_host(y_host)) : nullptr;
+    if (x_map)
+        st = check_launch(stage_in(x_map, x_dev, M * K, s), "reading x from the host");
+    else
+        st = check_launch(cudaMemcpyAsync(x_dev, x_host, xb, cudaMemcpyHostToDevice, s), "copying x to the device");
     if (st) return st;
-    st = vkq_matmul(device, qtype, w, w_bytes, K, N, x_dev, M, y_dev, workspace, workspace_bytes, stream);
-    if (st) return st;
-    return check_launch(cudaMemcpyAsync(y_host, y_dev, (size_t)(M * N) * sizeof(float), cudaMemcpyDeviceToHost, s),
-                        "copying y to the host");
+    st = vkq_matmul(device, qtype, w, w_bytes, K, N, x_dev, M, y_map ? y_map : y_dev, workspace, workspace_bytes,
+                    stream);
+    if (st || y_map) return st;
+    return check_launch(cudaMemcpyAsync(y_host, y_dev, yb, cudaMemcpyDeviceToHost, s), "copying y to the host");
 }
 
 int vkq_ipc_alloc(int device, size_t bytes, void **ptr, unsigned char handle[64]) {

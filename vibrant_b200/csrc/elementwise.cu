@@ -65,6 +65,36 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float *__r
     for (int64_t i = threadIdx.x; i < n; i += kNormThreads) yr[i] = (xr[i] / r) * weight[i];
 }
 
+// dst[0..n) = src[0..n), src being pinned host memory that the device reads
+// through its mapping.  The loads do not depend on the preceding kernel and
+// are issued before griddepcontrol.wait; only the stores into dst (which the
+// preceding kernel may still be reading) wait for it.  Each thread moves up
+// to four floats.
+__global__ void __launch_bounds__(256) stage_in_kernel(const float *__restrict__ src, float *__restrict__ dst,
+                                                       int64_t n) {
+    pdl_launch_dependents();
+    const int64_t i0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    const bool vec = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15u) == 0;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vec && i0 + 4 <= n) {
+        const float4 q = __ldcv(reinterpret_cast<const float4 *>(src + i0));
+        v[0] = q.x;
+        v[1] = q.y;
+        v[2] = q.z;
+        v[3] = q.w;
+    } else {
+        for (int j = 0; j < 4; j++)
+            if (i0 + j < n) v[j] = __ldcv(src + i0 + j);
+    }
+    pdl_wait();
+    if (vec && i0 + 4 <= n) {
+        *reinterpret_cast<float4 *>(dst + i0) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        for (int j = 0; j < 4; j++)
+            if (i0 + j < n) dst[i0 + j] = v[j];
+    }
+}
+
 static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, cudaStream_t s, void **args) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
@@ -85,6 +115,12 @@ cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, 
     if (blocks > 4 * sms) blocks = 4 * sms;
     void *args[] = {(void *)&gate, (void *)&up, (void *)&out, (void *)&n};
     return launch_pdl((const void *)silu_mul_kernel, dim3((unsigned)blocks), dim3(256), s, args);
+}
+
+cudaError_t stage_in(const float *src_mapped, float *dst, int64_t n, cudaStream_t s) {
+    const int64_t blocks = (n + 1023) / 1024;
+    void *args[] = {(void *)&src_mapped, (void *)&dst, (void *)&n};
+    return launch_pdl((const void *)stage_in_kernel, dim3((unsigned)blocks), dim3(256), s, args);
 }
 
 cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,

@@ -128,6 +128,9 @@ int gemm_read_status();  // reads and clears this TU's device status word (synch
 cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, cudaStream_t s, int device);
 cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,
                      cudaStream_t s);
+// dst[0..n) = src[0..n) from pinned host memory through its device mapping
+// (elementwise.cu), as a kernel that takes part in programmatic dependent launch.
+cudaError_t stage_in(const float *src_mapped, float *dst, int64_t n, cudaStream_t s);
 
 void set_error(const char *fmt, ...);
 bool vkq_last_error_empty();
