@@ -26,6 +26,11 @@
 //    atoms, SBO 1024 B).  No multicast;
 //  * D: fp32 in TMEM, 128 lanes (n) x bm columns (m), double-buffered so the
 //    epilogue warps drain tile i to Y while the MMA warp accumulates tile i+1.
+// Wide units (M > 256): 128 n x 2 bm m, one 16 KB A tile per stage read by
+// both MMAs (one per m half, B = the two X tiles), so each weight tile is
+// dequantized once for up to 512 rows of m instead of once per 256; each
+// dequant thread decodes half a 32-value unit.  Prefill 512 x 2048 x 11008:
+// 40 -> 35 us; 2048 x 5120 x 27648: 1.24 PFLOP/s.
 // The grid is persistent (at most one CTA per SM); work units are
 // (n tile, m tile, k split) taken round-robin.  When the output tiles alone
 // cannot fill the machine (narrow N), K is split and the partial products go
@@ -75,6 +80,7 @@ struct GemmParams {
     int raw_tma;        // raw stages are 2D tile copies (k rows with a 16-byte pitch)
     int tmem_cols, acc_stride;
     int nbuf;           // TMEM accumulator buffers (2: the epilogue overlaps the next unit)
+    int wide;           // units of 128 n x 2*bm m (one dequantized A tile for both MMA halves)
 };
 
 __device__ __forceinline__ void g_set_status(int c) { atomicExch(&g_gemm_status, c); }
@@ -102,11 +108,32 @@ __device__ __forceinline__ float2 int_pair(uint32_t E, uint32_t O) {
     return make_float2(__uint_as_float(prmt(E, 0u, 0x4440u | J)), __uint_as_float(prmt(O, 0u, 0x4440u | J)));
 }
 
+// Moves the second 16 values of a loaded unit to where decode_unit_bf16
+// reads the first 16 (quant words, Q5_K fifth bits, Q6_K high bits and
+// 16-value scale), so that decode_unit_bf16<QT, 2> yields that half.
 template <int QT>
-__device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&out)[16]) {
+__device__ __forceinline__ void shift_half(RawUnit &u) {
+    if constexpr (QT == kQ4K || QT == kQ5K) {
+        u.v[4] = u.v[6];
+        u.v[5] = u.v[7];
+        if constexpr (QT == kQ5K) u.v[8] >>= 16;
+    } else {
+        u.v[0] = u.v[2];
+        u.v[1] = u.v[3];
+        u.v[2] = u.v[4];
+        u.v[5] = u.v[6];
+        u.v[6] = u.v[7];
+        u.v[8] = (u.v[8] & 0xFFFF0000u) | ((u.v[8] >> 8) & 0xFFu);
+    }
+}
+
+// Decodes the first 8 * NC values of a unit (NC = 4: all 32) into 4 * NC
+// bf16 pairs.
+template <int QT, int NC = 4>
+__device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&out)[4 * NC]) {
     if (!u.valid) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) out[i] = 0u;
+        for (int i = 0; i < 4 * NC; i++) out[i] = 0u;
         return;
     }
     if constexpr (QT == kQ4K || QT == kQ5K) {
@@ -119,7 +146,7 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
         const float ndm = (dmin * -kWDown) * (float)((m24 >> sh) & 63u);
         const float2 s2 = make_float2(ds, ds), nm2 = make_float2(ndm, ndm);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < NC; c++) {
             uint32_t E = u.v[4 + c] & 0x0F0F0F0Fu;
             uint32_t O = (u.v[4 + c] >> 4) & 0x0F0F0F0Fu;
             if constexpr (QT == kQ5K) {
@@ -149,7 +176,7 @@ __device__ __forceinline__ void decode_unit_bf16(const RawUnit &u, uint32_t (&ou
         // -32 * d*s * 2^-49 = (d*s * 2^100) * -2^-144, exact
         const float o0 = ds0 * -0x1p-144f, o1 = ds1 * -0x1p-144f;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < NC; c++) {
             // byte lane j of X = nibble j of the chunk's 16 qh bits
             //                  = (hi2 of value 2j+1) << 2 | (hi2 of value 2j)
             const uint32_t X = prmt(qh[c >> 1], qhs[c >> 1], (c & 1) ? 0x7362u : 0x5140u) & 0x0F0F0F0Fu;
@@ -177,27 +204,33 @@ __device__ __forceinline__ Unit unit_of(const GemmParams &p, int u) {
     Unit r;
     const int split = u % p.splits;
     const int tile = u / p.splits;
-    r.n0 = (int64_t)(tile / p.m_tiles) * kGBN;
-    r.m0 = (tile % p.m_tiles) * p.bm;
+    r.n0 = (int64_t)(tile / p.m_tiles) * (p.wide ? kMmaM : kGBN);
+    r.m0 = (tile % p.m_tiles) * (p.wide ? 2 * p.bm : p.bm);
     r.kb = split * p.kper;
     r.ke = min(r.kb + p.kper, p.ksteps);
     r.split = split;
     return r;
 }
 
-template <int QT>
+// WIDE: a unit is 128 n x 2 bm m; the A stage is one MMA operand (16 KB), the
+// B stage two X tiles (m0 and m0 + bm), and both MMAs of a 16-k step read the
+// same A (each weight tile is dequantized once for 2 bm rows of m).
+template <int QT, bool WIDE>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmx,
                                                             const __grid_constant__ CUtensorMap tmw,
                                                             const GemmParams p) {
     constexpr int B = QT_<QT>::BYTES;
+    constexpr int kA = WIDE ? kAHalf : kAStage;  // bytes of an A stage
+    constexpr int kNU = WIDE ? kMmaM : kGBN;     // n per unit
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32addr(smem_raw);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
     uint8_t *const gbase = smem_raw + (base - raw_base);  // generic pointer to `base`
-    const uint32_t b_stage = (uint32_t)(p.bm * 128);
+    const uint32_t b_tile = (uint32_t)(p.bm * 128);       // one X tile: bm rows of 64 k
+    const uint32_t b_stage = WIDE ? 2u * b_tile : b_tile;
     const uint32_t raw_stage = (uint32_t)(kGBK * p.raw_slot);
-    const uint32_t a_ring = base;                                    // sa x 16 KB
-    const uint32_t b_ring = a_ring + (uint32_t)(p.sa * kAStage);     // sb x bm*128
+    const uint32_t a_ring = base;                                    // sa x kA
+    const uint32_t b_ring = a_ring + (uint32_t)(p.sa * kA);          // sb x b_stage
     const uint32_t r_ring = b_ring + (uint32_t)p.sb * b_stage;       // sr x 64*raw_slot
     const uint32_t bars = r_ring + (uint32_t)p.sr * raw_stage;
     auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
@@ -271,8 +304,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                   "=r"(r[15])
                 : "r"(taddr));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            const int64_t n = un.n0 + kMmaM * h + 32 * q + lane;
-            const int64_t mb = un.m0 + c;
+            // accumulator half h: n rows 128h.. (or, WIDE, m rows bm*h..)
+            const int64_t n = un.n0 + (WIDE ? 0 : kMmaM * h) + 32 * q + lane;
+            const int64_t mb = un.m0 + (WIDE ? h * p.bm : 0) + c;
             const int mv = (int)min((int64_t)16, p.M - mb);
             if (n < p.N && mv > 0) {
                 float *yp = yb + mb * p.N + n;  // walks down the m rows of this column
@@ -293,7 +327,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         RingPos rp;
         for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
             const Unit un = unit_of(p, u);
-            const int64_t nv = min((int64_t)kGBN, p.N - un.n0);
+            const int64_t nv = min((int64_t)kNU, p.N - un.n0);
             bool ok = true;
             for (int ks = un.kb; ks < un.ke; ks++, rp.next((uint32_t)p.sr)) {
                 const int s = (int)rp.idx;
@@ -363,6 +397,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                     }
                     mbar_arrive_expect_tx(bar(BF + s), b_stage);
                     tma_load_2d(b_ring + (uint32_t)s * b_stage, &tmx, ks * kGBK, un.m0, bar(BF + s));
+                    // the second m half (rows past M read as zeros)
+                    if (WIDE)
+                        tma_load_2d(b_ring + (uint32_t)s * b_stage + b_tile, &tmx, ks * kGBK, un.m0 + p.bm,
+                                    bar(BF + s));
                 }
                 if (!ok) break;
             }
@@ -397,19 +435,20 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;");
-                    const uint64_t da = da0 + (uint64_t)((uint32_t)(sa * kAStage) >> 4);
+                    const uint64_t da = da0 + (uint64_t)((uint32_t)(sa * kA) >> 4);
                     const uint64_t db = db0 + (uint64_t)(((uint32_t)sb * b_stage) >> 4);
                     const uint32_t acc0 = ks > un.kb ? 1u : 0u;
                     // A half h (n 128h..128h+127): two k groups of 8 per 16-k step
                     // (2048 B apart), 64-n halves 1024 B apart.  B: K-major, 16 k =
                     // 32 bytes into each 128-byte row, 8-row atoms 1024 B apart.
-                    umma_bf16(dt0, da, db, idesc, acc0);
-                    umma_bf16(dt1, da + (kAHalf >> 4), db, idesc, acc0);
+                    // WIDE: one A, and the second MMA takes the second X tile.
+                    const uint32_t a1 = WIDE ? 0u : (uint32_t)kAHalf, b1 = WIDE ? b_tile : 0u;
 #pragma unroll
-                    for (int kk = 1; kk < kGBK / 16; kk++) {
-                        umma_bf16(dt0, da + (uint64_t)(kk * 4096 >> 4), db + (uint64_t)(kk * 32 >> 4), idesc, 1u);
-                        umma_bf16(dt1, da + (uint64_t)((kAHalf + kk * 4096) >> 4), db + (uint64_t)(kk * 32 >> 4),
-                                  idesc, 1u);
+                    for (int kk = 0; kk < kGBK / 16; kk++) {
+                        const uint32_t acc = kk == 0 ? acc0 : 1u;
+                        umma_bf16(dt0, da + (uint64_t)(kk * 4096 >> 4), db + (uint64_t)(kk * 32 >> 4), idesc, acc);
+                        umma_bf16(dt1, da + (uint64_t)((a1 + kk * 4096) >> 4), db + (uint64_t)((b1 + kk * 32) >> 4),
+                                  idesc, acc);
                     }
                     umma_commit(bar(AE + sa));  // frees the stages once these MMAs have read them
                     umma_commit(bar(BE + sb));
@@ -423,23 +462,27 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         }
     } else if (warp < kWEpi) {
         // ------------- dequant warps: raw stage -> bf16 A tile -------------
-        constexpr int UPT = kGBK * (kGBN / 32) / (kNDeq * 32);  // units per thread per stage
+        // WIDE: 128 n x 64 k per stage, half a 32-value unit per thread
+        constexpr int NC = WIDE ? 2 : 4;                                      // 16-byte A chunks per unit
+        constexpr int UPT = WIDE ? 1 : kGBK * (kGBN / 32) / (kNDeq * 32);  // units per thread per stage
         const int dt = threadIdx.x - kWDeq * 32;
         // unit j of the thread in every stage: uu = dt + j * 32 * kNDeq is k row
-        // 8 * (uu / 64) + uu % 8 and 32 n starting at 32 * ((uu / 8) % 8); the 8
-        // lanes of a shared-memory phase take the 8 k rows of one swizzle atom,
-        // so their 16-byte A stores land in 8 different bank groups
-        int kl[UPT], c8[UPT];
-        uint32_t a_off[UPT][4];  // the unit's four 16-byte chunks within an A stage
+        // 8 * (uu / 64) + uu % 8 and 32 n starting at 32 * ((uu / 8) % 8)
+        // (WIDE: the half (uu / 8) % 2 of the 32 n starting at 32 * ((uu / 16) % 4));
+        // the 8 lanes of a shared-memory phase take the 8 k rows of one swizzle
+        // atom, so their 16-byte A stores land in 8 different bank groups
+        int kl[UPT], c8[UPT], hf[UPT];
+        uint32_t a_off[UPT][NC];  // the unit's 16-byte chunks within an A stage
 #pragma unroll
         for (int j = 0; j < UPT; j++) {
             const int uu = dt + j * 32 * kNDeq;
             kl[j] = 8 * (uu >> 6) + (uu & 7);
-            c8[j] = (uu >> 3) & 7;
-            const int h = c8[j] >> 2, c32 = c8[j] & 3, g = kl[j] >> 3, kin = kl[j] & 7;
+            c8[j] = WIDE ? (uu >> 4) & 3 : (uu >> 3) & 7;
+            hf[j] = WIDE ? (uu >> 3) & 1 : 0;
+            const int h = WIDE ? 0 : c8[j] >> 2, c32 = c8[j] & 3, g = kl[j] >> 3, kin = kl[j] & 7;
 #pragma unroll
-            for (int c4 = 0; c4 < 4; c4++) {
-                const int nl = 32 * c32 + 8 * c4;  // first n of the chunk within the MMA half
+            for (int c4 = 0; c4 < NC; c4++) {
+                const int nl = 32 * c32 + 16 * hf[j] + 8 * c4;  // first n of the chunk within the MMA half
                 const int hh = nl >> 6, c = (nl & 63) >> 3;
                 a_off[j][c4] = (uint32_t)(h * kAHalf + (g * 2 + hh) * 1024 + kin * 128 + ((c ^ kin) << 4));
             }
@@ -472,7 +515,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                     if (valid) {
                         if (p.raw_tma) {
                             blk = st_r + tma_off[j];
-                            within = 32u * (uint32_t)c8[j];
+                            within = (uint32_t)(un.n0 & 255) + 32u * (uint32_t)c8[j];
                         } else {
                             const int64_t v0 = k * p.N + un.n0;
                             const int64_t blk0 = v0 >> 8;
@@ -486,19 +529,21 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar(RE + sr));
-                uint32_t wv[UPT][16];
+                uint32_t wv[UPT][4 * NC];
 #pragma unroll
-                for (int j = 0; j < UPT; j++)
-                    decode_unit_bf16<QT>(ru[j], wv[j]);  // before the wait: overlaps the MMAs still reading the stage
+                for (int j = 0; j < UPT; j++) {
+                    if (WIDE && hf[j]) shift_half<QT>(ru[j]);
+                    decode_unit_bf16<QT, NC>(ru[j], wv[j]);  // before the wait: overlaps the MMAs still reading the stage
+                }
                 if (pa.uses >= (uint32_t)p.sa && !wait(bar(AE + sa), pa.phase ^ 1u, true)) {
                     ok = false;
                     break;
                 }
-                const uint32_t a_s = a_ring + (uint32_t)(sa * kAStage);
+                const uint32_t a_s = a_ring + (uint32_t)(sa * kA);
 #pragma unroll
                 for (int j = 0; j < UPT; j++)
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; c4++)
+                    for (int c4 = 0; c4 < NC; c4++)
                         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a_s + a_off[j][c4]),
                                      "r"(wv[j][4 * c4]), "r"(wv[j][4 * c4 + 1]), "r"(wv[j][4 * c4 + 2]),
                                      "r"(wv[j][4 * c4 + 3])
@@ -595,6 +640,7 @@ EncodeTiledFn encode_tiled_fn() {
 struct GemmPlan {
     int bm, m_tiles, n_tiles, splits, units, ksteps, kper;
     int sr, sa, sb, raw_slot, raw_tma, tmem_cols, nbuf;
+    int wide;  // 128 n x 2 bm m units (see gemm_kernel)
     int64_t xb_bytes, part_bytes;  // workspace after the counter head: bf16 X, then the split partials
     size_t smem;
     int grid;
@@ -602,17 +648,19 @@ struct GemmPlan {
 
 static int block_bytes_of(int qt) { return qt == kQ4K ? 144 : qt == kQ5K ? 176 : 210; }
 
-// Cost model in SM cycles for one 256 n x bm m unit and one 64-k step: the
-// two MMAs 128 x bm x 16 of each 16-k step take about bm / 2 cycles each
-// (4 * bm per step); dequantizing 256 x 64 values takes about kDeqCycles; the
-// SM pulls the raw stage and the X tile out of L2 at about kL2Bytes per cycle.
-// Units run in waves of `sms`; the epilogue writes 256 x bm floats per unit at
-// about kYBytes per cycle and is hidden behind the next unit only when two
-// accumulator buffers fit in TMEM (4 * bm <= 512 columns).  Split partials
-// cost a write and a read of splits * M * N floats.
+// Cost model in SM cycles for one unit (256 n x bm m, or WIDE 128 n x 2 bm m)
+// and one 64-k step: the two MMAs 128 x bm x 16 of each 16-k step take about
+// bm / 2 cycles each (4 * bm per step); dequantizing the stage's weights
+// takes about kDeqCycles (256 x 64 values, measured ~1,900 cycles with the
+// sixteen dequant warps) or kDeqWide (128 x 64); the SM pulls the raw stage
+// and the X tiles out of L2 at about kL2Bytes per cycle.  Units run in waves
+// of `sms`; the epilogue writes the unit's floats at about kYBytes per cycle
+// and is hidden behind the next unit only when two accumulator buffers fit in
+// TMEM (4 * bm <= 512 columns).  Split partials cost a write and a read of
+// splits * M * N floats.
 static GemmPlan gemm_plan(const GemvShape &s, int sms) {
-    constexpr double kDeqCycles = 600.0, kL2Bytes = 55.0, kYBytes = 40.0, kUnitOverhead = 1500.0,
-                     kBytesPerCycle = 3000.0;
+    constexpr double kDeqCycles = 1900.0, kDeqWide = 1100.0, kL2Bytes = 55.0, kYBytes = 40.0,
+                     kUnitOverhead = 1500.0, kBytesPerCycle = 3000.0;
     GemmPlan g{};
     const int B = block_bytes_of(s.qtype);
     // k rows whose byte pitch is a multiple of 16 (N % 256 == 0 and N/256*B % 16
@@ -623,36 +671,51 @@ static GemmPlan gemm_plan(const GemvShape &s, int sms) {
     else g.raw_slot = (2 * B + 15 + 15) & ~15;
     const double raw_stage = (double)kGBK * g.raw_slot;
     g.ksteps = (int)((s.K + kGBK - 1) / kGBK);
-    g.n_tiles = (int)((s.N + kGBN - 1) / kGBN);
     double best = 1e300;
-    for (int bm = 16; bm <= 256; bm += 16) {
-        const int64_t mt = (s.M + bm - 1) / bm;
-        if (bm > 16 && (s.M + bm - 17) / (bm - 16) == mt) continue;  // bm - 16 gives the same m tiles
-        const int64_t tiles = mt * g.n_tiles;
-        const double step = std::max({4.0 * bm, kDeqCycles, (raw_stage + 128.0 * bm) / kL2Bytes});
-        const double epi = (double)kGBN * bm * 4.0 / kYBytes;
-        const bool two_bufs = 4 * bm <= 512;
-        for (int sp : {1, 2, 3, 4, 6, 8}) {
-            if (sp > g.ksteps) break;
-            const int kper = (g.ksteps + sp - 1) / sp;
-            if ((int64_t)(sp - 1) * kper >= g.ksteps) continue;  // every split gets k steps
-            const int64_t units = tiles * sp;
-            const int64_t waves = (units + sms - 1) / sms;
-            double cost = (double)waves * (kper * step + kUnitOverhead) + (two_bufs ? epi : (double)waves * epi);
-            if (sp > 1) cost += 2.0 * sp * (double)s.M * (double)s.N * 4.0 / kBytesPerCycle + kUnitOverhead;
-            if (cost < best * 0.999) {
-                best = cost;
-                g.bm = bm;
-                g.m_tiles = (int)mt;
-                g.splits = sp;
-                g.kper = kper;
-                g.units = (int)units;
+    // WIDE only pays when one m tile of 256 cannot hold M (otherwise its
+    // second m half would be empty)
+    const size_t ring_budget = 227 * 1024 - (1024 + 8 * (6 * kMaxStages + 8) + 16);
+    for (int wide = 0; wide <= (s.M > 256 ? 1 : 0); wide++) {
+        const int nu = wide ? kMmaM : kGBN, mh = wide ? 2 : 1;
+        const int64_t n_tiles = (s.N + nu - 1) / nu;
+        for (int bm = 16; bm <= 256; bm += 16) {
+            const int64_t mt = (s.M + mh * bm - 1) / (mh * bm);
+            if (bm > 16 && (s.M + mh * (bm - 16) - 1) / (mh * (bm - 16)) == mt) continue;  // bm - 16: same m tiles
+            // WIDE needs three A and three raw stages beside two X stages (with
+            // two of each the hand-offs, not the work, set the pace: Q6_K rows
+            // that are not 16-byte pitched took 127 us at M = 512)
+            if (wide && 3 * (size_t)kAHalf + 2 * (size_t)mh * bm * 128 + 3 * (size_t)raw_stage > ring_budget) continue;
+            const int64_t tiles = mt * n_tiles;
+            const double step = std::max({4.0 * bm, wide ? kDeqWide : kDeqCycles,
+                                          (raw_stage + 128.0 * mh * bm) / kL2Bytes});
+            const double epi = (double)nu * mh * bm * 4.0 / kYBytes;
+            const bool two_bufs = 4 * bm <= 512;
+            for (int sp : {1, 2, 3, 4, 6, 8}) {
+                if (sp > g.ksteps) break;
+                const int kper = (g.ksteps + sp - 1) / sp;
+                if ((int64_t)(sp - 1) * kper >= g.ksteps) continue;  // every split gets k steps
+                const int64_t units = tiles * sp;
+                const int64_t waves = (units + sms - 1) / sms;
+                double cost =
+                    (double)waves * (kper * step + kUnitOverhead) + (two_bufs ? epi : (double)waves * epi);
+                if (sp > 1) cost += 2.0 * sp * (double)s.M * (double)s.N * 4.0 / kBytesPerCycle + kUnitOverhead;
+                if (cost < best * 0.999) {
+                    best = cost;
+                    g.wide = wide;
+                    g.n_tiles = (int)n_tiles;
+                    g.bm = bm;
+                    g.m_tiles = (int)mt;
+                    g.splits = sp;
+                    g.kper = kper;
+                    g.units = (int)units;
+                }
             }
         }
     }
     g.nbuf = 4 * g.bm <= 512 ? 2 : 1;
     g.grid = std::min(g.units, sms);
-    const size_t a_st = kAStage, b_st = (size_t)g.bm * 128, r_st = (size_t)kGBK * g.raw_slot;
+    const size_t a_st = g.wide ? kAHalf : kAStage, b_st = (size_t)(g.wide ? 2 : 1) * g.bm * 128,
+                 r_st = (size_t)kGBK * g.raw_slot;
     const size_t fixed = 1024 + 8 * (6 * kMaxStages + 8) + 16;
     const size_t budget = 227 * 1024 - fixed;
     // Ring depths: every stage makes a round trip through several mbarrier
@@ -692,10 +755,10 @@ size_t gemm_workspace_bytes(const GemvShape &s, int device) {
     return kWorkspaceCounterHead + (size_t)(g.xb_bytes + g.part_bytes);
 }
 
-template <int QT>
+template <int QT, bool WIDE>
 static cudaError_t launch_gemm(const CUtensorMap &tm, const CUtensorMap &tw, const GemmParams &gp, const GemmPlan &g,
                                cudaStream_t st) {
-    auto kern = gemm_kernel<QT>;
+    auto kern = gemm_kernel<QT, WIDE>;
     cudaError_t e = kernel_smem((const void *)kern, g.smem, false);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
@@ -814,11 +877,12 @@ int gemm_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float 
     gp.tmem_cols = g.tmem_cols;
     gp.acc_stride = 2 * g.bm;
     gp.nbuf = g.nbuf;
+    gp.wide = g.wide;
     cudaError_t e;
     switch (s.qtype) {
-    case kQ4K: e = launch_gemm<kQ4K>(tm, tw, gp, g, stream); break;
-    case kQ5K: e = launch_gemm<kQ5K>(tm, tw, gp, g, stream); break;
-    default: e = launch_gemm<kQ6K>(tm, tw, gp, g, stream); break;
+    case kQ4K: e = g.wide ? launch_gemm<kQ4K, true>(tm, tw, gp, g, stream) : launch_gemm<kQ4K, false>(tm, tw, gp, g, stream); break;
+    case kQ5K: e = g.wide ? launch_gemm<kQ5K, true>(tm, tw, gp, g, stream) : launch_gemm<kQ5K, false>(tm, tw, gp, g, stream); break;
+    default: e = g.wide ? launch_gemm<kQ6K, true>(tm, tw, gp, g, stream) : launch_gemm<kQ6K, false>(tm, tw, gp, g, stream); break;
     }
     if (e != cudaSuccess) {
         set_error("gemm launch failed: %s", cudaGetErrorString(e));
