@@ -475,6 +475,37 @@ def secondary_q6k(ctx, args):
             "l2": f"{nc} rotated weight copies ({nc * nb / 1e6:.0f} MB), L2 flushed before the timed region"}
 
 
+def secondary_upstream(ctx, args):
+    """The headline's weight (11008 outputs x 2048 inputs, Q4_K) in the
+    upstream GGUF orientation, through vkq_matmul_upstream."""
+    torch = ctx.torch
+    from vibrant_b200 import synth, vkq
+    from vibrant_b200 import tensor as vt
+    qt, K, N = synth.Q4_K, 2048, 11008
+    base = vt.QuantWeight(qt, K, N, synth.weights(qt, K, N, seed=5), device=ctx.dev)
+    nc = n_copies(base.nbytes)
+    copies = [base] + [_clone(base) for _ in range(nc - 1)]
+    x = torch.from_numpy(synth.activations(1, K, seed=6)).to(ctx.dev)
+    y = torch.empty(1, N, device=ctx.dev)
+
+    def step(i):
+        c = copies[i % nc]
+        vkq.matmul_upstream(qt, c.buf.data_ptr(), c.nbytes, K, N, x.data_ptr(), 1, y.data_ptr(), device=ctx.local,
+                            stream=ctx.stream)
+
+    dt = timed_graph(ctx, step, max(20, min(args.steps, 200)), 5)
+    ctx.status("the upstream-orientation GEMV")
+    b = algorithmic_bytes(qt, K, N, 1)
+    gbs = b / dt / 1e9
+    return {"workload": "q4k_upstream_gemv_11008x2048", "value": round(gbs, 2), "unit": "GB/s",
+            "us_per_launch": round(dt * 1e6, 3),
+            "orientation": "upstream GGUF [out][in]: row n = the 8 super-blocks of output n along K",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": ctx.hbm, "unit": "GB/s",
+                         "frac": round(gbs / ctx.hbm, 4), "traffic": None, "peak_kind": ctx.peak_kind,
+                         "kernel": "vkq::gemv_rows_kernel<Q4_K,1>", "algorithmic_bytes_per_launch": b},
+            "l2": f"{nc} rotated weight copies ({nc * base.nbytes / 1e6:.0f} MB), L2 flushed before the timed region"}
+
+
 def secondary_gemm(ctx, args):
     name = "q5k_prefill_gemm_512x2048x11008"
     dt, qt, K, N, M, nc, nb = gemv_workload(ctx, name, max(20, min(args.steps, 200)))
@@ -773,6 +804,7 @@ def sweep_14b(ctx, args):
 # ---------------------------------------------------------------- driver
 SECONDARY = (("q6k_vocab_gemv_2048x151936", secondary_q6k, True),
              ("q5k_prefill_gemm_512x2048x11008", secondary_gemm, True),
+             ("q4k_upstream_gemv_11008x2048", secondary_upstream, True),
              ("decode_3b", decode_3b, False),
              ("decode_sweep_14b", sweep_14b, False))
 

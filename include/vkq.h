@@ -130,6 +130,18 @@ VKQ_API int vkq_matmul_host(int device, int qtype, const void *w, int64_t w_byte
                             const float *x_host, int64_t M, float *y_host, float *x_dev, float *y_dev,
                             void *workspace, size_t workspace_bytes, void *stream);
 
+/* The upstream GGUF orientation, behind an entry point of its own: a weight
+ * stored [N rows][K] as GGUF files written by other engines hold a linear
+ * layer ([out][in]: row n is the K/256 super-blocks of output n along K, so
+ * W[n][k] = value n*K + k of the stream), where vibrant's loader reads value
+ * k*N + n as W[k][n] (internal/gguf/loader.go:24-27) and every other entry
+ * point of this library follows vibrant.  y[m][n] = sum_k x[m][k] * W[n][k],
+ * fp32 accumulate within max relative error 1e-5 of sum_k |x w|; needs
+ * K % 256 == 0 and x 16-byte aligned; any M (a warp per output row, four
+ * rows of x per launch); no workspace. */
+VKQ_API int vkq_matmul_upstream(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
+                                const float *x, int64_t M, float *y, void *stream);
+
 /* The fp32-class GEMV path of vkq_matmul, for 1 <= M <= 8 (decode): the
  * Q4_K column-strip kernel (M == 1, N % 256 == 0), the tensor-core kernel
  * (M <= 4; dequantized quants and per-sub-block scaled x split into three

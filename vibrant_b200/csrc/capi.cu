@@ -320,6 +320,24 @@ int vkq_matmul(int device, int qtype, const void *w, int64_t w_bytes, int64_t K,
     return VKQ_OK;
 }
 
+int vkq_matmul_upstream(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N, const float *x,
+                        int64_t M, float *y, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    st = check_matmul_args(qtype, w, w_bytes, K, N, x, M, y);  // the same blocks: ceil(K*N/256)
+    if (st) return st;
+    if (K % 256 != 0) {
+        set_error("vkq_matmul_upstream needs K %% 256 == 0 (rows of whole super-blocks), got K=%lld", (long long)K);
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 15u) {
+        set_error("vkq_matmul_upstream needs x 16-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(gemv_rows_launch(qtype, w, K, N, x, M, y, (cudaStream_t)stream, device),
+                        "upstream-orientation GEMV launch");
+}
+
 int vkq_matmul_host(int device, int qtype, const void *w, int64_t w_bytes, int64_t K, int64_t N,
                     const float *x_host, int64_t M, float *y_host, float *x_dev, float *y_dev, void *workspace,
                     size_t workspace_bytes, void *stream) {

@@ -118,6 +118,12 @@ int gemv_strip_gather(const GemvShape &s, const void *w, int64_t w_bytes, const 
                       cudaStream_t stream, int device);
 int gemv_strip_read_status();  // reads and clears the column-strip kernel's device status word
 
+// fp32 GEMV for weights in the upstream GGUF orientation (gemv_rows.cu):
+// y[m][n] = sum_k x[m][k] * W[n][k], W[n][k] = value n*K + k; K % 256 == 0,
+// x 16-byte aligned, any M (four rows of x per launch).
+cudaError_t gemv_rows_launch(int qtype, const void *w, int64_t K, int64_t N, const float *x, int64_t M, float *y,
+                             cudaStream_t s, int device);
+
 // bf16 tensor-core GEMM (tcgen05), any M; needs N % 32 == 0 and K % 8 == 0.
 size_t gemm_workspace_bytes(const GemvShape &s, int device);
 int gemm_launch(const GemvShape &s, const void *w, int64_t w_bytes, const float *x, float *y, void *ws,

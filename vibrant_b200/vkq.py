@@ -37,6 +37,7 @@ SIGNATURES = {
     "vkq_gemv": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
     "vkq_gemm": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _sz, _vp]),
     "vkq_matmul_host": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "vkq_matmul_upstream": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "vkq_gemv_noalloc": (_int, [_int, _int, _vp, _i64, _i64, _i64, _vp, _i64, _vp, _vp]),
     "vkq_device_status": (_int, [_int, ctypes.POINTER(_int)]),
     "vkq_ipc_alloc": (_int, [_int, _sz, ctypes.POINTER(_vp), ctypes.POINTER(ctypes.c_ubyte * 64)]),
@@ -157,6 +158,13 @@ def gemm(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: in
          ws_ptr: int | None, ws_bytes: int, device: int = -1, stream=None) -> None:
     _check(load().vkq_gemm(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, ws_ptr, ws_bytes,
                            _stream_ptr(stream)))
+
+
+def matmul_upstream(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_ptr: int, M: int, y_ptr: int,
+                    device: int = -1, stream=None) -> None:
+    """vkq_matmul_upstream: y[m][n] = sum_k x[m][k] * W[n][k] for a weight in
+    the upstream GGUF orientation (row n = the blocks of output n along K)."""
+    _check(load().vkq_matmul_upstream(device, qtype, w_ptr, w_bytes, K, N, x_ptr, M, y_ptr, _stream_ptr(stream)))
 
 
 def matmul_host(qtype: int, w_ptr: int, w_bytes: int, K: int, N: int, x_host_ptr: int, M: int, y_host_ptr: int,
