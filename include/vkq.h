@@ -196,6 +196,22 @@ VKQ_API int vkq_silu_mul(int device, const float *gate, const float *up, float *
 VKQ_API int vkq_rms_norm(int device, const float *x, const float *weight, float *out, int64_t rows, int64_t n,
                          float eps, void *stream);
 
+/* Rotary position embedding over interleaved pairs: replaces rope_f32
+ * (internal/gpu/cuda/kernels.cu:363-414, launched by LaunchRoPEKernel,
+ * internal/gpu/cuda/library.go:397-415) with the arithmetic of
+ * RoPE.ApplyRotation (internal/transformer/rope.go:49-124).  x and out are
+ * [batch][heads][seq][head_dim] float32 (8-byte aligned, may be the same
+ * buffer); cos_table and sin_table [max_seq][head_dim / 2] (as NewRoPE,
+ * rope.go:19-43, builds them); positions[seq] (int32) the position of each
+ * token.  Pair i of a token at position p: out[2i] = x[2i]*c - x[2i+1]*s,
+ * out[2i+1] = x[2i]*s + x[2i+1]*c with c, s at table entry p*head_dim/2 + i,
+ * each product and sum rounded on its own: bit-identical to the reference's
+ * float32 results.  A position outside [0, max_seq) leaves its pairs
+ * unwritten; vkq_device_status then reports VKQ_ERR_INVALID_ARGUMENT. */
+VKQ_API int vkq_rope_f32(int device, const float *x, float *out, const float *cos_table, const float *sin_table,
+                         const int32_t *positions, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                         int64_t max_seq, void *stream);
+
 /* The fused linears of a decode step: one launch over `nweights` Q4_K
  * weights [K, N_i] (N_i % 256 == 0, 16-byte aligned) that share the input
  * x [M, K] (4-byte aligned):

@@ -106,3 +106,15 @@ def test_build_never_flushes_subnormals():
     flags = build.NVCC_FLAGS
     assert "-ftz=false" in flags
     assert not any(f in flags for f in ("--use_fast_math", "-use_fast_math", "-ftz=true", "--ftz=true"))
+
+
+def test_rope_tables_follow_the_reference_formula():
+    """rope_tables restates NewRoPE (internal/transformer/rope.go:19-43)."""
+    import math
+    from vibrant_b200 import vkq
+    c, s = vkq.rope_tables(64, 10000.0, 16)
+    assert c.shape == (16, 32) and c.dtype == np.float32
+    for pos, i in [(0, 0), (1, 0), (5, 7), (15, 31)]:
+        angle = pos * (1.0 / math.pow(10000.0, 2 * i / 64))
+        assert abs(float(c[pos, i]) - math.cos(angle)) <= 1e-7
+        assert abs(float(s[pos, i]) - math.sin(angle)) <= 1e-7

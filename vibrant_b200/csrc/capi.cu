@@ -518,6 +518,25 @@ int vkq_rms_norm(int device, const float *x, const float *weight, float *out, in
     return check_launch(rms_norm(x, weight, out, rows, n, eps, (cudaStream_t)stream), "rms_norm");
 }
 
+int vkq_rope_f32(int device, const float *x, float *out, const float *cos_table, const float *sin_table,
+                 const int32_t *positions, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t max_seq,
+                 void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (!x || !out || !cos_table || !sin_table || !positions || batch <= 0 || heads <= 0 || seq <= 0 ||
+        head_dim <= 0 || head_dim % 2 != 0 || max_seq <= 0 || batch * heads * seq > (int64_t(1) << 40) / head_dim) {
+        set_error("invalid arguments to vkq_rope_f32 (head_dim must be even, every count positive)");
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 7u) {
+        set_error("vkq_rope_f32 needs x and out 8-byte aligned");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(rope(x, out, cos_table, sin_table, positions, batch * heads * seq, seq, head_dim, max_seq,
+                             (cudaStream_t)stream, device),
+                        "rope");
+}
+
 size_t vkq_gather_channel_bytes(int64_t m_max, int64_t N) {
     return m_max > 0 && N > 0 ? gather_channel_bytes(m_max, N) : 0;
 }
@@ -647,10 +666,12 @@ int vkq_device_status(int device, int *code) {
     const int g2 = gemm_read_status();
     const int g3 = gemv_tc_read_status();
     const int g4 = gemv_strip_read_status();
+    const int g5 = elem_read_status();
     if (g == 0) g = g2;
     if (g == 0) g = g3;
     if (g == 0) g = g4;
-    if (g < 0 || g2 < 0 || g3 < 0 || g4 < 0) {
+    if (g == 0) g = g5;
+    if (g < 0 || g2 < 0 || g3 < 0 || g4 < 0 || g5 < 0) {
         set_error("cannot read the device status word");
         return VKQ_ERR_CUDA;
     }

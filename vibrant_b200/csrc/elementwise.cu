@@ -65,6 +65,45 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const float *__r
     for (int64_t i = threadIdx.x; i < n; i += kNormThreads) yr[i] = (xr[i] / r) * weight[i];
 }
 
+static __device__ int g_elem_status;
+
+// Rotary position embedding over interleaved pairs, as the reference's
+// rope_f32 (internal/gpu/cuda/kernels.cu:363-414) and its CPU path
+// RoPE.ApplyRotation (internal/transformer/rope.go:49-124): x and out are
+// [rows][half pairs] with rows = batch * heads * seq and seq the fastest of
+// the three ([batch][head][seq][dim]); pair i of a token at position p is
+// rotated by cos/sin table entry p * half + i:
+//   out[2i] = x[2i]*c - x[2i+1]*s,  out[2i+1] = x[2i]*s + x[2i+1]*c,
+// each product and each sum rounded on its own (no fused multiply-add), as
+// the reference's float32 arithmetic does, so the results are bit-identical.
+// A position outside [0, max_seq) leaves its pairs unwritten and records
+// VKQ_ERR_INVALID_ARGUMENT in the status word.  x and out may be the same.
+__global__ void __launch_bounds__(256) rope_kernel(const float2 *x, float2 *out, const float *__restrict__ cos_t,
+                                                   const float *__restrict__ sin_t, const int *__restrict__ pos,
+                                                   int64_t pairs, int64_t seq, int64_t half, int64_t max_seq) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = p % half, s = (p / half) % seq;
+        const int ps = pos[s];
+        if (ps < 0 || ps >= max_seq) {
+            atomicExch(&g_elem_status, VKQ_ERR_INVALID_ARGUMENT);
+            continue;
+        }
+        const float c = cos_t[(int64_t)ps * half + i], sn = sin_t[(int64_t)ps * half + i];
+        const float2 v = x[p];
+        out[p] = make_float2(__fsub_rn(__fmul_rn(v.x, c), __fmul_rn(v.y, sn)),
+                             __fadd_rn(__fmul_rn(v.x, sn), __fmul_rn(v.y, c)));
+    }
+}
+
+int elem_read_status() {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_elem_status, sizeof(int)) != cudaSuccess) return -1;
+    cudaMemcpyToSymbol(g_elem_status, &zero, sizeof(int));
+    return v;
+}
+
 // dst[0..n) = src[0..n), src being pinned host memory that the device reads
 // through its mapping.  The loads do not depend on the preceding kernel and
 // are issued before griddepcontrol.wait; only the stores into dst (which the
@@ -115,6 +154,17 @@ cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, 
     if (blocks > 4 * sms) blocks = 4 * sms;
     void *args[] = {(void *)&gate, (void *)&up, (void *)&out, (void *)&n};
     return launch_pdl((const void *)silu_mul_kernel, dim3((unsigned)blocks), dim3(256), s, args);
+}
+
+cudaError_t rope(const float *x, float *out, const float *cos_t, const float *sin_t, const int *positions,
+                 int64_t rows, int64_t seq, int64_t head_dim, int64_t max_seq, cudaStream_t s, int device) {
+    const int64_t half = head_dim / 2, pairs = rows * half;
+    int64_t blocks = (pairs + 255) / 256;
+    const int64_t cap = 8 * (int64_t)device_sm_count(device);
+    if (blocks > cap) blocks = cap;
+    void *args[] = {(void *)&x, (void *)&out, (void *)&cos_t, (void *)&sin_t, (void *)&positions,
+                    (void *)&pairs, (void *)&seq, (void *)&half, (void *)&max_seq};
+    return launch_pdl((const void *)rope_kernel, dim3((unsigned)blocks), dim3(256), s, args);
 }
 
 cudaError_t stage_in(const float *src_mapped, float *dst, int64_t n, cudaStream_t s) {

@@ -134,6 +134,12 @@ int gemm_read_status();  // reads and clears this TU's device status word (synch
 cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, cudaStream_t s, int device);
 cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,
                      cudaStream_t s);
+// Rotary position embedding over interleaved pairs (elementwise.cu): x and
+// out [rows][head_dim] with rows = batch * heads * seq, seq the fastest;
+// tables [max_seq][head_dim / 2]; 8-byte aligned x, out.
+cudaError_t rope(const float *x, float *out, const float *cos_t, const float *sin_t, const int *positions,
+                 int64_t rows, int64_t seq, int64_t head_dim, int64_t max_seq, cudaStream_t s, int device);
+int elem_read_status();  // reads and clears the elementwise kernels' status word
 // dst[0..n) = src[0..n) from pinned host memory through its device mapping
 // (elementwise.cu), as a kernel that takes part in programmatic dependent launch.
 cudaError_t stage_in(const float *src_mapped, float *dst, int64_t n, cudaStream_t s);

@@ -54,6 +54,7 @@ SIGNATURES = {
                                           _int, _vp]),
     "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
+    "vkq_rope_f32": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "vkq_linear_fused": (_int, [_int, _int, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64,
                                 ctypes.POINTER(_i64), _vp, _i64, _vp, ctypes.c_float, _int, ctypes.POINTER(_vp), _vp]),
     "vkq_gguf_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
@@ -203,6 +204,28 @@ def rms_norm(x_ptr: int, w_ptr: int, out_ptr: int, rows: int, n: int, eps: float
              stream=None) -> None:
     """vkq_rms_norm: out[r] = x[r] / sqrt(mean(x[r]^2) + eps) * weight."""
     _check(load().vkq_rms_norm(device, x_ptr, w_ptr, out_ptr, rows, n, eps, _stream_ptr(stream)))
+
+
+def rope_f32(x_ptr: int, out_ptr: int, cos_ptr: int, sin_ptr: int, pos_ptr: int, batch: int, heads: int, seq: int,
+             head_dim: int, max_seq: int, device: int = -1, stream=None) -> None:
+    """vkq_rope_f32: rotary position embedding over interleaved pairs of
+    x [batch][heads][seq][head_dim] with cos/sin tables [max_seq][head_dim/2]."""
+    _check(load().vkq_rope_f32(device, x_ptr, out_ptr, cos_ptr, sin_ptr, pos_ptr, batch, heads, seq, head_dim,
+                               max_seq, _stream_ptr(stream)))
+
+
+def rope_tables(head_dim: int, freq_base: float, max_seq: int):
+    """cos and sin tables [max_seq][head_dim/2] as float32 numpy arrays, built
+    as the reference's NewRoPE (internal/transformer/rope.go:19-43) builds
+    them: angle = pos / freq_base^(2i/head_dim) in float64, then cos and sin
+    rounded to float32 (this host's libm may differ from Go's math package in
+    the last bit of an entry; the kernel takes the tables as given)."""
+    import numpy as np
+    half = head_dim // 2
+    i = np.arange(half, dtype=np.float64)
+    freq = 1.0 / np.power(freq_base, 2.0 * i / head_dim)
+    angle = np.arange(max_seq, dtype=np.float64)[:, None] * freq[None, :]
+    return np.cos(angle).astype(np.float32), np.sin(angle).astype(np.float32)
 
 
 def device_status(device: int = -1) -> int:
