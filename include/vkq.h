@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define VKQ_ABI_VERSION 3
+#define VKQ_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define VKQ_API __attribute__((visibility("default")))
