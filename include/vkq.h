@@ -212,6 +212,20 @@ VKQ_API int vkq_rope_f32(int device, const float *x, float *out, const float *co
                          const int32_t *positions, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                          int64_t max_seq, void *stream);
 
+/* Decode attention, one query token per sequence against its KV cache:
+ * replaces computeAttention (internal/transformer/attention.go:316-363) for
+ * the reference's decode step, where the new token's K and V are appended to
+ * the cache (:147-162), grouped KV heads are shared (expandKVHeads, :280-314)
+ * and no mask applies (applyCausalMask :429-460, one query row):
+ *   o[b][h] = softmax(q[b][h] . K[b][h / g]^T * float32(1/sqrt(D))) . V[b][h / g]
+ * with g = heads / kv_heads.  q and out are [batch][heads][D]; the caches are
+ * [batch][kv_heads][cache_len][D] with rows 0 .. len-1 valid (cache_len is
+ * the allocated length, >= len).  D = 64 or 128; len <= 51200.  fp32, within
+ * 1e-5 of sum_j p_j |v_j| of the reference's arithmetic. */
+VKQ_API int vkq_attention_decode_f32(int device, const float *q, const float *k_cache, const float *v_cache,
+                                     float *out, int64_t batch, int64_t heads, int64_t kv_heads, int64_t len,
+                                     int64_t cache_len, int64_t head_dim, void *stream);
+
 /* The fused linears of a decode step: one launch over `nweights` Q4_K
  * weights [K, N_i] (N_i % 256 == 0, 16-byte aligned) that share the input
  * x [M, K] (4-byte aligned):

@@ -1,0 +1,99 @@
+"""vkq_attention_decode_f32: one query token per sequence against its KV
+cache, against a float64 restatement of the reference's decode attention
+(computeAttention, internal/transformer/attention.go:316-363, with the cache
+of :147-162, grouped KV heads of expandKVHeads :280-314 and no mask for one
+query row).  Parity bar: each output within 1e-5 of sum_j p_j |v_j|."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(q, kc, vc, length, heads, kv_heads):
+    B, H, D = q.shape
+    g = heads // kv_heads
+    out = np.empty((B, H, D))
+    bound = np.empty((B, H, D))
+    scale = np.float64(np.float32(1.0 / np.sqrt(D)))
+    for b in range(B):
+        for h in range(H):
+            k = kc[b, h // g, :length].astype(np.float64)
+            v = vc[b, h // g, :length].astype(np.float64)
+            s = (k @ q[b, h].astype(np.float64)) * scale
+            p = np.exp(s - s.max())
+            p /= p.sum()
+            out[b, h] = p @ v
+            bound[b, h] = p @ np.abs(v)
+    return out, bound
+
+
+def _run(q, kc, vc, length):
+    import torch
+    from vibrant_b200 import vkq
+    B, H, D = q.shape
+    KVH, cap = kc.shape[1], kc.shape[2]
+    qt, kt, vt = (torch.from_numpy(a).cuda() for a in (q, kc, vc))
+    o = torch.full((B, H, D), float("nan"), device="cuda")
+    vkq.attention_decode_f32(qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), o.data_ptr(), B, H, KVH, length, cap, D,
+                             device=0)
+    torch.cuda.synchronize()
+    assert vkq.device_status(0) == vkq.OK
+    return o.cpu().numpy()
+
+
+@pytest.mark.parametrize("B,H,KVH,D,length,cap", [
+    (1, 16, 2, 128, 1, 1),          # the first token: p = 1
+    (1, 16, 2, 128, 7, 64),         # 3B-class heads (16 query, 2 KV), a preallocated cache
+    (1, 16, 2, 128, 300, 300),
+    (2, 8, 8, 64, 257, 512),        # no grouping, two sequences
+    (1, 40, 8, 128, 4096, 5000),    # 14B-class heads, a long context
+    (1, 4, 1, 64, 51200, 51200),    # the longest context served
+], ids=lambda v: str(v))
+def test_attention_decode_matches_reference(B, H, KVH, D, length, cap):
+    rng = np.random.default_rng(length + H)
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    kc = rng.standard_normal((B, KVH, cap, D)).astype(np.float32)
+    vc = rng.standard_normal((B, KVH, cap, D)).astype(np.float32)
+    kc[:, :, length:] = np.nan  # rows past the valid length are never read
+    vc[:, :, length:] = np.nan
+    o = _run(q, kc, vc, length)
+    ref, bound = _ref(q, kc, vc, length, H, KVH)
+    err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
+    assert err <= 1e-5, err
+
+
+def test_attention_decode_peaked_scores():
+    """Scores far apart (one key dominates): the max subtraction keeps exp
+    finite and the result follows that key's value row."""
+    B, H, KVH, D, L = 1, 2, 1, 128, 33
+    rng = np.random.default_rng(3)
+    q = (rng.standard_normal((B, H, D)) * 8).astype(np.float32)
+    kc = rng.standard_normal((B, KVH, L, D)).astype(np.float32)
+    kc[0, 0, 17] = q[0, 0] * 4  # key 17 matches head 0's query strongly
+    vc = rng.standard_normal((B, KVH, L, D)).astype(np.float32)
+    o = _run(q, kc, vc, L)
+    ref, bound = _ref(q, kc, vc, L, H, KVH)
+    assert np.isfinite(o).all()
+    assert float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30))) <= 1e-5
+    assert np.allclose(o[0, 0], vc[0, 0, 17], atol=1e-4)
+
+
+def test_attention_decode_error_paths():
+    import torch
+    from vibrant_b200 import vkq
+    buf = torch.zeros(1 << 16, device="cuda")
+    p = buf.data_ptr()
+
+    def call(**kw):
+        a = dict(batch=1, heads=16, kv_heads=2, length=4, cache_len=8, head_dim=128)
+        a.update(kw)
+        vkq.attention_decode_f32(p, p, p, p, a["batch"], a["heads"], a["kv_heads"], a["length"], a["cache_len"],
+                                 a["head_dim"], device=0)
+
+    for bad, status in [(dict(kv_heads=3), vkq.ERR_INVALID_ARGUMENT), (dict(length=9), vkq.ERR_INVALID_ARGUMENT),
+                        (dict(length=0), vkq.ERR_INVALID_ARGUMENT), (dict(head_dim=96), vkq.ERR_UNSUPPORTED),
+                        (dict(length=51201, cache_len=51201), vkq.ERR_INVALID_ARGUMENT)]:
+        with pytest.raises(vkq.VkqError) as e:
+            call(**bad)
+        assert e.value.status == status, bad
+    assert vkq.device_status(0) == vkq.OK

@@ -537,6 +537,34 @@ int vkq_rope_f32(int device, const float *x, float *out, const float *cos_table,
                         "rope");
 }
 
+int vkq_attention_decode_f32(int device, const float *q, const float *k_cache, const float *v_cache, float *out,
+                             int64_t batch, int64_t heads, int64_t kv_heads, int64_t len, int64_t cache_len,
+                             int64_t head_dim, void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (!q || !k_cache || !v_cache || !out || batch <= 0 || batch > 65535 || heads <= 0 || heads > 65535 ||
+        kv_heads <= 0 || heads % kv_heads != 0 || len <= 0 || cache_len < len ||
+        (uint64_t)len > attention_max_len()) {
+        set_error("invalid arguments to vkq_attention_decode_f32 (heads a multiple of kv_heads, 0 < len <= "
+                  "cache_len, len <= %zu)",
+                  attention_max_len());
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (head_dim != 64 && head_dim != 128) {
+        set_error("vkq_attention_decode_f32 serves head_dim 64 or 128 (got %lld)", (long long)head_dim);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+         reinterpret_cast<uintptr_t>(out)) &
+        3u) {
+        set_error("vkq_attention_decode_f32 needs 4-byte aligned buffers");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(attention_decode(q, k_cache, v_cache, out, batch, heads, kv_heads, len, cache_len, head_dim,
+                                         (cudaStream_t)stream),
+                        "decode attention");
+}
+
 size_t vkq_gather_channel_bytes(int64_t m_max, int64_t N) {
     return m_max > 0 && N > 0 ? gather_channel_bytes(m_max, N) : 0;
 }

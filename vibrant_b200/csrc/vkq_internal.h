@@ -134,6 +134,12 @@ int gemm_read_status();  // reads and clears this TU's device status word (synch
 cudaError_t silu_mul(const float *gate, const float *up, float *out, int64_t n, cudaStream_t s, int device);
 cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t rows, int64_t n, float eps,
                      cudaStream_t s);
+// Decode attention (attention.cu): q [batch][heads][D], caches
+// [batch][kv_heads][cache_len][D] with len valid rows, out [batch][heads][D];
+// D = 64 or 128, len <= attention_max_len().
+size_t attention_max_len();
+cudaError_t attention_decode(const float *q, const float *kc, const float *vc, float *o, int64_t batch, int64_t heads,
+                             int64_t kv_heads, int64_t len, int64_t cache_len, int64_t head_dim, cudaStream_t s);
 // Rotary position embedding over interleaved pairs (elementwise.cu): x and
 // out [rows][head_dim] with rows = batch * heads * seq, seq the fastest;
 // tables [max_seq][head_dim / 2]; 8-byte aligned x, out.

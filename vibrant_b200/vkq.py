@@ -55,6 +55,7 @@ SIGNATURES = {
     "vkq_silu_mul": (_int, [_int, _vp, _vp, _vp, _i64, _vp]),
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "vkq_rope_f32": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "vkq_attention_decode_f32": (_int, [_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "vkq_linear_fused": (_int, [_int, _int, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64,
                                 ctypes.POINTER(_i64), _vp, _i64, _vp, ctypes.c_float, _int, ctypes.POINTER(_vp), _vp]),
     "vkq_gguf_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
@@ -212,6 +213,14 @@ def rope_f32(x_ptr: int, out_ptr: int, cos_ptr: int, sin_ptr: int, pos_ptr: int,
     x [batch][heads][seq][head_dim] with cos/sin tables [max_seq][head_dim/2]."""
     _check(load().vkq_rope_f32(device, x_ptr, out_ptr, cos_ptr, sin_ptr, pos_ptr, batch, heads, seq, head_dim,
                                max_seq, _stream_ptr(stream)))
+
+
+def attention_decode_f32(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch: int, heads: int, kv_heads: int,
+                         length: int, cache_len: int, head_dim: int, device: int = -1, stream=None) -> None:
+    """vkq_attention_decode_f32: one query token per sequence against its KV
+    cache (rows 0 .. length-1 of [batch][kv_heads][cache_len][head_dim])."""
+    _check(load().vkq_attention_decode_f32(device, q_ptr, k_ptr, v_ptr, out_ptr, batch, heads, kv_heads, length,
+                                           cache_len, head_dim, _stream_ptr(stream)))
 
 
 def rope_tables(head_dim: int, freq_base: float, max_seq: int):
