@@ -43,6 +43,7 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 ROTATION_BYTES = 512 << 20      # rotated weight copies per GPU: 4x the 126 MB L2
 FLUSH_BYTES = 256 << 20         # L2 flush before every timed region
+CTX_3B = 1024                   # tokens in every layer's KV cache in the 3B decode step
 
 
 def parse():
@@ -564,12 +565,13 @@ class Linear:
 
 def decode_3b(ctx, args):
     """The full 3B-class decode step (config 3): 36 layers of {RMSNorm, q, k,
-    v, o, RMSNorm, gate, up, SiLU*up, down} and the final RMSNorm + Q6_K LM
-    head, batch 1.  Attention itself is outside the matmul path: q's output
-    stands in for the attention output that feeds o.  At N > 1 every linear
-    layer is row-sharded with the all-gather fused into its GEMV, except k
-    and v (256 outputs: replicated, their whole weight is one super-block
-    column)."""
+    v, RoPE on q and k, the new token's K and V appended to the layer's KV
+    cache, attention over the cache, o, RMSNorm, gate, up, SiLU*up, down} and
+    the final RMSNorm + Q6_K LM head, batch 1, at a context of CTX_3B tokens
+    (the caches hold random keys and values for the earlier tokens).  At N > 1
+    every linear layer is row-sharded with the all-gather fused into its
+    GEMV, except k and v (256 outputs: replicated, their whole weight is one
+    super-block column); RoPE and attention then run whole on every rank."""
     torch = ctx.torch
     import numpy as np
     from oracle import kq_oracle
@@ -597,6 +599,34 @@ def decode_3b(ctx, args):
     st = ctx.stream
     taps = {}
 
+    # attention: 16 query / 2 KV heads of 128, this token at position
+    # CTX_3B - 1 of every layer's cache [kv_heads][CTX_3B][128]
+    hd = 128
+    heads, kvh = m["q_out"] // hd, m["kv_out"] // hd
+    cos_t, sin_t = (torch.from_numpy(t).to(ctx.dev) for t in vkq.rope_tables(hd, 1000000.0, CTX_3B))
+    pos = torch.full((1,), CTX_3B - 1, dtype=torch.int32, device=ctx.dev)
+    gen = torch.Generator(device=ctx.dev)
+    gen.manual_seed(31)
+    kcache = [torch.randn(kvh, CTX_3B, hd, device=ctx.dev, generator=gen) for _ in range(m["layers"])]
+    vcache = [torch.randn(kvh, CTX_3B, hd, device=ctx.dev, generator=gen) for _ in range(m["layers"])]
+    q_rot = torch.empty(1, m["q_out"], device=ctx.dev)
+    k_rot = torch.empty(1, m["kv_out"], device=ctx.dev)
+    attn = torch.empty(1, m["q_out"], device=ctx.dev)
+
+    def attend(li, q, k, v):
+        """RoPE on q and k, k and v into row CTX_3B - 1 of the layer's caches,
+        decode attention over the whole cache."""
+        vkq.rope_f32(q.data_ptr(), q_rot.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), pos.data_ptr(), 1, heads,
+                     1, hd, CTX_3B, ctx.local, st)
+        vkq.rope_f32(k.data_ptr(), k_rot.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), pos.data_ptr(), 1, kvh, 1,
+                     hd, CTX_3B, ctx.local, st)
+        with torch.cuda.stream(st):
+            kcache[li][:, CTX_3B - 1].copy_(k_rot.view(kvh, hd), non_blocking=True)
+            vcache[li][:, CTX_3B - 1].copy_(v.view(kvh, hd), non_blocking=True)
+        vkq.attention_decode_f32(q_rot.data_ptr(), kcache[li].data_ptr(), vcache[li].data_ptr(), attn.data_ptr(), 1,
+                                 heads, kvh, CTX_3B, CTX_3B, hd, ctx.local, st)
+        return attn
+
     # q|k|v and gate|up(+SiLU) in one launch each, RMSNorm folded in; on
     # several GPUs q and gate|up are this rank's shards, gathered in the
     # launch, and k, v whole on every rank
@@ -623,7 +653,7 @@ def decode_3b(ctx, args):
         x = x0
         for li, lay in enumerate(layers):
             q = qkv(x, lay)
-            o = lay["o"](q)
+            o = lay["o"](attend(li, q, qkv_out[1], qkv_out[2]))
             a = gate_up(o, lay)
             x = lay["down"](a)
         vkq.rms_norm(x.data_ptr(), norm_w.data_ptr(), h.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
@@ -634,9 +664,9 @@ def decode_3b(ctx, args):
         for li, lay in enumerate(layers):
             vkq.rms_norm(x.data_ptr(), norm_w.data_ptr(), h.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
             q = lay["q"](h)
-            lay["k"](h)
-            lay["v"](h)
-            o = lay["o"](q)
+            k = lay["k"](h)
+            v = lay["v"](h)
+            o = lay["o"](attend(li, q, k, v))
             vkq.rms_norm(o.data_ptr(), norm_w.data_ptr(), h2.data_ptr(), 1, m["hidden"], 1e-6, ctx.local, st)
             g = lay["gate"](h2)
             u = lay["up"](h2)
@@ -671,11 +701,14 @@ def decode_3b(ctx, args):
     for c in chans.values():
         c.close()
     nbytes = synth.model_bytes(m)
-    launches = m["layers"] * (4 if fused else 10) + 2
+    kv_bytes = m["layers"] * 2 * kvh * CTX_3B * hd * 4  # the caches attention reads, K and V
+    # per layer: rope q, rope k, attention (+ the 2 torch copies appending K and V, not counted)
+    launches = m["layers"] * ((4 if fused else 10) + 3) + 2
     return {"workload": "decode_3b_q4k_q6k_36x2048", "value": round(1.0 / dt, 2), "unit": "tokens/s",
             "ms_per_token": round(dt * 1e3, 4), "weight_bytes_per_token": nbytes,
-            "gbs": round(nbytes / dt / 1e9, 1),
-            "hbm_frac_per_gpu": round(nbytes / dt / 1e9 / ctx.world / ctx.hbm, 4),
+            "context_tokens": CTX_3B, "kv_cache_bytes_per_token": kv_bytes,
+            "gbs": round((nbytes + kv_bytes) / dt / 1e9, 1),
+            "hbm_frac_per_gpu": round((nbytes / ctx.world + kv_bytes) / dt / 1e9 / ctx.hbm, 4),
             "launches_per_token": launches, "parity_layer0_q_max_rel_err": err,
             "fused": ("rms_norm+q|k|v and rms_norm+gate|up+SiLU*up in one launch each "
                       + ("(vkq_linear_fused_allgather: q and gate|up sharded and gathered in the launch)"

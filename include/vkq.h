@@ -220,8 +220,8 @@ VKQ_API int vkq_rope_f32(int device, const float *x, float *out, const float *co
  *   o[b][h] = softmax(q[b][h] . K[b][h / g]^T * float32(1/sqrt(D))) . V[b][h / g]
  * with g = heads / kv_heads.  q and out are [batch][heads][D]; the caches are
  * [batch][kv_heads][cache_len][D] with rows 0 .. len-1 valid (cache_len is
- * the allocated length, >= len).  D = 64 or 128; len <= 51200.  fp32, within
- * 1e-5 of sum_j p_j |v_j| of the reference's arithmetic. */
+ * the allocated length, >= len).  D = 64 or 128; len <= 409600.  fp32, within
+ * 1e-5 of sum_j p_j |v_j| of the reference's arithmetic.  Allocates nothing. */
 VKQ_API int vkq_attention_decode_f32(int device, const float *q, const float *k_cache, const float *v_cache,
                                      float *out, int64_t batch, int64_t heads, int64_t kv_heads, int64_t len,
                                      int64_t cache_len, int64_t head_dim, void *stream);

@@ -27,12 +27,20 @@ def _ref(q, kc, vc, length, heads, kv_heads):
     return out, bound
 
 
-def _run(q, kc, vc, length):
+def _run(q, kc, vc, length, shift=0):
+    """shift > 0 places q and the caches that many floats past an aligned
+    start, so that no lane's values form a whole vector."""
     import torch
     from vibrant_b200 import vkq
     B, H, D = q.shape
     KVH, cap = kc.shape[1], kc.shape[2]
-    qt, kt, vt = (torch.from_numpy(a).cuda() for a in (q, kc, vc))
+
+    def dev(a):
+        t = torch.empty(a.size + shift, device="cuda")
+        t[shift:] = torch.from_numpy(a.reshape(-1)).cuda()
+        return t[shift:]
+
+    qt, kt, vt = dev(q), dev(kc), dev(vc)
     o = torch.full((B, H, D), float("nan"), device="cuda")
     vkq.attention_decode_f32(qt.data_ptr(), kt.data_ptr(), vt.data_ptr(), o.data_ptr(), B, H, KVH, length, cap, D,
                              device=0)
@@ -41,13 +49,17 @@ def _run(q, kc, vc, length):
     return o.cpu().numpy()
 
 
+# The cluster size (CTAs splitting one head's keys) follows from len and
+# heads x batch: 1 for the shortest, 4 with a ragged last chunk for 257 and
+# 300 keys, 8 for 512 and 4096 keys, and 8 chunks of 51,200 for the longest.
 @pytest.mark.parametrize("B,H,KVH,D,length,cap", [
     (1, 16, 2, 128, 1, 1),          # the first token: p = 1
     (1, 16, 2, 128, 7, 64),         # 3B-class heads (16 query, 2 KV), a preallocated cache
     (1, 16, 2, 128, 300, 300),
+    (1, 16, 2, 128, 512, 512),      # 3B-class heads at a 512-token context
     (2, 8, 8, 64, 257, 512),        # no grouping, two sequences
     (1, 40, 8, 128, 4096, 5000),    # 14B-class heads, a long context
-    (1, 4, 1, 64, 51200, 51200),    # the longest context served
+    (1, 4, 1, 64, 409600, 409600),  # the longest context served
 ], ids=lambda v: str(v))
 def test_attention_decode_matches_reference(B, H, KVH, D, length, cap):
     rng = np.random.default_rng(length + H)
@@ -57,6 +69,20 @@ def test_attention_decode_matches_reference(B, H, KVH, D, length, cap):
     kc[:, :, length:] = np.nan  # rows past the valid length are never read
     vc[:, :, length:] = np.nan
     o = _run(q, kc, vc, length)
+    ref, bound = _ref(q, kc, vc, length, H, KVH)
+    err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
+    assert err <= 1e-5, err
+
+
+@pytest.mark.parametrize("D,length", [(128, 300), (64, 1000)])
+def test_attention_decode_unaligned_buffers(D, length):
+    """q and the caches one float past a 16-byte boundary: scalar lane loads."""
+    B, H, KVH = 1, 8, 2
+    rng = np.random.default_rng(D + length)
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    kc = rng.standard_normal((B, KVH, length, D)).astype(np.float32)
+    vc = rng.standard_normal((B, KVH, length, D)).astype(np.float32)
+    o = _run(q, kc, vc, length, shift=1)
     ref, bound = _ref(q, kc, vc, length, H, KVH)
     err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
     assert err <= 1e-5, err
@@ -92,7 +118,7 @@ def test_attention_decode_error_paths():
 
     for bad, status in [(dict(kv_heads=3), vkq.ERR_INVALID_ARGUMENT), (dict(length=9), vkq.ERR_INVALID_ARGUMENT),
                         (dict(length=0), vkq.ERR_INVALID_ARGUMENT), (dict(head_dim=96), vkq.ERR_UNSUPPORTED),
-                        (dict(length=51201, cache_len=51201), vkq.ERR_INVALID_ARGUMENT)]:
+                        (dict(length=409601, cache_len=409601), vkq.ERR_INVALID_ARGUMENT)]:
         with pytest.raises(vkq.VkqError) as e:
             call(**bad)
         assert e.value.status == status, bad
