@@ -609,22 +609,14 @@ def decode_3b(ctx, args):
     gen.manual_seed(31)
     kcache = [torch.randn(kvh, CTX_3B, hd, device=ctx.dev, generator=gen) for _ in range(m["layers"])]
     vcache = [torch.randn(kvh, CTX_3B, hd, device=ctx.dev, generator=gen) for _ in range(m["layers"])]
-    q_rot = torch.empty(1, m["q_out"], device=ctx.dev)
-    k_rot = torch.empty(1, m["kv_out"], device=ctx.dev)
     attn = torch.empty(1, m["q_out"], device=ctx.dev)
 
     def attend(li, q, k, v):
-        """RoPE on q and k, k and v into row CTX_3B - 1 of the layer's caches,
-        decode attention over the whole cache."""
-        vkq.rope_f32(q.data_ptr(), q_rot.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), pos.data_ptr(), 1, heads,
-                     1, hd, CTX_3B, ctx.local, st)
-        vkq.rope_f32(k.data_ptr(), k_rot.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), pos.data_ptr(), 1, kvh, 1,
-                     hd, CTX_3B, ctx.local, st)
-        with torch.cuda.stream(st):
-            kcache[li][:, CTX_3B - 1].copy_(k_rot.view(kvh, hd), non_blocking=True)
-            vcache[li][:, CTX_3B - 1].copy_(v.view(kvh, hd), non_blocking=True)
-        vkq.attention_decode_f32(q_rot.data_ptr(), kcache[li].data_ptr(), vcache[li].data_ptr(), attn.data_ptr(), 1,
-                                 heads, kvh, CTX_3B, CTX_3B, hd, ctx.local, st)
+        """RoPE on q and k, the new K and V appended at row CTX_3B - 1 of the
+        layer's caches and attention over the whole cache, in one launch."""
+        vkq.attention_rope_decode_f32(q.data_ptr(), k.data_ptr(), v.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(),
+                                      pos.data_ptr(), kcache[li].data_ptr(), vcache[li].data_ptr(), attn.data_ptr(),
+                                      1, heads, kvh, CTX_3B, CTX_3B, hd, CTX_3B, ctx.local, st)
         return attn
 
     # q|k|v and gate|up(+SiLU) in one launch each, RMSNorm folded in; on
@@ -702,8 +694,7 @@ def decode_3b(ctx, args):
         c.close()
     nbytes = synth.model_bytes(m)
     kv_bytes = m["layers"] * 2 * kvh * CTX_3B * hd * 4  # the caches attention reads, K and V
-    # per layer: rope q, rope k, attention (+ the 2 torch copies appending K and V, not counted)
-    launches = m["layers"] * ((4 if fused else 10) + 3) + 2
+    launches = m["layers"] * ((4 if fused else 10) + 1) + 2  # + the fused RoPE/append/attention launch
     return {"workload": "decode_3b_q4k_q6k_36x2048", "value": round(1.0 / dt, 2), "unit": "tokens/s",
             "ms_per_token": round(dt * 1e3, 4), "weight_bytes_per_token": nbytes,
             "context_tokens": CTX_3B, "kv_cache_bytes_per_token": kv_bytes,

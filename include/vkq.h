@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define VKQ_ABI_VERSION 4
+#define VKQ_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define VKQ_API __attribute__((visibility("default")))
@@ -225,6 +225,28 @@ VKQ_API int vkq_rope_f32(int device, const float *x, float *out, const float *co
 VKQ_API int vkq_attention_decode_f32(int device, const float *q, const float *k_cache, const float *v_cache,
                                      float *out, int64_t batch, int64_t heads, int64_t kv_heads, int64_t len,
                                      int64_t cache_len, int64_t head_dim, void *stream);
+
+/* The decode branch of Attention.Forward after its projections, in one
+ * launch: replaces, for one new token per sequence, ApplyRotation on q and k
+ * (internal/transformer/attention.go:141-143, rope.go:49-124), the cache
+ * concatenation (attention.go:146-162, concatenateSeqDim) and
+ * expandKVHeads + computeAttention (:164-172).  q [batch][heads][D], k_new
+ * and v_new [batch][kv_heads][D] are the projections before RoPE;
+ * positions[batch] (int32) the new token's position, cos_table and
+ * sin_table [max_seq][D / 2] as for vkq_rope_f32.  q and k_new are rotated
+ * with vkq_rope_f32's arithmetic (bit-identical), the rotated k_new and
+ * v_new are stored at row len - 1 of k_cache and v_cache
+ * ([batch][kv_heads][cache_len][D], rows 0 .. len-2 already valid), and out
+ * [batch][heads][D] is vkq_attention_decode_f32 over rows 0 .. len-1, within
+ * the same 1e-5 of sum_j p_j |v_j|.  Same limits as vkq_attention_decode_f32;
+ * 4-byte aligned buffers; allocates nothing.  A position outside
+ * [0, max_seq) leaves that sequence's out and cache rows unwritten, and
+ * vkq_device_status then reports VKQ_ERR_INVALID_ARGUMENT. */
+VKQ_API int vkq_attention_rope_decode_f32(int device, const float *q, const float *k_new, const float *v_new,
+                                          const float *cos_table, const float *sin_table, const int32_t *positions,
+                                          float *k_cache, float *v_cache, float *out, int64_t batch, int64_t heads,
+                                          int64_t kv_heads, int64_t len, int64_t cache_len, int64_t head_dim,
+                                          int64_t max_seq, void *stream);
 
 /* The fused linears of a decode step: one launch over `nweights` Q4_K
  * weights [K, N_i] (N_i % 256 == 0, 16-byte aligned) that share the input

@@ -123,3 +123,86 @@ def test_attention_decode_error_paths():
             call(**bad)
         assert e.value.status == status, bad
     assert vkq.device_status(0) == vkq.OK
+
+
+def _rope_rows(x, cos_t, sin_t, pos):
+    """float32 RoPE of rows x [..., D] at one position, each product and sum
+    rounded on its own (RoPE.ApplyRotation, rope.go:49-124)."""
+    c, s = cos_t[pos], sin_t[pos]
+    x0, x1 = x[..., 0::2], x[..., 1::2]
+    out = np.empty_like(x)
+    out[..., 0::2] = x0 * c - x1 * s
+    out[..., 1::2] = x0 * s + x1 * c
+    return out
+
+
+def _run_step(q, k_new, v_new, kc, vc, length, positions, max_seq, base=1000000.0):
+    import torch
+    from vibrant_b200 import vkq
+    B, H, D = q.shape
+    KVH, cap = kc.shape[1], kc.shape[2]
+    cos_t, sin_t = vkq.rope_tables(D, base, max_seq)
+    t = {k: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+         for k, a in dict(q=q, kn=k_new, vn=v_new, kc=kc, vc=vc, cos=cos_t, sin=sin_t,
+                          pos=np.asarray(positions, dtype=np.int32)).items()}
+    o = torch.full((B, H, D), float("nan"), device="cuda")
+    vkq.attention_rope_decode_f32(t["q"].data_ptr(), t["kn"].data_ptr(), t["vn"].data_ptr(), t["cos"].data_ptr(),
+                                  t["sin"].data_ptr(), t["pos"].data_ptr(), t["kc"].data_ptr(), t["vc"].data_ptr(),
+                                  o.data_ptr(), B, H, KVH, length, cap, D, max_seq, device=0)
+    torch.cuda.synchronize()
+    return o.cpu().numpy(), t["kc"].cpu().numpy(), t["vc"].cpu().numpy(), vkq.device_status(0), cos_t, sin_t
+
+
+@pytest.mark.parametrize("B,H,KVH,D,length,cap", [
+    (1, 16, 2, 128, 1, 4),          # the first token: only the new key
+    (1, 16, 2, 128, 1024, 1024),    # the 3B-class decode step's shape
+    (2, 8, 8, 64, 257, 300),        # no grouping, two sequences, a ragged last chunk
+    (1, 40, 8, 128, 4096, 5000),    # 14B-class heads
+    (1, 4, 1, 64, 204801, 204801),  # 8 chunks of 25,601 keys, the last one ragged
+], ids=lambda v: str(v))
+def test_attention_rope_decode_matches_reference(B, H, KVH, D, length, cap):
+    """The fused step against RoPE, append and attention restated: the new
+    cache rows bit for bit, every other row untouched, the output within
+    1e-5 of sum p|v|."""
+    from vibrant_b200 import vkq
+    rng = np.random.default_rng(length * 3 + H)
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k_new = rng.standard_normal((B, KVH, D)).astype(np.float32)
+    v_new = rng.standard_normal((B, KVH, D)).astype(np.float32)
+    kc = rng.standard_normal((B, KVH, cap, D)).astype(np.float32)
+    vc = rng.standard_normal((B, KVH, cap, D)).astype(np.float32)
+    kc[:, :, length - 1:] = np.nan  # row len-1 is written by the call, later rows never read
+    vc[:, :, length - 1:] = np.nan
+    positions = [length - 1 + 3 * b for b in range(B)]
+    max_seq = length + 3 * B
+    o, kc_out, vc_out, st, cos_t, sin_t = _run_step(q, k_new, v_new, kc, vc, length, positions, max_seq)
+    assert st == vkq.OK
+    kr = np.stack([_rope_rows(k_new[b], cos_t, sin_t, positions[b]) for b in range(B)])
+    qr = np.stack([_rope_rows(q[b], cos_t, sin_t, positions[b]) for b in range(B)])
+    want_k, want_v = kc.copy(), vc.copy()
+    want_k[:, :, length - 1] = kr
+    want_v[:, :, length - 1] = v_new
+    assert np.array_equal(kc_out.view(np.uint32), want_k.view(np.uint32))
+    assert np.array_equal(vc_out.view(np.uint32), want_v.view(np.uint32))
+    ref, bound = _ref(qr, want_k, want_v, length, H, KVH)
+    err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
+    assert err <= 1e-5, err
+
+
+def test_attention_rope_decode_bad_position():
+    """A position past the tables: that sequence's output and cache rows stay
+    unwritten, the other sequence is served, and the device status says so."""
+    from vibrant_b200 import vkq
+    B, H, KVH, D, L = 2, 8, 2, 128, 40
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal((B, H, D)).astype(np.float32)
+    k_new = rng.standard_normal((B, KVH, D)).astype(np.float32)
+    v_new = rng.standard_normal((B, KVH, D)).astype(np.float32)
+    kc = rng.standard_normal((B, KVH, L, D)).astype(np.float32)
+    vc = rng.standard_normal((B, KVH, L, D)).astype(np.float32)
+    o, kc_out, vc_out, st, cos_t, sin_t = _run_step(q, k_new, v_new, kc, vc, L, [L - 1, 64], 64)
+    assert st == vkq.ERR_INVALID_ARGUMENT
+    assert np.isnan(o[1]).all() and np.isfinite(o[0]).all()
+    assert np.array_equal(kc_out[1], kc[1]) and np.array_equal(vc_out[1], vc[1])
+    assert np.array_equal(kc_out[0, :, :L - 1], kc[0, :, :L - 1])
+    assert vkq.device_status(0) == vkq.OK  # the status word was cleared by the read

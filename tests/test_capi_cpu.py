@@ -53,7 +53,7 @@ def test_only_declared_symbols_are_exported(lib):
 
 
 def test_abi_version_and_block_bytes(lib):
-    assert lib.vkq_abi_version() == 4
+    assert lib.vkq_abi_version() == 5
     assert [lib.vkq_block_bytes(t) for t in (12, 13, 14)] == [144, 176, 210]
     assert lib.vkq_block_bytes(2) == 0
 

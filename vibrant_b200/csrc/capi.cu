@@ -565,6 +565,39 @@ int vkq_attention_decode_f32(int device, const float *q, const float *k_cache, c
                         "decode attention");
 }
 
+int vkq_attention_rope_decode_f32(int device, const float *q, const float *k_new, const float *v_new,
+                                  const float *cos_table, const float *sin_table, const int32_t *positions,
+                                  float *k_cache, float *v_cache, float *out, int64_t batch, int64_t heads,
+                                  int64_t kv_heads, int64_t len, int64_t cache_len, int64_t head_dim, int64_t max_seq,
+                                  void *stream) {
+    int st = enter(device);
+    if (st) return st;
+    if (!q || !k_new || !v_new || !cos_table || !sin_table || !positions || !k_cache || !v_cache || !out ||
+        batch <= 0 || batch > 65535 || heads <= 0 || heads > 65535 || kv_heads <= 0 || heads % kv_heads != 0 ||
+        len <= 0 || cache_len < len || (uint64_t)len > attention_max_len() || max_seq <= 0) {
+        set_error("invalid arguments to vkq_attention_rope_decode_f32 (heads a multiple of kv_heads, 0 < len <= "
+                  "cache_len, len <= %zu, max_seq > 0)",
+                  attention_max_len());
+        return VKQ_ERR_INVALID_ARGUMENT;
+    }
+    if (head_dim != 64 && head_dim != 128) {
+        set_error("vkq_attention_rope_decode_f32 serves head_dim 64 or 128 (got %lld)", (long long)head_dim);
+        return VKQ_ERR_UNSUPPORTED;
+    }
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+         reinterpret_cast<uintptr_t>(cos_table) | reinterpret_cast<uintptr_t>(sin_table) |
+         reinterpret_cast<uintptr_t>(positions) | reinterpret_cast<uintptr_t>(k_cache) |
+         reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(out)) &
+        3u) {
+        set_error("vkq_attention_rope_decode_f32 needs 4-byte aligned buffers");
+        return VKQ_ERR_MISALIGNED;
+    }
+    return check_launch(attention_decode_rope(q, k_new, v_new, cos_table, sin_table, positions, k_cache, v_cache, out,
+                                              batch, heads, kv_heads, len, cache_len, head_dim, max_seq,
+                                              (cudaStream_t)stream),
+                        "fused decode attention");
+}
+
 size_t vkq_gather_channel_bytes(int64_t m_max, int64_t N) {
     return m_max > 0 && N > 0 ? gather_channel_bytes(m_max, N) : 0;
 }
@@ -695,11 +728,13 @@ int vkq_device_status(int device, int *code) {
     const int g3 = gemv_tc_read_status();
     const int g4 = gemv_strip_read_status();
     const int g5 = elem_read_status();
+    const int g6 = attention_read_status();
     if (g == 0) g = g2;
     if (g == 0) g = g3;
     if (g == 0) g = g4;
     if (g == 0) g = g5;
-    if (g < 0 || g2 < 0 || g3 < 0 || g4 < 0 || g5 < 0) {
+    if (g == 0) g = g6;
+    if (g < 0 || g2 < 0 || g3 < 0 || g4 < 0 || g5 < 0 || g6 < 0) {
         set_error("cannot read the device status word");
         return VKQ_ERR_CUDA;
     }

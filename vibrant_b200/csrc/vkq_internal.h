@@ -140,6 +140,16 @@ cudaError_t rms_norm(const float *x, const float *weight, float *out, int64_t ro
 size_t attention_max_len();
 cudaError_t attention_decode(const float *q, const float *kc, const float *vc, float *o, int64_t batch, int64_t heads,
                              int64_t kv_heads, int64_t len, int64_t cache_len, int64_t head_dim, cudaStream_t s);
+// The fused decode step: q [batch][heads][D] and k_new, v_new
+// [batch][kv_heads][D] before RoPE; rotates q and k_new at positions[b],
+// stores the rotated k_new and v_new at row len - 1 of the caches and
+// attends over rows 0 .. len-1.  A position outside [0, max_seq) skips its
+// sequence and sets the status word attention_read_status() returns.
+cudaError_t attention_decode_rope(const float *q, const float *k_new, const float *v_new, const float *cos_t,
+                                  const float *sin_t, const int *positions, float *kc, float *vc, float *o,
+                                  int64_t batch, int64_t heads, int64_t kv_heads, int64_t len, int64_t cache_len,
+                                  int64_t head_dim, int64_t max_seq, cudaStream_t s);
+int attention_read_status();  // reads and clears the attention kernels' status word
 // Rotary position embedding over interleaved pairs (elementwise.cu): x and
 // out [rows][head_dim] with rows = batch * heads * seq, seq the fastest;
 // tables [max_seq][head_dim / 2]; 8-byte aligned x, out.

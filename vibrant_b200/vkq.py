@@ -56,6 +56,8 @@ SIGNATURES = {
     "vkq_rms_norm": (_int, [_int, _vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),
     "vkq_rope_f32": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "vkq_attention_decode_f32": (_int, [_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "vkq_attention_rope_decode_f32": (_int, [_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                                              _i64, _i64, _i64, _i64, _vp]),
     "vkq_linear_fused": (_int, [_int, _int, _int, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _i64,
                                 ctypes.POINTER(_i64), _vp, _i64, _vp, ctypes.c_float, _int, ctypes.POINTER(_vp), _vp]),
     "vkq_gguf_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
@@ -221,6 +223,18 @@ def attention_decode_f32(q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, batch
     cache (rows 0 .. length-1 of [batch][kv_heads][cache_len][head_dim])."""
     _check(load().vkq_attention_decode_f32(device, q_ptr, k_ptr, v_ptr, out_ptr, batch, heads, kv_heads, length,
                                            cache_len, head_dim, _stream_ptr(stream)))
+
+
+def attention_rope_decode_f32(q_ptr: int, k_new_ptr: int, v_new_ptr: int, cos_ptr: int, sin_ptr: int, pos_ptr: int,
+                              k_cache_ptr: int, v_cache_ptr: int, out_ptr: int, batch: int, heads: int,
+                              kv_heads: int, length: int, cache_len: int, head_dim: int, max_seq: int,
+                              device: int = -1, stream=None) -> None:
+    """vkq_attention_rope_decode_f32: RoPE on q and k_new at positions[b],
+    the rotated k_new and v_new stored at row length-1 of the caches, and
+    attention over rows 0 .. length-1, in one launch."""
+    _check(load().vkq_attention_rope_decode_f32(device, q_ptr, k_new_ptr, v_new_ptr, cos_ptr, sin_ptr, pos_ptr,
+                                                k_cache_ptr, v_cache_ptr, out_ptr, batch, heads, kv_heads, length,
+                                                cache_len, head_dim, max_seq, _stream_ptr(stream)))
 
 
 def rope_tables(head_dim: int, freq_base: float, max_seq: int):
