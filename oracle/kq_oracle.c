@@ -502,3 +502,112 @@ int ko_matmul_quant_sequential(int qtype, const float *a, int64_t M, int64_t K, 
     free(w);
     return 0;
 }
+
+/* ---- decode attention and RoPE (internal/transformer) ---------------------- */
+
+/* NewRoPE, internal/transformer/rope.go:19-43. */
+void ko_rope_tables(int64_t head_dim, double freq_base, int64_t max_seq, float *cos_t, float *sin_t) {
+    const int64_t half = head_dim / 2;
+    for (int64_t pos = 0; pos < max_seq; pos++) {
+        for (int64_t i = 0; i < half; i++) {
+            const double freq = 1.0 / pow(freq_base, (double)(2 * i) / (double)head_dim);
+            const double angle = (double)pos * freq;
+            cos_t[pos * half + i] = (float)cos(angle);
+            sin_t[pos * half + i] = (float)sin(angle);
+        }
+    }
+}
+
+/* RoPE.ApplyRotation, CPU branch, rope.go:49-124 (the loop :98-118). */
+int ko_rope_apply(const float *x, float *out, const float *cos_t, const float *sin_t, const int32_t *positions,
+                  int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t max_seq) {
+    const int64_t half = head_dim / 2;
+    for (int64_t s = 0; s < seq; s++)
+        if (positions[s] < 0 || positions[s] >= max_seq) return -1;
+    for (int64_t b = 0; b < batch; b++) {
+        for (int64_t h = 0; h < heads; h++) {
+            for (int64_t s = 0; s < seq; s++) {
+                const int64_t off = ((b * heads + h) * seq + s) * head_dim;
+                const int64_t t = (int64_t)positions[s] * half;
+                for (int64_t i = 0; i < half; i++) {
+                    const float c = cos_t[t + i], sn = sin_t[t + i];
+                    const float x0 = x[off + 2 * i], x1 = x[off + 2 * i + 1];
+                    const float p0 = x0 * c, p1 = x1 * sn, p2 = x0 * sn, p3 = x1 * c;
+                    out[off + 2 * i] = p0 - p1;
+                    out[off + 2 * i + 1] = p2 + p3;
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* concatenateSeqDim, attention.go:529-569: the cached rows stay where they
+ * are and the new rows follow them. */
+int ko_kv_append(float *cache, const float *new_rows, int64_t batch, int64_t kv_heads, int64_t cache_len,
+                 int64_t row0, int64_t n_new, int64_t head_dim) {
+    if (row0 < 0 || n_new < 0 || row0 + n_new > cache_len) return -1;
+    for (int64_t b = 0; b < batch; b++) {
+        for (int64_t h = 0; h < kv_heads; h++) {
+            float *dst = cache + ((b * kv_heads + h) * cache_len + row0) * head_dim;
+            const float *src = new_rows + (b * kv_heads + h) * n_new * head_dim;
+            memcpy(dst, src, (size_t)(n_new * head_dim) * sizeof(float));
+        }
+    }
+    return 0;
+}
+
+/* expandKVHeads (attention.go:280-314) and computeAttention (:316-363) for one
+ * query row: scaleScores :413-427, applyCausalMask :429-460 (nothing masked
+ * when rows < cols, and a 1x1 score has nothing above its diagonal),
+ * applySoftmax :462-527, both products through matmulSIMDSingleRow's
+ * untransposed branch (matmul_simd.go:189-199, ko_matmul_single_row_u). */
+int ko_attention_decode(const float *q, const float *kc, const float *vc, float *out, int64_t batch, int64_t heads,
+                        int64_t kv_heads, int64_t len, int64_t cache_len, int64_t head_dim) {
+    if (batch <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || len <= 0 || cache_len < len ||
+        head_dim <= 0)
+        return -1;
+    const int64_t group = heads / kv_heads, D = head_dim;
+    float *kt = (float *)malloc((size_t)(D * len) * sizeof(float));
+    float *row = (float *)malloc((size_t)len * sizeof(float));
+    if (!kt || !row) {
+        free(kt);
+        free(row);
+        return -2;
+    }
+    const float scale = (float)(1.0 / sqrt((double)D));
+    const float neg_inf = -INFINITY;
+    for (int64_t b = 0; b < batch; b++) {
+        for (int64_t h = 0; h < heads; h++) {
+            const int64_t kvh = h / group;
+            const float *kr = kc + (b * kv_heads + kvh) * cache_len * D;
+            const float *vr = vc + (b * kv_heads + kvh) * cache_len * D;
+            const float *qh = q + (b * heads + h) * D;
+            /* Transpose (ops.go:445-468): kt[d][j] = K[j][d] */
+            for (int64_t j = 0; j < len; j++)
+                for (int64_t d = 0; d < D; d++) kt[d * len + j] = kr[j * D + d];
+            ko_matmul_single_row_u(qh, kt, D, len, row);
+            for (int64_t j = 0; j < len; j++) row[j] *= scale;
+            float mx = row[0];
+            for (int64_t j = 0; j < len; j++)
+                if (row[j] > mx) mx = row[j];
+            float sum = 0.0f;
+            for (int64_t j = 0; j < len; j++) {
+                if (row[j] == neg_inf) {
+                    row[j] = 0.0f;
+                } else {
+                    row[j] = (float)exp((double)(row[j] - mx));
+                    sum += row[j];
+                }
+            }
+            if (sum > 0.0f) {
+                const float inv = 1.0f / sum;
+                for (int64_t j = 0; j < len; j++) row[j] *= inv;
+            }
+            ko_matmul_single_row_u(row, vr, len, D, out + (b * heads + h) * D);
+        }
+    }
+    free(kt);
+    free(row);
+    return 0;
+}

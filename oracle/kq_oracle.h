@@ -12,7 +12,11 @@
  * quant_q6k_integration_test.go, quant_q5k_test.go, dequant_transpose_test.go,
  * tensor_cuda_test.go) are checked in tests/test_oracle_golden.py, and an
  * independent numpy restatement (tests/golden/make_golden.py) produced the
- * committed fixtures the oracle is compared with.
+ * committed fixtures the oracle is compared with.  The decode-attention and
+ * RoPE restatements (internal/transformer) are checked in
+ * tests/test_oracle_attention.py against the values of
+ * internal/transformer/transformer_test.go that it holds and against numpy
+ * restatements; that test file's header says what it pins.
  *
  * Compiled with -ffp-contract=off: the reference is built for the default
  * GOAMD64 level, where the Go compiler does not fuse a*b+c into an FMA, so
@@ -122,6 +126,46 @@ int ko_matmul_quant_sequential(int qtype, const float *a, int64_t M, int64_t K, 
  * ceil(n/256) blocks. */
 int ko_quantize_q4k(const float *in, int64_t n, uint8_t *out);
 int ko_quantize_q6k(const float *in, int64_t n, uint8_t *out);
+
+/* ---- decode attention and RoPE (internal/transformer) ---------------------- */
+
+/* NewRoPE (internal/transformer/rope.go:19-43): tables [max_seq][head_dim/2],
+ * angle = pos * (1 / pow(freq_base, 2i / head_dim)) in double, then cos and
+ * sin rounded to float.  (This libm may differ from Go's math package in the
+ * last bit of a double, which float rounding almost always hides.) */
+void ko_rope_tables(int64_t head_dim, double freq_base, int64_t max_seq, float *cos_t, float *sin_t);
+
+/* RoPE.ApplyRotation, CPU branch (rope.go:49-124): x and out
+ * [batch][heads][seq][head_dim] (out may be x), positions[seq].  Pair i of a
+ * token at position p: out[2i] = x0*c - x1*s, out[2i+1] = x0*s + x1*c, every
+ * product and sum rounded to float.  Returns -1 (out untouched) if a position
+ * lies outside [0, max_seq). */
+int ko_rope_apply(const float *x, float *out, const float *cos_t, const float *sin_t, const int32_t *positions,
+                  int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int64_t max_seq);
+
+/* concatenateSeqDim (attention.go:529-569) into a preallocated cache: the
+ * n_new rows of new_rows [batch][kv_heads][n_new][head_dim] become rows
+ * row0 .. row0+n_new-1 of cache [batch][kv_heads][cache_len][head_dim].
+ * Returns -1 if they do not fit. */
+int ko_kv_append(float *cache, const float *new_rows, int64_t batch, int64_t kv_heads, int64_t cache_len,
+                 int64_t row0, int64_t n_new, int64_t head_dim);
+
+/* The decode branch of Attention.Forward after RoPE and the append
+ * (attention.go:164-172): expandKVHeads (:280-314, query head h reads KV
+ * head h / (heads / kv_heads)), then computeAttention (:316-363) for one
+ * query row against rows 0 .. len-1 of the caches:
+ *   scores = MatMul(q, Transpose(K)): Transpose copies (ops.go:445-468), so
+ *     MatMul (matmul.go:46-99) takes matmulSIMDSingleRow's untransposed
+ *     outer-product branch (matmul_simd.go:189-199);
+ *   scaleScores (:413-427) by float(1 / sqrt(head_dim));
+ *   applyCausalMask (:429-460) masks nothing for one query row;
+ *   applySoftmax (:462-527): max, float(exp(double(s - max))), float sum,
+ *     then a multiply by 1/sum;
+ *   out = MatMul(p, V), the same outer-product branch.
+ * q, out [batch][heads][head_dim]; caches [batch][kv_heads][cache_len][head_dim].
+ * Returns -1 on bad sizes, -2 if scratch cannot be allocated. */
+int ko_attention_decode(const float *q, const float *kc, const float *vc, float *out, int64_t batch, int64_t heads,
+                        int64_t kv_heads, int64_t len, int64_t cache_len, int64_t head_dim);
 
 #ifdef __cplusplus
 }

@@ -54,6 +54,12 @@ def lib() -> ctypes.CDLL:
         L.ko_matmul_quant_sequential.argtypes = [ctypes.c_int, f32p, i64, i64, u8p, i64, f32p]
         L.ko_quantize_q4k.argtypes = [f32p, i64, u8p]
         L.ko_quantize_q6k.argtypes = [f32p, i64, u8p]
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        L.ko_rope_tables.argtypes = [i64, ctypes.c_double, i64, f32p, f32p]
+        L.ko_rope_tables.restype = None
+        L.ko_rope_apply.argtypes = [f32p, f32p, f32p, f32p, i32p, i64, i64, i64, i64, i64]
+        L.ko_kv_append.argtypes = [f32p, f32p, i64, i64, i64, i64, i64, i64]
+        L.ko_attention_decode.argtypes = [f32p, f32p, f32p, f32p, i64, i64, i64, i64, i64, i64]
         _lib = L
     return _lib
 
@@ -176,3 +182,75 @@ def matmul_quant_sequential(qtype: int, a: np.ndarray, bq: np.ndarray, K: int, N
                                           _u8p(np.ascontiguousarray(bq, np.uint8)), N, _f32p(c))
     assert rc == 0
     return c
+
+
+# ---- decode attention and RoPE (internal/transformer) -----------------------
+
+def rope_tables(head_dim: int, freq_base: float, max_seq: int):
+    """NewRoPE's cos and sin tables [max_seq][head_dim/2] (rope.go:19-43)."""
+    half = head_dim // 2
+    c = np.empty((max_seq, half), np.float32)
+    s = np.empty((max_seq, half), np.float32)
+    lib().ko_rope_tables(head_dim, float(freq_base), max_seq, _f32p(c), _f32p(s))
+    return c, s
+
+
+def rope_apply(x: np.ndarray, cos_t: np.ndarray, sin_t: np.ndarray, positions) -> np.ndarray:
+    """RoPE.ApplyRotation on x [batch][heads][seq][head_dim] (rope.go:49-124)."""
+    x = np.ascontiguousarray(x, np.float32)
+    B, H, S, D = x.shape
+    pos = np.ascontiguousarray(np.asarray(positions, np.int32))
+    assert pos.size == S
+    out = np.empty_like(x)
+    rc = lib().ko_rope_apply(_f32p(x), _f32p(out), _f32p(np.ascontiguousarray(cos_t, np.float32)),
+                             _f32p(np.ascontiguousarray(sin_t, np.float32)),
+                             pos.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), B, H, S, D, cos_t.shape[0])
+    if rc != 0:
+        raise ValueError("position outside the RoPE tables")
+    return out
+
+
+def kv_append(cache: np.ndarray, new_rows: np.ndarray, row0: int) -> None:
+    """concatenateSeqDim (attention.go:529-569) in place: new_rows
+    [batch][kv_heads][n][D] become rows row0 .. row0+n-1 of cache
+    [batch][kv_heads][cache_len][D]."""
+    assert cache.dtype == np.float32 and cache.flags.c_contiguous
+    new_rows = np.ascontiguousarray(new_rows, np.float32)
+    B, KVH, cap, D = cache.shape
+    rc = lib().ko_kv_append(_f32p(cache), _f32p(new_rows), B, KVH, cap, row0, new_rows.shape[2], D)
+    if rc != 0:
+        raise ValueError("rows do not fit the cache")
+
+
+def attention_decode(q: np.ndarray, kc: np.ndarray, vc: np.ndarray, length: int) -> np.ndarray:
+    """computeAttention (attention.go:316-363) for one query row per (batch,
+    head) against rows 0 .. length-1 of the caches, grouped KV heads expanded
+    as expandKVHeads does.  q [batch][heads][D], caches
+    [batch][kv_heads][cache_len][D]; returns [batch][heads][D]."""
+    q = np.ascontiguousarray(q, np.float32)
+    kc = np.ascontiguousarray(kc, np.float32)
+    vc = np.ascontiguousarray(vc, np.float32)
+    B, H, D = q.shape
+    KVH, cap = kc.shape[1], kc.shape[2]
+    out = np.empty((B, H, D), np.float32)
+    rc = lib().ko_attention_decode(_f32p(q), _f32p(kc), _f32p(vc), _f32p(out), B, H, KVH, length, cap, D)
+    assert rc == 0, rc
+    return out
+
+
+def attention_rope_decode(q, k_new, v_new, kc, vc, length: int, cos_t, sin_t, positions):
+    """Attention.Forward's decode branch after the projections
+    (attention.go:141-172) for one new token per sequence: RoPE on q and
+    k_new at positions[b], the rotated k_new and v_new appended as row
+    length-1 of copies of the caches, attention over rows 0 .. length-1.
+    Returns (out, k_cache, v_cache)."""
+    B, H, D = q.shape
+    KVH = k_new.shape[1]
+    qr = np.stack([rope_apply(q[b][None, :, None, :], cos_t, sin_t, [positions[b]])[0, :, 0] for b in range(B)])
+    kr = np.stack([rope_apply(k_new[b][None, :, None, :], cos_t, sin_t, [positions[b]])[0, :, 0]
+                   for b in range(B)])
+    kc = np.array(kc, np.float32, copy=True, order="C")
+    vc = np.array(vc, np.float32, copy=True, order="C")
+    kv_append(kc, kr.reshape(B, KVH, 1, D), length - 1)
+    kv_append(vc, np.asarray(v_new, np.float32).reshape(B, KVH, 1, D), length - 1)
+    return attention_decode(qr, kc, vc, length), kc, vc

@@ -2,7 +2,10 @@
 cache, against a float64 restatement of the reference's decode attention
 (computeAttention, internal/transformer/attention.go:316-363, with the cache
 of :147-162, grouped KV heads of expandKVHeads :280-314 and no mask for one
-query row).  Parity bar: each output within 1e-5 of sum_j p_j |v_j|."""
+query row), and against the oracle's float32 restatement of the same
+arithmetic (oracle/kq_oracle.c ko_attention_decode, with ko_rope_apply and
+ko_kv_append for the fused step).  Parity bar: each output within 1e-5 of
+sum_j p_j |v_j|; the cache rows the fused step writes bit for bit."""
 import numpy as np
 import pytest
 
@@ -25,6 +28,15 @@ def _ref(q, kc, vc, length, heads, kv_heads):
             out[b, h] = p @ v
             bound[b, h] = p @ np.abs(v)
     return out, bound
+
+
+def _oracle_err(o, q, kc, vc, length, bound):
+    """Distance of the kernel's output from the oracle's float32 restatement
+    of the reference's arithmetic (kq_oracle.attention_decode), in units of
+    sum_j p_j |v_j|."""
+    from oracle import kq_oracle
+    ora = kq_oracle.attention_decode(q, kc, vc, length).astype(np.float64)
+    return float(np.max(np.abs(o - ora) / np.maximum(bound, 1e-30)))
 
 
 def _run(q, kc, vc, length, shift=0):
@@ -72,6 +84,7 @@ def test_attention_decode_matches_reference(B, H, KVH, D, length, cap):
     ref, bound = _ref(q, kc, vc, length, H, KVH)
     err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
     assert err <= 1e-5, err
+    assert _oracle_err(o, q, kc, vc, length, bound) <= 1e-5
 
 
 @pytest.mark.parametrize("D,length", [(128, 300), (64, 1000)])
@@ -86,6 +99,7 @@ def test_attention_decode_unaligned_buffers(D, length):
     ref, bound = _ref(q, kc, vc, length, H, KVH)
     err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
     assert err <= 1e-5, err
+    assert _oracle_err(o, q, kc, vc, length, bound) <= 1e-5
 
 
 def test_attention_decode_peaked_scores():
@@ -187,6 +201,12 @@ def test_attention_rope_decode_matches_reference(B, H, KVH, D, length, cap):
     ref, bound = _ref(qr, want_k, want_v, length, H, KVH)
     err = float(np.max(np.abs(o - ref) / np.maximum(bound, 1e-30)))
     assert err <= 1e-5, err
+    # the oracle's whole decode branch: RoPE, append, attention
+    from oracle import kq_oracle
+    ora, ora_k, ora_v = kq_oracle.attention_rope_decode(q, k_new, v_new, kc, vc, length, cos_t, sin_t, positions)
+    assert np.array_equal(kc_out.view(np.uint32), ora_k.view(np.uint32))
+    assert np.array_equal(vc_out.view(np.uint32), ora_v.view(np.uint32))
+    assert float(np.max(np.abs(o - ora.astype(np.float64)) / np.maximum(bound, 1e-30))) <= 1e-5
 
 
 def test_attention_rope_decode_bad_position():
